@@ -1,0 +1,65 @@
+"""`.p12` codec and archive parity with the reference packer (scripts/pack_weights.py)."""
+import numpy as np
+import pytest
+
+from conftest import GOLDEN
+
+
+@pytest.fixture(scope="module")
+def vectors():
+    return np.load(GOLDEN / "packer_vectors.npz")
+
+
+def _names(vectors):
+    return sorted({k.split(".")[0] for k in vectors.files})
+
+
+def test_pack_matches_reference_vectors(pkg, vectors):
+    """pack()/tag() outputs equal the reference's for every golden input (pack_weights.py:19-74)."""
+    for name in _names(vectors):
+        values = vectors[f"{name}.values"]
+        data, offsets, minima = pkg.packing.pack(values)
+        assert np.array_equal(data, vectors[f"{name}.data"]), name
+        assert np.array_equal(offsets, vectors[f"{name}.offsets"]), name
+        assert np.array_equal(minima, vectors[f"{name}.minima"]), name
+        assert np.array_equal(pkg.packing.tag(offsets, minima), vectors[f"{name}.entries"]), name
+
+
+def test_self_test_round_trip(pkg):
+    """pack_weights.py:77-86: every bf16 pattern, signed zeros and mixed-sign blocks round-trip."""
+    for values in [np.arange(65536, dtype="<u2"), np.zeros(256, dtype="<u2"), np.full(128, 0x8000, dtype="<u2"),
+                   np.tile(np.array([0, 0x8000, 0x3F80, 0xBF80], dtype="<u2"), 64)]:
+        data, offsets, minima = pkg.packing.pack(values)
+        entries = pkg.packing.tag(offsets, minima)
+        off, mins = pkg.packing.untag(entries)
+        restored = pkg.packing.unpack(data, off, mins)
+        assert np.array_equal(restored.reshape(-1), values)
+
+
+def test_archive_bytes_match_reference_packer(pkg, micro_dir, tmp_path):
+    """Our writer reproduces the reference main()'s archive byte for byte (pack_weights.py:89-135)."""
+    import shutil
+    for f in ["config.json", "config-mlx.json", "model.safetensors"]:
+        shutil.copy(micro_dir / f, tmp_path / f)
+    pkg.packing.write_p12(tmp_path)
+    assert (tmp_path / "model.p12").read_bytes() == (micro_dir / "model.p12").read_bytes()
+
+
+def test_archive_unpacks_bit_identical(pkg, micro_dir):
+    manifest, payload = pkg.packing.read_p12(micro_dir / "model.p12")
+    import json, struct
+    raw = (micro_dir / "model.safetensors").read_bytes()
+    n = struct.unpack("<Q", raw[:8])[0]
+    header = json.loads(raw[8:8 + n])
+    for name in manifest["tensors"]:
+        b, e = header[name]["data_offsets"]
+        src = np.frombuffer(raw[8 + n + b:8 + n + e], dtype="<u2").reshape(header[name]["shape"])
+        assert np.array_equal(pkg.packing.unpack_tensor(manifest, payload, name), src), name
+    assert "model.embed_tokens.weight" not in manifest["tensors"]
+
+
+def test_oracle_packed_decode_golden(oracle):
+    """Kernels.metal:23-31 restated: all 323,584 words of PackedDecodeTests.swift:8-31."""
+    g = np.load(GOLDEN / "packed_decode.npz")
+    out = oracle.packed_decode(g["payload"], g["entries"], g["expected"].size)
+    assert np.array_equal(out, g["expected"])
