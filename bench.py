@@ -1,0 +1,345 @@
+#!/usr/bin/env python
+"""Benchmark: batch-1 greedy decode of the PLaMo-3 0.8B decoder on B200.
+
+Workload (per GPU): the reference-dims model (d 1536, 16 layers, 16 q-heads / 1 KV head, FFN 6144,
+vocab 107520) with random-init weights (seed 0, normal std 0.02 in bf16, norms 1.0) written to a
+model directory on the box, a 512-token seeded-uniform prompt (seed 1 + rank), prefill, then greedy
+decode. One step = one decoded token (one pass of the decoder over one token, weights streamed
+from HBM; the 1.45 GB of weights are far larger than the 126 MB L2, so no flush is needed).
+
+  value  tokens/s over exactly K device-chained steps (inputs resident, each step's argmax feeds
+         the next on the device), timed with CUDA events on the runtime's stream; N GPUs run
+         independent replicas (weak scaling), max time over ranks, value = N*K / time.
+  e2e    the same metric through the public C ABI (plamo_forward per token: host id in via a
+         pinned H2D copy, next id out via D2H), wall clock per call sequence.
+  roofline  the dominant kernel class (the projection GEMVs) timed live with CUDA events around
+         every launch; algorithmic bytes = weight bytes streamed per launch.
+  cpu_baseline  the CPU restatement of the same forward (oracle/, OpenMP on all host cores) on a
+         bounded sample of the same workload (rank 0, N=1).
+
+--impl reference runs the reference arm: the reference (Swift + Metal) cannot run on Linux, so its
+CPU path is the restatement in oracle/ (see DESIGN.md), timed on the host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import importlib.util
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+PROMPT = 512
+
+
+def _load(name, path, package=False):
+    if name in sys.modules:
+        return sys.modules[name]
+    kw = {"submodule_search_locations": [str(path.parent)]} if package else {}
+    spec = importlib.util.spec_from_file_location(name, path, **kw)
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[name] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def pkg():
+    return _load("plamo_b200", REPO / "plamo3-0.8b-runtime_b200" / "__init__.py", package=True)
+
+
+def oracle_mod():
+    return _load("plamo_oracle", REPO / "oracle" / "oracle.py")
+
+
+def peaks():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return dict(hbm=float(d["hbm_gbs"]), bf16=float(d["bf16_tflops"]), source="measured")
+    return dict(hbm=6650.0, bf16=1590.0, source="fallback")
+
+
+class Clocks:
+    """Samples SM clock, max clock and throttle reasons with NVML while the timed region runs."""
+
+    REASONS = {0x8: "hw_slowdown", 0x40: "hw_thermal_slowdown", 0x20: "sw_thermal_slowdown", 0x4: "sw_power_cap",
+               0x80: "hw_power_brake_slowdown", 0x1: "gpu_idle"}
+
+    def __init__(self, device: int):
+        self.samples, self.reasons, self.stop_flag = [], set(), False
+        self.max_mhz = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            idx = device
+            vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+            if vis:
+                idx = int(vis.split(",")[device])
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(idx)
+            self.nv = pynvml
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+        except Exception as e:  # pragma: no cover - no NVML
+            self.nv = None
+            self.error = str(e)
+
+    def _run(self):
+        while not self.stop_flag:
+            try:
+                self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+                mask = self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                for bit, name in self.REASONS.items():
+                    if mask & bit and name != "gpu_idle":
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(0.01)
+
+    def __enter__(self):
+        if self.nv:
+            self.t = threading.Thread(target=self._run, daemon=True)
+            self.t.start()
+        return self
+
+    def __exit__(self, *a):
+        self.stop_flag = True
+        if self.nv:
+            self.t.join()
+
+    def summary(self):
+        if not self.nv:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "error": getattr(self, "error", "no nvml")}
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None, "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+def ensure_model(root: Path, packed: bool, rank: int, dist) -> Path:
+    P = pkg()
+    d = root / "reference"
+    marker = d / (".ready_packed" if packed else ".ready")
+    if rank == 0 and not marker.exists():
+        if not (d / ".ready").exists():
+            P.synthetic.write_model(d, P.synthetic.REFERENCE, seed=0)
+            (d / ".ready").write_text("ok")
+        if packed:
+            P.packing.write_p12(d)
+            marker.write_text("ok")
+    if dist is not None:
+        dist.barrier()
+    return d
+
+
+def linear_bytes(model_dir: Path, packed: bool) -> int:
+    """Algorithmic weight bytes streamed per decode token by the projection GEMVs."""
+    P = pkg()
+    if not packed:
+        return 2 * P.synthetic.REFERENCE.linear_params()
+    manifest, _ = P.packing.read_p12(model_dir / "model.p12")
+    total = 0
+    for rec in manifest["tensors"].values():
+        if "offsets" in rec:
+            total += rec["offsets"][1] - rec["offsets"][0] + rec["data"][1] - rec["data"][0]
+    return total
+
+
+def cpu_baseline(model_dir: Path, prompt, budget_s: float, max_steps: int):
+    """CPU restatement: prefill the prompt (untimed), then time decode steps for ~budget_s."""
+    O = oracle_mod()
+    O.set_threads(os.cpu_count() or 1)
+    ora = O.OracleRuntime(model_dir, context=len(prompt) + max_steps + 8)
+    nxt = ora.prefill(prompt)
+    t0 = time.perf_counter()
+    nxt = ora.forward([nxt])
+    one = time.perf_counter() - t0
+    n = max(2, min(max_steps, int(budget_s / max(one, 1e-3))))
+    t0 = time.perf_counter()
+    for _ in range(n):
+        nxt = ora.forward([nxt])
+    el = time.perf_counter() - t0
+    import platform
+    cpu = platform.processor() or ""
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                cpu = line.split(":", 1)[1].strip()
+                break
+    except OSError:
+        pass
+    return dict(value=n / el, unit="tok/s", cores=O.threads(), kind="port",
+                sample=f"{n} greedy decode steps at positions {len(prompt) + 1}..{len(prompt) + n} after a "
+                       f"{len(prompt)}-token prefill of the reference-dims model (CPU restatement, fp32 "
+                       f"accumulation, {O.threads()} OpenMP threads, {cpu})")
+
+
+def run_reference(args):
+    """Reference arm: the reference's CPU path (restated in oracle/) on the host cores."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    root = Path(args.model_root)
+    model = ensure_model(root, args.packed, 0, None)
+    P = pkg()
+    prompt = P.synthetic.seeded_tokens(PROMPT, 107520, seed=1)
+    steps = max(1, min(args.steps, args.reference_max_steps))
+    O = oracle_mod()
+    O.set_threads(os.cpu_count() or 1)
+    ora = O.OracleRuntime(model, context=PROMPT + args.warmup + steps + 8, packed=args.packed)
+    nxt = ora.prefill(prompt)
+    for _ in range(args.warmup):
+        nxt = ora.forward([nxt])
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        nxt = ora.forward([nxt])
+    el = time.perf_counter() - t0
+    value = steps / el
+    line = dict(metric="decode tok/s (bs1)", value=value, unit="tok/s", n_gpus=args.gpus, steps=args.steps,
+                warmup=args.warmup, ms_per_step=1e3 * el / steps, higher_is_better=True, scaling="weak",
+                vs_baseline=None, dtype="bf16 weights, fp32 accumulate", data="synthetic", impl="reference",
+                config=workload_config(args),
+                cpu_baseline=dict(value=value, unit="tok/s", cores=O.threads(), kind="port",
+                                  sample=f"{steps} of {args.steps} requested decode steps (bounded) after a {PROMPT}-token "
+                                         f"prefill; CPU restatement of the reference forward"),
+                e2e=dict(value=value, unit="tok/s", h2d_bytes_per_step=0, d2h_bytes_per_step=0))
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def workload_config(args):
+    return {"workload": "BASELINE config 2: reference-dims PLaMo-3 0.8B (d1536 L16 H16/KV1 F6144 V107520), "
+                        f"{PROMPT}-token seeded prompt, prefill then greedy bs1 decode"
+                        + (" from the .p12 packed archive (config 3)" if args.packed else ", bf16 weights"),
+            "prompt_tokens": PROMPT, "batch": 1, "weights": "p12" if args.packed else "bf16",
+            "parallelism": f"replicas x{args.gpus} (weights broadcast by NCCL at load)" if args.gpus > 1 else "single GPU",
+            "l2": "weights (1.45 GB) exceed L2 (126 MB): no flush needed"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=1024)
+    ap.add_argument("--warmup", type=int, default=16)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--packed", action="store_true")
+    ap.add_argument("--model-root", default=os.environ.get("PLAMO_BENCH_MODELS", "/tmp/plamo_bench"))
+    ap.add_argument("--cpu-budget", type=float, default=12.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-steps", type=int, default=16)
+    ap.add_argument("--reference-max-steps", type=int, default=64)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    if args.impl == "reference":
+        return run_reference(args)
+
+    import torch
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=torch.device("cuda", local))
+    P = pkg()
+    model = ensure_model(Path(args.model_root), args.packed, rank, dist)
+    context = PROMPT + 2 * (args.warmup + args.steps) + args.profile_steps + 16
+    if context > 32768:
+        raise SystemExit("steps too large for the 32768-token context")
+    if world > 1:
+        uid = [P.Runtime.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        rt = P.Runtime.broadcast(model, context, args.packed, local, uid[0], rank, world)
+    else:
+        rt = P.Runtime(model, context=context, packed=args.packed, device=local)
+    prompt = P.synthetic.seeded_tokens(PROMPT, rt.vocab, seed=1 + rank)
+
+    # ---- value: device-chained decode, K timed steps ---------------------------------------
+    rt.prefill(prompt)
+    rt.decode_chain(args.warmup)
+    launches = rt.step_launches()
+    if dist: dist.barrier()
+    torch.cuda.synchronize()
+    clocks = Clocks(local)
+    g0 = rt.gpu_seconds
+    with clocks:
+        rt.decode_chain(args.steps)
+    torch.cuda.synchronize()
+    elapsed = rt.gpu_seconds - g0
+    if dist: dist.barrier()
+    t = torch.tensor([elapsed], device="cuda", dtype=torch.float64)
+    if dist: dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    elapsed_max = float(t.item())
+
+    # ---- roofline of the dominant kernel class, timed live ---------------------------------
+    prof = rt.profile_decode(args.profile_steps)
+    wbytes = linear_bytes(model, args.packed)
+    gemv = prof["gemv"]
+    per_launch_bytes = (wbytes * args.profile_steps) / max(1, gemv["launches"])
+    per_launch_s = gemv["ms"] * 1e-3 / max(1, gemv["launches"])
+    pk = peaks()
+    achieved = per_launch_bytes / per_launch_s / 1e9
+    total_ms = sum(v["ms"] for v in prof.values())
+    traffic = None
+    tf = REPO / "profiles" / ("gemv_decode_traffic_p12.json" if args.packed else "gemv_decode_traffic.json")
+    if tf.exists():
+        traffic = json.loads(tf.read_text()).get("dram_bytes_per_launch")
+
+    # ---- e2e through the public API ---------------------------------------------------------
+    rt.reset()
+    nxt = rt.prefill(prompt)
+    for _ in range(args.warmup):
+        nxt = rt.forward([nxt])
+    if dist: dist.barrier()
+    torch.cuda.synchronize()
+    w0 = time.perf_counter()
+    for _ in range(args.steps):
+        nxt = rt.forward([nxt])
+    w1 = time.perf_counter()
+    torch.cuda.synchronize()
+    e2e_t = torch.tensor([w1 - w0], device="cuda", dtype=torch.float64)
+    if dist:
+        dist.barrier()
+        dist.all_reduce(e2e_t, op=dist.ReduceOp.MAX)
+    e2e_elapsed = float(e2e_t.item())
+    bcast = rt.broadcast_seconds
+    rt.close()
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(model, prompt, args.cpu_budget, 64)
+
+    if rank == 0:
+        value = world * args.steps / elapsed_max
+        tok_bytes = wbytes
+        line = dict(
+            metric="decode tok/s (bs1)", value=value, unit="tok/s", n_gpus=world, steps=args.steps,
+            warmup=args.warmup, ms_per_step=1e3 * elapsed_max / args.steps, higher_is_better=True, scaling="weak",
+            vs_baseline=None, dtype="bf16 weights, fp32 accumulate", data="synthetic (seeded random-init weights and ids)",
+            config=workload_config(args),
+            e2e=dict(value=world * args.steps / e2e_elapsed, unit="tok/s", h2d_bytes_per_step=24, d2h_bytes_per_step=4),
+            gpu_launches=launches * args.steps,
+            roofline=dict(bound="hbm", kernel="k_gemv (all projection GEMVs of a decode step)", achieved=achieved,
+                          peak=pk["hbm"], unit="GB/s", frac=achieved / pk["hbm"], traffic=traffic,
+                          peak_source=pk["source"], bytes_per_launch=per_launch_bytes,
+                          launch_us=per_launch_s * 1e6,
+                          step_hbm_frac=(tok_bytes / (elapsed_max / args.steps)) / 1e9 / pk["hbm"],
+                          class_share={k: round(v["ms"] / total_ms, 4) for k, v in prof.items()}),
+            clocks=clocks.summary(),
+        )
+        if cpu:
+            line["cpu_baseline"] = cpu
+        if world > 1:
+            line["weight_broadcast_s"] = bcast
+        print(json.dumps(line), flush=True)
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,127 @@
+/* libplamo_cuda: B200 (sm_100a) backend for the PLaMo-3 0.8B decoder hot path.
+ *
+ * C ABI that replaces the Metal compute layer of mikuteto-dev/plamo3-0.8b-runtime one to one:
+ * the members of `Runtime` (Sources/Plamo/Runtime.swift) and `Batch` (Sources/Plamo/Batch.swift)
+ * that the Swift engine calls. Plain pointers and sizes only; every call is synchronous (it returns
+ * after the device work and the result copy finished, like the reference's waitUntilCompleted) and
+ * reports failure through its status: 0 = success, non-zero = failure with the message available
+ * from plamo_last_error() (thread-local). Handles are single-threaded; separate handles on separate
+ * devices may be used concurrently. The library owns all device memory; callers own host arrays,
+ * which are copied before the call returns.
+ */
+#ifndef PLAMO_H
+#define PLAMO_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifndef PLAMO_API
+#define PLAMO_API __attribute__((visibility("default")))
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct plamo_runtime plamo_runtime;
+typedef struct plamo_batch plamo_batch;
+
+/* Runtime.init(directory:context:packed:) — Runtime.swift:164-286.
+ * Loads <model_dir>/config.json, config-mlx.json and model.safetensors (+ model.p12 when packed),
+ * validates them (Runtime.swift:181-189, :33-101; Packed.swift:12-91) and makes the weights
+ * resident on CUDA device `device`. context: 1...32768. */
+PLAMO_API int plamo_open(const char* model_dir, int context, int packed, int device, plamo_runtime** out);
+
+/* Same as plamo_open, but the weights are received from rank 0 with one ncclBroadcast of the
+ * weight arena over NVLink instead of being read from disk on every rank (ranks > 0 still read
+ * config.json/config-mlx.json and the archive headers). `nccl_id` is the 128-byte ncclUniqueId
+ * created on rank 0 (plamo_nccl_unique_id) and shared out of band. No reference counterpart: the
+ * reference is single-GPU; this is the data-parallel loader. */
+PLAMO_API int plamo_open_broadcast(const char* model_dir, int context, int packed, int device,
+                         const void* nccl_id, int rank, int world, plamo_runtime** out);
+PLAMO_API int plamo_nccl_unique_id(void* out_128_bytes);
+/* Seconds spent in the load-time weight broadcast (0 when loaded from disk). */
+PLAMO_API double plamo_broadcast_seconds(const plamo_runtime*);
+
+PLAMO_API void plamo_close(plamo_runtime*);
+
+/* Runtime.prefill(_:) — Runtime.swift:469-483: feeds ids in 16-token chunks; returns the greedy
+ * next id of the last position in *next_id. Errors: "Input exceeds context". */
+PLAMO_API int plamo_prefill(plamo_runtime*, const int32_t* ids, int n, int32_t* next_id);
+
+/* Runtime.forward(_:output:) — Runtime.swift:321-467: 1...min(context,16) ids at the current
+ * position; with output != 0 writes the greedy next id (else -1).
+ * Errors: "Invalid tokens or context exhausted". */
+PLAMO_API int plamo_forward(plamo_runtime*, const int32_t* ids, int n, int output, int32_t* next_id);
+
+/* Runtime.logits(into:slot:) / logitValues() — Runtime.swift:540-552: the last output row's
+ * bf16 logits widened to vocab_size floats. */
+PLAMO_API int plamo_logits(plamo_runtime*, int slot, float* out);
+
+/* Final-normed hidden row of the last output (Runtime.normalized after the head), hidden_size floats. */
+PLAMO_API int plamo_hidden(plamo_runtime*, float* out);
+
+PLAMO_API void plamo_reset(plamo_runtime*);                    /* Runtime.reset() — Runtime.swift:319 */
+PLAMO_API int plamo_position(const plamo_runtime*);            /* Runtime.position */
+PLAMO_API double plamo_gpu_seconds(const plamo_runtime*);      /* Runtime.gpuSeconds (device time, events) */
+PLAMO_API size_t plamo_weight_bytes(const plamo_runtime*);     /* Weights.gpuBytes — bytes of resident weights */
+PLAMO_API size_t plamo_device_bytes(const plamo_runtime*);     /* Runtime.peakMetalBytes — device bytes allocated */
+PLAMO_API const char* plamo_device_name(const plamo_runtime*); /* device.name */
+/* Model dimensions: hidden, layers, heads, kv_heads, head_dim, ffn, vocab, window, pattern, context. */
+PLAMO_API int plamo_dims(const plamo_runtime*, int32_t out[10]);
+
+/* Batch(runtime) — Batch.swift:33-78. lanes: 1...64 (the reference CLI uses 4). Requires
+ * context < 8192 (Batch.swift:34-35). */
+PLAMO_API int plamo_batch_open(plamo_runtime*, int lanes, plamo_batch** out);
+
+/* Batch.prefill(_:) — Batch.swift:80-106: prompt i goes to lane i (n <= lanes); next_ids[i] is the
+ * greedy next id of lane i. Errors: "Expected one to four valid prompts". */
+PLAMO_API int plamo_batch_prefill(plamo_batch*, const int32_t* const* prompts, const int32_t* lens, int n, int32_t* next_ids);
+
+/* Batch.step(_:) — Batch.swift:109-179: tokens[i] < 0 marks an inactive lane; n must equal the
+ * number of prefilled lanes; next_ids receives every lane's latest prediction.
+ * Errors: "Invalid quad step or context exhausted". */
+PLAMO_API int plamo_batch_step(plamo_batch*, const int32_t* tokens, int n, int32_t* next_ids);
+
+/* Batch.logits (per-lane bf16 logits, widened) and Batch.hidden rows. */
+PLAMO_API int plamo_batch_logits(plamo_batch*, int lane, float* out);
+PLAMO_API int plamo_batch_hidden(plamo_batch*, int lane, float* out);
+
+PLAMO_API void plamo_batch_reset(plamo_batch*);                  /* Batch.reset() — Batch.swift:182 */
+PLAMO_API double plamo_batch_gpu_seconds(const plamo_batch*);    /* Batch.gpuSeconds */
+PLAMO_API void plamo_batch_close(plamo_batch*);
+
+/* decodeBatch — BatchDecode.swift:8-38 (Batch.generate, :41-47): prefill + greedy decode of n
+ * prompts with per-lane output limits; stop ids 1 and 16 end a lane ("stop"), reaching its limit
+ * ends it ("length"); stop_on_truncation drops lanes after the first truncated one. Outputs:
+ * out_ids[i*out_stride ...] (out_lens[i] ids), reasons[i] = 0 stop / 1 length. On error the batch is
+ * reset (BatchDecode.swift:45-46). Returns the number of lanes reported in *out_count. */
+PLAMO_API int plamo_batch_generate(plamo_batch*, const int32_t* const* prompts, const int32_t* lens, const int32_t* limits,
+                         int n, int stop_on_truncation, int32_t* out_ids, int out_stride, int32_t* out_lens,
+                         int32_t* reasons, int32_t* out_count);
+
+/* Debug/state access used by the parity tests: copies one layer's KV cache (scalar runtime, or one
+ * lane of a batch) as bf16 bits, capacity*kv_heads*128 values each. */
+PLAMO_API int plamo_debug_kv(plamo_runtime*, int layer, uint16_t* keys, uint16_t* values);
+PLAMO_API int plamo_batch_debug_kv(plamo_batch*, int layer, int lane, uint16_t* keys, uint16_t* values);
+
+/* Device-chained greedy decode for benchmarking: runs `steps` batch-1 decode steps back to back on
+ * the device (each step feeds its argmax to the next, no host round trip), starting from the last
+ * prediction. Writes the generated ids to out_ids. Equivalent to `steps` plamo_forward calls. */
+PLAMO_API int plamo_decode_chain(plamo_runtime*, int steps, int32_t* out_ids);
+
+/* Number of kernel launches in one batch-1 decode step (the nodes of the captured decode graph). */
+PLAMO_API int plamo_step_launches(plamo_runtime*);
+
+/* Profiling: runs `steps` batch-1 decode steps (as plamo_decode_chain, launched without the graph)
+ * with every kernel launch bracketed by CUDA events. class_ms[5] / launches[5] receive the summed
+ * device milliseconds and launch counts per kernel class: 0 GEMV (projections, lm_head), 1 QK-norm +
+ * RoPE + KV append, 2 attention, 3 norms + embedding, 4 argmax finalisation. */
+PLAMO_API int plamo_profile_decode(plamo_runtime*, int steps, double* class_ms, int32_t* launches);
+
+PLAMO_API const char* plamo_last_error(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* PLAMO_H */

@@ -1,0 +1,63 @@
+/* libplamo_cuda kernel-level entry points: the hot-path kernels on caller-provided DEVICE
+ * buffers, enqueued on `stream` (a cudaStream_t, NULL = default stream). They return 0 on a
+ * successful launch, non-zero with plamo_last_error() set otherwise; completion is the caller's
+ * stream synchronisation. bf16 values are passed as uint16_t bit patterns. Each entry point names
+ * the reference Metal kernel it replaces (Sources/Plamo/Kernels.metal, Batch.metal).
+ */
+#ifndef PLAMO_KERNELS_H
+#define PLAMO_KERNELS_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifndef PLAMO_API
+#define PLAMO_API __attribute__((visibility("default")))
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* linear (Kernels.metal:92-114), matrix (:149-200), project3/4 (Batch.metal:171-221).
+ * y[r][m] = bf16(sum_k W[m][k] * x[r][k]) for r < rows, fp32 accumulation.
+ * W: raw bf16 [M][K] (offsets == NULL), or a .p12 tensor: `w` = data region, `offsets` = tagged
+ * block table (packed_four, Kernels.metal:33-44). K % 128 == 0.
+ * mode 0: plain, y is [rows][M]. mode 1: SwiGLU epilogue (Kernels.metal:202-210): W has 2F rows,
+ * y is [rows][F] = bf16(bf16(silu(g)) * u). mode 2: logits + first-index argmax
+ * (Kernels.metal:704-729): y is [rows][M] bf16 logits and argmax_keys[r] (zeroed by the caller)
+ * receives a 64-bit key, decoded by plamo_k_argmax_keys. */
+PLAMO_API int plamo_k_linear(const void* w, const uint32_t* offsets, const uint16_t* x, int rows, int K, int M, int mode,
+                   uint16_t* y, uint64_t* argmax_keys, void* stream);
+
+/* Converts argmax keys to indices (0xFFFFFFFF when a row had only NaN). */
+PLAMO_API int plamo_k_argmax_keys(const uint64_t* keys, int rows, uint32_t* out, void* stream);
+
+/* norm (Kernels.metal:46-90): z = bf(bf(src*rsqrt(mean(src^2)+1e-6)) * bf(w+offset)).
+ * residual == 0: x := z. residual != 0: x := bf(x + z) and, when next_w != NULL,
+ * next := norm(x, next_w, offset 1). Rows of n <= 4096 values. */
+PLAMO_API int plamo_k_norm(const uint16_t* w, const uint16_t* src, uint16_t* x, int rows, int n, float offset, int residual,
+                 const uint16_t* next_w, uint16_t* next, void* stream);
+
+/* argmax (Kernels.metal:704-729) over `rows` rows of n bf16 logits: first index of the maximum,
+ * NaN never wins, all-NaN rows give 0xFFFFFFFF. `scratch` holds rows 64-bit keys. */
+PLAMO_API int plamo_k_argmax(const uint16_t* logits, int rows, int n, uint64_t* scratch, uint32_t* out, void* stream);
+
+/* packed_bits / packed_four (Kernels.metal:23-44): reconstructs `count` bf16 weights (count %
+ * 16 == 0) from a .p12 data region and its tagged block table. */
+PLAMO_API int plamo_k_packed_decode(const uint8_t* data, const uint32_t* entries, long long count, uint16_t* out, void* stream);
+
+/* Split-K decode attention for one query row (attention + attention_merge, Kernels.metal:440-562;
+ * matrix_rotary / softmax / attend, :301-437): q is heads*128 bf16 (already rotated);
+ * keys/values are [cap][kv_heads][128] bf16. Keys r in [0,count) sit at slot (first + r) % cap;
+ * the row sees r in [begin, end). Local layers (full == 0) re-rotate raw keys with coordinate r
+ * using rope_local ([rows][64] u32 = cos bits | sin bits << 16). out: heads*128 bf16.
+ * `splits` key partitions; the partial results live in library-owned device scratch that is
+ * allocated on the first call and grown as needed (cudaMalloc). */
+PLAMO_API int plamo_k_attention(const uint16_t* q, const uint16_t* keys, const uint16_t* values, int heads, int kv_heads,
+                      int cap, int first, int count, int begin, int end, int full, const uint32_t* rope_local,
+                      int splits, uint16_t* out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* PLAMO_KERNELS_H */

@@ -1,0 +1,80 @@
+// Shared device helpers for the sm_100a kernels.
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#define PLAMO_HD 128        // head_dim
+#define PLAMO_EPS 1e-6f     // rms_norm_eps
+#define PLAMO_ATTN_SCALE 0.08838834764831845f  // 1/sqrt(128), Kernels.metal:372
+
+namespace plamo {
+
+constexpr unsigned FULL_MASK = 0xffffffffu;
+
+// bf16 widening and the reference's round-to-nearest-even narrowing (Kernels.metal:5-10); the
+// integer form reproduces its behaviour bit for bit, NaN payloads included.
+__device__ __forceinline__ float bf2f(uint32_t b) { return __uint_as_float(b << 16); }
+__device__ __forceinline__ uint32_t f2bf(float x) {
+    uint32_t u = __float_as_uint(x);
+    return ((u + 0x7fffu + ((u >> 16) & 1u)) >> 16) & 0xffffu;
+}
+__device__ __forceinline__ float rbf(float x) { return bf2f(f2bf(x)); }
+__device__ __forceinline__ float lo_bf(uint32_t pair) { return __uint_as_float(pair << 16); }
+__device__ __forceinline__ float hi_bf(uint32_t pair) { return __uint_as_float(pair & 0xffff0000u); }
+
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+    uint32_t r;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
+    return r;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(FULL_MASK, v, o);
+    return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(FULL_MASK, v, o));
+    return v;
+}
+
+// Reduces NV per-lane values across the warp in 31 shuffles (recursive halving). On return,
+// lane L holds in v[0] the warp total of value index L / (32 / NV) (the top log2(NV) lane bits).
+template <int NV>
+__device__ __forceinline__ float warp_reduce_transposed(float (&v)[NV], int lane) {
+    static_assert(NV >= 1 && NV <= 32 && (NV & (NV - 1)) == 0, "NV must be a power of two <= 32");
+    int n = NV;
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) {
+        if (n > 1) {
+            const bool upper = lane & off;
+#pragma unroll
+            for (int j = 0; j < NV / 2; j++) {
+                if (j < n / 2) {
+                    float send = upper ? v[j] : v[j + n / 2];
+                    float keep = upper ? v[j + n / 2] : v[j];
+                    v[j] = keep + __shfl_xor_sync(FULL_MASK, send, off);
+                }
+            }
+            n >>= 1;
+        } else {
+            v[0] += __shfl_xor_sync(FULL_MASK, v[0], off);
+        }
+    }
+    return v[0];
+}
+
+// Total-order key for the first-index argmax of Kernels.metal:704-729: larger value wins, ties go
+// to the lower index, NaN never wins (no key), -0 == +0. Key 0 means "no candidate".
+__device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t index) {
+    if (v != v) return 0ull;
+    uint32_t b = __float_as_uint(v == 0.0f ? 0.0f : v);
+    uint32_t ordered = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+    return (static_cast<unsigned long long>(ordered) << 32) | static_cast<unsigned long long>(0xffffffffu - index);
+}
+__device__ __forceinline__ uint32_t argmax_index(unsigned long long key) {
+    return key == 0ull ? 0xffffffffu : 0xffffffffu - static_cast<uint32_t>(key & 0xffffffffull);
+}
+
+}  // namespace plamo

@@ -1,0 +1,154 @@
+// Kernel-level C ABI (include/plamo_kernels.h): thin launchers over kernels.cu on caller-owned
+// device buffers.
+#include "../../include/plamo_kernels.h"
+#include "kernels.h"
+
+#include <mutex>
+#include <string>
+
+namespace plamo {
+extern thread_local std::string g_error;
+}
+using namespace plamo;
+
+static int kfail(cudaError_t e) {
+    g_error = std::string("CUDA error: ") + cudaGetErrorString(e);
+    return 1;
+}
+
+static bool configured() {
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess) return false;
+    static std::mutex mu;
+    static bool done[64] = {false};
+    std::lock_guard<std::mutex> lock(mu);
+    if (dev < 0 || dev >= 64) return false;
+    if (!done[dev]) done[dev] = configure_kernels() == cudaSuccess;
+    return done[dev];
+}
+
+namespace {
+__global__ void k_keys_to_index(const unsigned long long* keys, int rows, uint32_t* out) {
+    const int r = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r < rows) {
+        const unsigned long long k = keys[r];
+        out[r] = k == 0ull ? 0xffffffffu : 0xffffffffu - uint32_t(k & 0xffffffffull);
+    }
+}
+}  // namespace
+
+extern "C" {
+
+int plamo_k_linear(const void* w, const uint32_t* offsets, const uint16_t* x, int rows, int K, int M, int mode,
+                   uint16_t* y, uint64_t* argmax_keys, void* stream) {
+    if (!w || !x || !y || rows < 1 || K < 128 || K % 128 || M < 1 || mode < 0 || mode > 2 ||
+        (mode == 1 && M % 2) || (mode == 2 && !argmax_keys)) {
+        g_error = "Invalid linear arguments";
+        return 1;
+    }
+    if (!configured()) { g_error = "Cannot configure kernels"; return 1; }
+    GemvArgs a;
+    a.lin.w = static_cast<const uint8_t*>(w);
+    a.lin.offsets = offsets;
+    a.lin.M = M;
+    a.lin.K = K;
+    a.x = x;
+    a.rows = rows;
+    a.y = y;
+    a.ystride = mode == 1 ? M / 2 : M;
+    a.keys = reinterpret_cast<unsigned long long*>(argmax_keys);
+    cudaError_t e = launch_gemv(a, mode, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? 0 : kfail(e);
+}
+
+int plamo_k_argmax_keys(const uint64_t* keys, int rows, uint32_t* out, void* stream) {
+    if (!keys || !out || rows < 1) { g_error = "Invalid arguments"; return 1; }
+    k_keys_to_index<<<(rows + 127) / 128, 128, 0, static_cast<cudaStream_t>(stream)>>>(
+        reinterpret_cast<const unsigned long long*>(keys), rows, out);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? 0 : kfail(e);
+}
+
+int plamo_k_norm(const uint16_t* w, const uint16_t* src, uint16_t* x, int rows, int n, float offset, int residual,
+                 const uint16_t* next_w, uint16_t* next, void* stream) {
+    if (!w || !src || !x || rows < 1 || n < 1 || n > 4096 || (next_w && !next) || (next_w && !residual)) {
+        g_error = "Invalid norm arguments";
+        return 1;
+    }
+    NormArgs a;
+    a.w = w; a.src = src; a.x = x; a.next_w = next_w; a.next = next; a.rows = rows; a.n = n; a.offset = offset;
+    a.residual = residual;
+    cudaError_t e = launch_norm(a, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? 0 : kfail(e);
+}
+
+int plamo_k_argmax(const uint16_t* logits, int rows, int n, uint64_t* scratch, uint32_t* out, void* stream) {
+    if (!logits || !scratch || !out || rows < 1 || n < 1) { g_error = "Invalid argmax arguments"; return 1; }
+    cudaError_t e = launch_argmax(logits, rows, n, reinterpret_cast<unsigned long long*>(scratch), out,
+                                  static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? 0 : kfail(e);
+}
+
+int plamo_k_packed_decode(const uint8_t* data, const uint32_t* entries, long long count, uint16_t* out, void* stream) {
+    if (!data || !entries || !out || count < 16 || count % 16) { g_error = "Invalid decode arguments"; return 1; }
+    cudaError_t e = launch_packed_decode(data, entries, count, out, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? 0 : kfail(e);
+}
+
+// Library-owned scratch for plamo_k_attention (per device, grown on demand, freed at exit).
+struct AttnScratch {
+    void* base = nullptr;
+    size_t bytes = 0;
+};
+static AttnScratch g_attn_scratch[64];
+static std::mutex g_attn_mu;
+
+int plamo_k_attention(const uint16_t* q, const uint16_t* keys, const uint16_t* values, int heads, int kv_heads,
+                      int cap, int first, int count, int begin, int end, int full, const uint32_t* rope_local,
+                      int splits, uint16_t* out, void* stream) {
+    if (!q || !keys || !values || !out || heads < 1 || heads > 32 || kv_heads < 1 || heads % kv_heads || cap < 1 ||
+        first < 0 || count < 1 || count > cap || begin < 0 || end > count || begin >= end || splits < 1 ||
+        splits > 4096 || (!full && !rope_local)) {
+        g_error = "Invalid attention arguments";
+        return 1;
+    }
+    if (!configured()) { g_error = "Cannot configure kernels"; return 1; }
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const int per_max = attention_per_max(count, splits);
+    if (attention_smem(heads, kv_heads, per_max) > 200 * 1024) { g_error = "Too few attention splits"; return 1; }
+    // scratch: RowDesc + RowGeo + partial outputs + (max, sum) statistics
+    const size_t part_o = size_t(splits) * heads * 128 * sizeof(float);
+    const size_t part_ml = size_t(splits) * heads * sizeof(float2);
+    const size_t need = 256 + part_o + part_ml;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    std::lock_guard<std::mutex> lock(g_attn_mu);
+    AttnScratch& sc = g_attn_scratch[dev & 63];
+    if (sc.bytes < need) {
+        if (sc.base) { cudaStreamSynchronize(s); cudaFree(sc.base); sc.base = nullptr; sc.bytes = 0; }
+        cudaError_t e = cudaMalloc(&sc.base, need);
+        if (e != cudaSuccess) return kfail(e);
+        sc.bytes = need;
+    }
+    uint8_t* base = static_cast<uint8_t*>(sc.base);
+    RowDesc* desc = reinterpret_cast<RowDesc*>(base);
+    RowGeo* geo = reinterpret_cast<RowGeo*>(base + 64);
+    const RowDesc hd{0, 0, 0, 1};
+    const RowGeo hg{first, count, begin, end};
+    cudaError_t e = cudaMemcpyAsync(desc, &hd, sizeof(hd), cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(geo, &hg, sizeof(hg), cudaMemcpyHostToDevice, s);
+    if (e != cudaSuccess) return kfail(e);
+    AttnArgs a;
+    a.q = q; a.keys = keys; a.values = values; a.desc = desc; a.geo = geo; a.rope_local = rope_local;
+    a.part_o = reinterpret_cast<float*>(base + 256);
+    a.part_ml = reinterpret_cast<float2*>(base + 256 + part_o);
+    a.out = out; a.lane_stride = 0; a.rows = 1; a.H = heads; a.KV = kv_heads; a.cap = cap; a.full = full;
+    a.splits = splits; a.per_max = per_max;
+    e = launch_attention(a, s);
+    if (e != cudaSuccess) return kfail(e);
+    // the host-side descriptors must outlive the async copies
+    e = cudaStreamSynchronize(s);
+    return e == cudaSuccess ? 0 : kfail(e);
+}
+
+}  // extern "C"

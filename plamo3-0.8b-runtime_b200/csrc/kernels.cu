@@ -1,0 +1,682 @@
+// sm_100a kernels for the PLaMo-3 decoder hot path (CUDA-core path: batch-1 / few-row decode
+// GEMVs, norms, QK-norm + RoPE + KV append, split-K attention, argmax).
+//
+// Reference counterparts (mikuteto-dev/plamo3-0.8b-runtime, Sources/Plamo/):
+//   k_gemv         Kernels.metal:92-114 (linear), :149-200 (matrix), Batch.metal:171-221
+//                  (project3/4), :202-210 (swiglu, fused here), :704-729 (argmax, fused here)
+//   load16<true>   Kernels.metal:23-44 (packed_bits / packed_four)
+//   k_norm         Kernels.metal:46-90
+//   k_embed_norm   Runtime.swift:104-110 + :377
+//   k_qkv          Kernels.metal:223-274, Batch.metal:1-39
+//   k_attn_*       Kernels.metal:277-285, :301-345, :358-437, :440-562, Batch.metal:42-168
+#include "common.cuh"
+#include "kernels.h"
+
+#include <cfloat>
+
+namespace plamo {
+
+// --------------------------------------------------------------------------------------------
+// streaming loads (weights are read once per token: keep them out of L1)
+__device__ __forceinline__ uint4 ld_stream(const void* p) {
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+    return v;
+}
+__device__ __forceinline__ uint2 ld_stream2(const void* p) {
+    uint2 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
+    return v;
+}
+
+// Decodes 16 consecutive weights of one packed block into 8 bf16 pairs.
+// sm: 16 sign|mantissa bytes; codes: 16 4-bit exponent codes (low nibble first); minimum: block
+// minimum exponent (108..170). bits = (sm & 127) | (sm & 128) << 8 | (code == 15 ? 0 : min+code) << 7.
+__device__ __forceinline__ void decode16(uint4 sm, uint2 codes, uint32_t minimum, uint32_t (&wp)[8]) {
+    const uint32_t zx = ((codes.x & 0x77777777u) + 0x11111111u) & codes.x & 0x88888888u;
+    const uint32_t zy = ((codes.y & 0x77777777u) + 0x11111111u) & codes.y & 0x88888888u;
+    const uint32_t s[4] = {sm.x, sm.y, sm.z, sm.w};
+    if ((zx | zy) == 0u) {
+        // No signed-zero codes: two weights per 32-bit operation.
+        const uint32_t min7 = (minimum << 7) * 0x00010001u;
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            const uint32_t w = h ? codes.y : codes.x;
+            const uint32_t lo = w & 0x0F0F0F0Fu, hi = (w >> 4) & 0x0F0F0F0Fu;
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                // [code(2k) | 0 | code(2k+1) | 0] as two 16-bit halves (sign-replicate gives 0x00)
+                const uint32_t c2 = prmt(lo, hi, uint32_t(k) | (uint32_t(8 | k) << 4) | (uint32_t(4 + k) << 8) |
+                                                     (uint32_t(8 | (4 + k)) << 12));
+                const uint32_t e7 = c2 * 128u + min7;
+                const uint32_t p = 2u * (k & 1);
+                const uint32_t dup = prmt(s[2 * h + (k >> 1)], 0u, p | (p << 4) | ((p + 1) << 8) | ((p + 1) << 12));
+                wp[4 * h + k] = (dup & 0x807F807Fu) | e7;
+            }
+        }
+    } else {
+#pragma unroll
+        for (int e = 0; e < 16; e += 2) {
+            uint32_t out = 0;
+#pragma unroll
+            for (int q = 0; q < 2; q++) {
+                const uint32_t i = e + q;
+                const uint32_t b = (s[i >> 2] >> (8 * (i & 3))) & 255u;
+                const uint32_t cw = i < 8 ? codes.x : codes.y;
+                const uint32_t code = (cw >> (4 * (i & 7))) & 15u;
+                const uint32_t ex = code == 15u ? 0u : minimum + code;
+                out |= ((b & 127u) | ((b & 128u) << 8) | (ex << 7)) << (16 * q);
+            }
+            wp[e >> 1] = out;
+        }
+    }
+}
+
+// 16 consecutive weights starting at flat element `el` (multiple of 16) as bf16 pairs.
+template <bool PACKED>
+__device__ __forceinline__ void load16(const Linear& lin, size_t el, uint32_t (&wp)[8]) {
+    if (!PACKED) {
+        const uint8_t* p = lin.w + el * 2;
+        const uint4 a = ld_stream(p), b = ld_stream(p + 16);
+        wp[0] = a.x; wp[1] = a.y; wp[2] = a.z; wp[3] = a.w;
+        wp[4] = b.x; wp[5] = b.y; wp[6] = b.z; wp[7] = b.w;
+    } else {
+        const uint32_t entry = __ldg(lin.offsets + (el >> 7));
+        const uint32_t i0 = uint32_t(el & 127);
+        const uint8_t* blk = lin.w + (entry & ~63u);
+        const uint32_t tag = entry & 63u;
+        if (tag) {
+            const uint4 sm = ld_stream(blk + i0);
+            const uint2 cd = ld_stream2(blk + 128 + (i0 >> 1));
+            decode16(sm, cd, tag + 107u, wp);
+        } else {
+            const uint4 a = ld_stream(blk + 2 * i0), b = ld_stream(blk + 2 * i0 + 16);
+            wp[0] = a.x; wp[1] = a.y; wp[2] = a.z; wp[3] = a.w;
+            wp[4] = b.x; wp[5] = b.y; wp[6] = b.z; wp[7] = b.w;
+        }
+    }
+}
+
+// --------------------------------------------------------------------------------------------
+// GEMV over R activation rows. One warp per output row; lane l covers weights
+// [g*512 + 16l, +16) of every 512-weight group g, so raw and packed weights are summed in the same
+// order (packed == raw bit for bit). x is staged in shared memory, permuted so that each 16-byte
+// shared load of a warp is conflict-free.
+template <int R, bool PACKED, int MODE>
+__global__ void __launch_bounds__(256) k_gemv(GemvArgs a) {
+    extern __shared__ uint4 xs[];
+    constexpr int NW = MODE == GEMV_SWIGLU ? 2 : 1;
+    // Two interleaved accumulators per (weight row, activation row): the per-row summation order
+    // is the same for every R and mode, so a batched step equals the batch-1 path bit for bit.
+    constexpr int A = 2;
+    constexpr int NV = NW * R;
+    constexpr int UG = R <= 4 ? 4 : 2;
+    const int K = a.lin.K, K8 = K >> 3, KP8 = (K8 + 63) & ~63;
+    const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    for (int i = t; i < R * K8; i += 256) {
+        const int r = i / K8, c = i - r * K8;
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (r < a.rows) v = reinterpret_cast<const uint4*>(a.x + size_t(r) * K)[c];
+        const int g = c >> 6, within = c & 63;
+        xs[r * KP8 + g * 64 + (within & 1) * 32 + (within >> 1)] = v;
+    }
+    __syncthreads();
+    const int Mout = MODE == GEMV_SWIGLU ? a.lin.M / 2 : a.lin.M;
+    const int G = (K + 511) >> 9;
+    constexpr int STRIDE = 32 / NV;
+    const int idx = lane / STRIDE;
+    const bool holder = (lane % STRIDE) == 0;
+    unsigned long long best = 0ull;
+    for (int m = blockIdx.x * 8 + warp; m < Mout; m += gridDim.x * 8) {
+        float acc[NW][R][A];
+#pragma unroll
+        for (int wr = 0; wr < NW; wr++)
+#pragma unroll
+            for (int r = 0; r < R; r++)
+#pragma unroll
+                for (int q = 0; q < A; q++) acc[wr][r][q] = 0.f;
+        for (int g0 = 0; g0 < G; g0 += UG) {
+            uint32_t wp[UG][NW][8];
+#pragma unroll
+            for (int u = 0; u < UG; u++) {
+                const int e0 = (g0 + u) * 512 + lane * 16;
+#pragma unroll
+                for (int wr = 0; wr < NW; wr++) {
+                    if (g0 + u < G && e0 < K) {
+                        load16<PACKED>(a.lin, size_t(m + wr * Mout) * K + e0, wp[u][wr]);
+                    } else {
+#pragma unroll
+                        for (int k = 0; k < 8; k++) wp[u][wr][k] = 0u;
+                    }
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < UG; u++) {
+                const int g = g0 + u;
+                if (g < G && g * 512 + lane * 16 < K) {
+#pragma unroll
+                    for (int r = 0; r < R; r++) {
+                        const uint4 xa = xs[r * KP8 + g * 64 + lane];
+                        const uint4 xb = xs[r * KP8 + g * 64 + 32 + lane];
+                        const uint32_t xp[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+#pragma unroll
+                        for (int wr = 0; wr < NW; wr++)
+#pragma unroll
+                            for (int k = 0; k < 8; k++) {
+                                acc[wr][r][(2 * k) % A] = fmaf(lo_bf(wp[u][wr][k]), lo_bf(xp[k]), acc[wr][r][(2 * k) % A]);
+                                acc[wr][r][(2 * k + 1) % A] = fmaf(hi_bf(wp[u][wr][k]), hi_bf(xp[k]), acc[wr][r][(2 * k + 1) % A]);
+                            }
+                    }
+                }
+            }
+        }
+        float v[NV];
+#pragma unroll
+        for (int wr = 0; wr < NW; wr++)
+#pragma unroll
+            for (int r = 0; r < R; r++)
+                v[wr * R + r] = acc[wr][r][0] + acc[wr][r][1];
+        const float res = warp_reduce_transposed<NV>(v, lane);
+        if (MODE == GEMV_SWIGLU) {
+            const float u = __shfl_down_sync(FULL_MASK, res, 16);
+            if (holder && idx < R && idx < a.rows) {
+                const float gq = rbf(res), uq = rbf(u);
+                const float act = rbf(rbf(gq / (1.0f + expf(-gq))) * uq);
+                const int orow = a.out_map ? a.out_map[idx] : idx;
+                a.y[size_t(orow) * a.ystride + m] = uint16_t(f2bf(act));
+            }
+        } else if (holder && idx < a.rows) {
+            const int orow = a.out_map ? a.out_map[idx] : idx;
+            const uint32_t b = f2bf(res);
+            a.y[size_t(orow) * a.ystride + m] = uint16_t(b);
+            if (MODE == GEMV_LOGITS) {
+                const unsigned long long key = argmax_key(bf2f(b), uint32_t(m));
+                best = key > best ? key : best;
+            }
+        }
+    }
+    if (MODE == GEMV_LOGITS) {
+        __shared__ unsigned long long s_best[8][R];
+        if (holder) s_best[warp][idx] = best;
+        __syncthreads();
+        if (t < R && t < a.rows) {
+            unsigned long long b = 0ull;
+#pragma unroll
+            for (int w = 0; w < 8; w++) b = s_best[w][t] > b ? s_best[w][t] : b;
+            const int orow = a.out_map ? a.out_map[t] : t;
+            if (b) atomicMax(a.keys + orow, b);
+        }
+    }
+}
+
+// --------------------------------------------------------------------------------------------
+// RMSNorm rows (Kernels.metal:46-90). One CTA of 256 threads per row, n <= 4096.
+constexpr int NPT = 16;
+
+__device__ __forceinline__ float block_sum(float v, float* red) {
+    v = warp_sum(v);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    __syncthreads();
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    if (warp == 0) {
+        float s = lane < 8 ? red[lane] : 0.f;
+        s = warp_sum(s);
+        if (lane == 0) red[8] = s;
+    }
+    __syncthreads();
+    return red[8];
+}
+
+__device__ __forceinline__ void norm_row(const float (&v)[NPT], int n, const uint16_t* w, float offset, float* red,
+                                         float (&z)[NPT]) {
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < NPT; j++) ss = fmaf(v[j], v[j], ss);
+    const float total = block_sum(ss, red);
+    const float scale = 1.0f / sqrtf(total / float(n) + PLAMO_EPS);
+#pragma unroll
+    for (int j = 0; j < NPT; j++) {
+        const int i = threadIdx.x + j * 256;
+        z[j] = i < n ? rbf(rbf(v[j] * scale) * rbf(bf2f(w[i]) + offset)) : 0.f;
+    }
+}
+
+__global__ void __launch_bounds__(256) k_norm(NormArgs a) {
+    __shared__ float red[9];
+    const int r = blockIdx.x;
+    float v[NPT], z[NPT];
+#pragma unroll
+    for (int j = 0; j < NPT; j++) {
+        const int i = threadIdx.x + j * 256;
+        v[j] = i < a.n ? bf2f(a.src[size_t(r) * a.n + i]) : 0.f;
+    }
+    norm_row(v, a.n, a.w, a.offset, red, z);
+    if (!a.residual) {
+        const int orow = a.out_map ? a.out_map[r] : r;
+#pragma unroll
+        for (int j = 0; j < NPT; j++) {
+            const int i = threadIdx.x + j * 256;
+            if (i < a.n) {
+                const uint16_t b = uint16_t(f2bf(z[j]));
+                a.x[size_t(r) * a.n + i] = b;
+                if (a.y2) a.y2[size_t(orow) * a.n + i] = b;
+            }
+        }
+        return;
+    }
+#pragma unroll
+    for (int j = 0; j < NPT; j++) {
+        const int i = threadIdx.x + j * 256;
+        if (i < a.n) {
+            const float val = rbf(bf2f(a.x[size_t(r) * a.n + i]) + z[j]);
+            a.x[size_t(r) * a.n + i] = uint16_t(f2bf(val));
+            v[j] = val;
+        } else {
+            v[j] = 0.f;
+        }
+    }
+    if (!a.next_w) return;
+    norm_row(v, a.n, a.next_w, 1.0f, red, z);
+#pragma unroll
+    for (int j = 0; j < NPT; j++) {
+        const int i = threadIdx.x + j * 256;
+        if (i < a.n) a.next[size_t(r) * a.n + i] = uint16_t(f2bf(z[j]));
+    }
+}
+
+// Embedding gather (bf16 rows, exact) + layer-0 pre-mixer norm; clears the argmax keys the head
+// of this call will write.
+__global__ void __launch_bounds__(256) k_embed_norm(const int* ids, int vocab, const uint16_t* embed, const uint16_t* w,
+                                                    int d, uint16_t* x, uint16_t* h, unsigned long long* keys,
+                                                    const int* key_map, int nkeys) {
+    __shared__ float red[9];
+    const int r = blockIdx.x;
+    if (r == 0 && keys)
+        for (int i = threadIdx.x; i < nkeys; i += 256) keys[key_map ? key_map[i] : i] = 0ull;
+    // Host-supplied ids are validated before upload; a device-chained id (an argmax) is always in
+    // range unless every logit was NaN, in which case row 0 is read instead of faulting.
+    const int id = ids[r];
+    const size_t row = size_t(id >= 0 && id < vocab ? id : 0) * d;
+    float v[NPT], z[NPT];
+#pragma unroll
+    for (int j = 0; j < NPT; j++) {
+        const int i = threadIdx.x + j * 256;
+        uint16_t b = 0;
+        if (i < d) { b = embed[row + i]; x[size_t(r) * d + i] = b; }
+        v[j] = bf2f(b);
+    }
+    norm_row(v, d, w, 1.0f, red, z);
+#pragma unroll
+    for (int j = 0; j < NPT; j++) {
+        const int i = threadIdx.x + j * 256;
+        if (i < d) h[size_t(r) * d + i] = uint16_t(f2bf(z[j]));
+    }
+}
+
+// --------------------------------------------------------------------------------------------
+// Rotate-half RoPE with a bf16 (cos, sin) pair (Kernels.metal:261-274).
+__device__ __forceinline__ float rope_rotate(float x, float other, int d, uint32_t cs) {
+    const float c = lo_bf(cs), s = hi_bf(cs);
+    return rbf(rbf(x * c) + rbf((d < 64 ? -other : other) * s));
+}
+
+// Per (row, head) warp: QK RMSNorm (w + 1), RoPE of queries, KV append into the ring slot
+// pos % cap of the row's lane slab (global layers store rotated keys, local layers raw keys).
+__global__ void __launch_bounds__(128) k_qkv(QkvArgs a) {
+    const int gw = blockIdx.x * 4 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    const int heads = a.H + a.KV;
+    if (gw >= a.rows * heads) return;
+    const int r = gw / heads, h = gw - r * heads;
+    const RowDesc dsc = a.desc[r];
+    int first, count, begin, end, qcoord;
+    if (a.full) {
+        first = 0; count = dsc.cstart + dsc.crows; end = dsc.pos + 1; begin = 0; qcoord = dsc.pos;
+    } else {  // Runtime.swift:389-392, Kernels.metal:251,368-369, Batch.metal:31
+        first = max(0, dsc.cstart - (a.W - 1));
+        count = dsc.cstart + dsc.crows - first;
+        end = dsc.pos - first + 1;
+        begin = max(0, end - a.W);
+        qcoord = dsc.pos - first;
+    }
+    if (h == 0 && lane == 0) a.geo[r] = RowGeo{first, count, begin, end};
+    const int width = (a.H + 2 * a.KV) * 128;
+    const uint16_t* src = a.qkv + size_t(r) * width + h * 128;
+    float v[4], ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; j++) { v[j] = bf2f(src[lane + 32 * j]); ss = fmaf(v[j], v[j], ss); }
+    ss = warp_sum(ss);
+    const float scale = 1.0f / sqrtf(ss / 128.0f + PLAMO_EPS);
+    const uint16_t* nw = h < a.H ? a.q_norm : a.k_norm;
+    float z[4];
+#pragma unroll
+    for (int j = 0; j < 4; j++) z[j] = rbf(rbf(v[j] * scale) * rbf(bf2f(nw[lane + 32 * j]) + 1.0f));
+    if (h < a.H) {
+        const uint32_t* table = a.full ? a.rope_global + size_t(qcoord) * 64 : a.rope_local + size_t(qcoord) * 64;
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const int d = lane + 32 * j;
+            a.q[size_t(r) * a.H * 128 + h * 128 + d] = uint16_t(f2bf(rope_rotate(z[j], z[(j + 2) & 3], d, table[d & 63])));
+        }
+    } else {
+        const int kvh = h - a.H;
+        const size_t slot = size_t(dsc.lane) * a.lane_stride + (size_t(dsc.pos % a.cap) * a.KV + kvh) * 128;
+        const uint32_t* table = a.rope_global + size_t(dsc.pos) * 64;
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const int d = lane + 32 * j;
+            const float k = a.full ? rope_rotate(z[j], z[(j + 2) & 3], d, table[d & 63]) : z[j];
+            a.keys[slot + d] = uint16_t(f2bf(k));
+            a.values[slot + d] = src[a.KV * 128 + d];  // v head kvh sits KV heads after k head kvh
+        }
+    }
+}
+
+// --------------------------------------------------------------------------------------------
+// Split-K attention. CTA (split s, row r) covers keys [s*per, (s+1)*per) of the row's window
+// (clipped to its visible range), computes scores for all heads (MQA/GQA: key tiles shared),
+// local softmax statistics and the unnormalised P.V partial; k_attn_merge combines the splits
+// (log-sum-exp) and rounds to bf16 (Kernels.metal:440-562).
+constexpr int QS = 132;
+
+int attention_per_max(int cap, int splits) { return ((cap + splits - 1) / splits + 31) & ~31; }
+size_t attention_smem(int H, int KV, int per_max) {
+    return sizeof(float) * (size_t(H) * QS + 32 * size_t(KV * 128 + 1) + size_t(H) * per_max);
+}
+
+__global__ void __launch_bounds__(256) k_attn_partial(AttnArgs a) {
+    extern __shared__ float smem[];
+    const int r = blockIdx.y, s = blockIdx.x, t = threadIdx.x;
+    const RowGeo g = a.geo[r];
+    const int lane_id = a.desc[r].lane;
+    const int H = a.H, KV = a.KV, group = H / KV, KS = KV * 128 + 1;
+    int per = (g.count + a.splits - 1) / a.splits;
+    per = (per + 31) & ~31;
+    const int k0 = s * per, k1 = min(k0 + per, g.count);
+    const int lo = max(k0, g.begin), hi = min(k1, g.end);
+    float2* ml = a.part_ml + (size_t(r) * a.splits + s) * H;
+    if (lo >= hi) {
+        for (int h = t; h < H; h += 256) ml[h] = make_float2(-INFINITY, 0.f);
+        return;
+    }
+    float* qs = smem;
+    float* ks = qs + H * QS;
+    float* sc = ks + 32 * KS;
+    const uint16_t* kbase = a.keys + size_t(lane_id) * a.lane_stride;
+    const uint16_t* vbase = a.values + size_t(lane_id) * a.lane_stride;
+    for (int i = t; i < H * 128; i += 256) qs[(i >> 7) * QS + (i & 127)] = bf2f(a.q[size_t(r) * H * 128 + i]);
+    const int n = hi - lo;
+    for (int t0 = 0; t0 < n; t0 += 32) {
+        __syncthreads();
+        const int tk = min(32, n - t0);
+        for (int i = t; i < 32 * KV * 128; i += 256) {
+            const int j = i / (KV * 128), e = i - j * (KV * 128);
+            float val = 0.f;
+            if (j < tk) {
+                const int key = lo + t0 + j;
+                const int phys = (g.first + key) % a.cap;
+                const uint16_t* kr = kbase + size_t(phys) * KV * 128;
+                if (a.full) {
+                    val = bf2f(kr[e]);
+                } else {  // window-relative re-rotation of raw local keys (Kernels.metal:277-285)
+                    const int d = e & 127, kvoff = e - d, partner = d < 64 ? d + 64 : d - 64;
+                    val = rope_rotate(bf2f(kr[kvoff + d]), bf2f(kr[kvoff + partner]), d, a.rope_local[key * 64 + (d & 63)]);
+                }
+            }
+            ks[j * KS + e] = val;
+        }
+        __syncthreads();
+        const int j = t & 31;
+        if (j < tk) {
+            for (int h = t >> 5; h < H; h += 8) {
+                const float* qh = qs + h * QS;
+                const float* kj = ks + j * KS + (h / group) * 128;
+                float acc = 0.f;
+#pragma unroll 16
+                for (int d = 0; d < 128; d++) acc = fmaf(qh[d], kj[d], acc);
+                sc[h * a.per_max + t0 + j] = acc * PLAMO_ATTN_SCALE;
+            }
+        }
+    }
+    __syncthreads();
+    const int warp = t >> 5, lane = t & 31;
+    for (int h = warp; h < H; h += 8) {
+        float* p = sc + h * a.per_max;
+        float m = -INFINITY;
+        for (int i = lane; i < n; i += 32) m = fmaxf(m, p[i]);
+        m = warp_max(m);
+        float l = 0.f;
+        for (int i = lane; i < n; i += 32) { const float e = expf(p[i] - m); p[i] = e; l += e; }
+        l = warp_sum(l);
+        if (lane == 0) ml[h] = make_float2(m, l);
+    }
+    __syncthreads();
+    const int d = t & 127, hh = t >> 7;
+    float acc[16];
+#pragma unroll
+    for (int q = 0; q < 16; q++) acc[q] = 0.f;
+    for (int i = 0; i < n; i++) {
+        const int phys = (g.first + lo + i) % a.cap;
+        const uint16_t* vr = vbase + size_t(phys) * KV * 128;
+        if (KV == 1) {
+            const float v = bf2f(vr[d]);
+#pragma unroll
+            for (int q = 0; q < 16; q++) {
+                const int h = hh + 2 * q;
+                if (h < H) acc[q] = fmaf(sc[h * a.per_max + i], v, acc[q]);
+            }
+        } else {
+#pragma unroll
+            for (int q = 0; q < 16; q++) {
+                const int h = hh + 2 * q;
+                if (h < H) acc[q] = fmaf(sc[h * a.per_max + i], bf2f(vr[(h / group) * 128 + d]), acc[q]);
+            }
+        }
+    }
+    float* po = a.part_o + (size_t(r) * a.splits + s) * H * 128;
+#pragma unroll
+    for (int q = 0; q < 16; q++) {
+        const int h = hh + 2 * q;
+        if (h < H) po[h * 128 + d] = acc[q];
+    }
+}
+
+__global__ void __launch_bounds__(128) k_attn_merge(AttnArgs a) {
+    const int r = blockIdx.x / a.H, h = blockIdx.x - r * a.H, d = threadIdx.x;
+    const float2* ml = a.part_ml + size_t(r) * a.splits * a.H;
+    float M = -INFINITY;
+    for (int s = 0; s < a.splits; s++) M = fmaxf(M, ml[s * a.H + h].x);
+    float L = 0.f, o = 0.f;
+    for (int s = 0; s < a.splits; s++) {
+        const float2 st = ml[s * a.H + h];
+        if (st.y > 0.f) {
+            const float w = expf(st.x - M);
+            L += w * st.y;
+            o = fmaf(a.part_o[((size_t(r) * a.splits + s) * a.H + h) * 128 + d], w, o);
+        }
+    }
+    a.out[size_t(r) * a.H * 128 + h * 128 + d] = uint16_t(f2bf(o / L));
+}
+
+// --------------------------------------------------------------------------------------------
+// Converts argmax keys to ids. Device-chained decode also feeds the id back as the next input,
+// advances the row descriptor and appends the id to a bounded history.
+__global__ void k_finalize(const unsigned long long* keys, const int* key_map, int rows, int* result,
+                           int* chain_ids, RowDesc* advance, int* hist, int* hist_count, int hist_cap) {
+    const int r = threadIdx.x;
+    if (r >= rows) return;
+    const int k = key_map ? key_map[r] : r;
+    const uint32_t id = argmax_index(keys[k]);
+    result[k] = int(id);
+    if (chain_ids) chain_ids[r] = int(id);
+    if (advance) { advance[r].pos += 1; advance[r].cstart += 1; }
+    if (hist && r == 0) {
+        const int c = *hist_count;
+        if (c < hist_cap) hist[c] = int(id);
+        *hist_count = c + 1;
+    }
+}
+
+// Standalone first-index argmax over bf16 rows (Kernels.metal:704-729).
+__global__ void __launch_bounds__(256) k_argmax(const uint16_t* logits, int n, unsigned long long* keys) {
+    const int r = blockIdx.y;
+    unsigned long long best = 0ull;
+    for (int i = blockIdx.x * 256 + threadIdx.x; i < n; i += gridDim.x * 256) {
+        const unsigned long long k = argmax_key(bf2f(logits[size_t(r) * n + i]), uint32_t(i));
+        best = k > best ? k : best;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long other = __shfl_xor_sync(FULL_MASK, best, o);
+        best = other > best ? other : best;
+    }
+    if ((threadIdx.x & 31) == 0 && best) atomicMax(keys + r, best);
+}
+
+__global__ void k_packed_decode(Linear lin, long long count, uint16_t* out) {
+    const long long c = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (c * 16 >= count) return;
+    uint32_t wp[8];
+    load16<true>(lin, size_t(c) * 16, wp);
+#pragma unroll
+    for (int k = 0; k < 8; k++) reinterpret_cast<uint32_t*>(out + c * 16)[k] = wp[k];
+}
+
+// --------------------------------------------------------------------------------------------
+// launchers
+
+constexpr size_t GEMV_SMEM_MAX = 227 * 1024;
+
+template <int R, bool P, int M>
+static cudaError_t gemv_launch(const GemvArgs& a, cudaStream_t s) {
+    const int K8 = a.lin.K >> 3, KP8 = (K8 + 63) & ~63;
+    const size_t smem = size_t(R) * KP8 * 16;
+    const int Mout = M == GEMV_SWIGLU ? a.lin.M / 2 : a.lin.M;
+    int grid = (Mout + 7) / 8;
+    if (M == GEMV_LOGITS) grid = grid < 148 * 4 ? grid : 148 * 4;
+    k_gemv<R, P, M><<<grid, 256, smem, s>>>(a);
+    return cudaGetLastError();
+}
+
+template <int R, bool P>
+static cudaError_t gemv_mode(const GemvArgs& a, int mode, cudaStream_t s) {
+    switch (mode) {
+        case GEMV_PLAIN: return gemv_launch<R, P, GEMV_PLAIN>(a, s);
+        case GEMV_SWIGLU: return gemv_launch<R, P, GEMV_SWIGLU>(a, s);
+        default: return gemv_launch<R, P, GEMV_LOGITS>(a, s);
+    }
+}
+
+template <bool P>
+static cudaError_t gemv_rows(const GemvArgs& a, int mode, cudaStream_t s) {
+    if (a.rows <= 1) return gemv_mode<1, P>(a, mode, s);
+    if (a.rows <= 2) return gemv_mode<2, P>(a, mode, s);
+    if (a.rows <= 4) return gemv_mode<4, P>(a, mode, s);
+    if (a.rows <= 8) return gemv_mode<8, P>(a, mode, s);
+    return gemv_mode<16, P>(a, mode, s);
+}
+
+cudaError_t launch_gemv(const GemvArgs& a, int mode, cudaStream_t s) {
+    if (a.lin.K % 128 || a.lin.K > 8192 || a.rows < 1) return cudaErrorInvalidValue;
+    // Rows beyond what the staged activations allow (16, fewer for very long K) run in passes;
+    // the weights are re-read once per pass.
+    const size_t row_bytes = size_t(((a.lin.K >> 3) + 63) & ~63) * 16;
+    int pass = 16;
+    while (pass > 1 && size_t(pass) * row_bytes > GEMV_SMEM_MAX) pass >>= 1;
+    for (int r0 = 0; r0 < a.rows; r0 += pass) {
+        GemvArgs b = a;
+        b.rows = a.rows - r0 < pass ? a.rows - r0 : pass;
+        b.x = a.x + size_t(r0) * a.lin.K;
+        if (a.out_map) b.out_map = a.out_map + r0;
+        else b.y = a.y + size_t(r0) * a.ystride;
+        cudaError_t e = a.lin.offsets ? gemv_rows<true>(b, mode, s) : gemv_rows<false>(b, mode, s);
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
+}
+
+template <int R, bool P, int M>
+static cudaError_t gemv_attr() {
+    return cudaFuncSetAttribute(k_gemv<R, P, M>, cudaFuncAttributeMaxDynamicSharedMemorySize, GEMV_SMEM_MAX);
+}
+template <int R, bool P>
+static cudaError_t gemv_attr_modes() {
+    cudaError_t e = gemv_attr<R, P, GEMV_PLAIN>();
+    if (e == cudaSuccess) e = gemv_attr<R, P, GEMV_SWIGLU>();
+    if (e == cudaSuccess) e = gemv_attr<R, P, GEMV_LOGITS>();
+    return e;
+}
+
+cudaError_t configure_kernels() {
+    cudaError_t e = cudaSuccess;
+#define PLAMO_ATTR(R)                                                    \
+    if (e == cudaSuccess) e = gemv_attr_modes<R, false>();               \
+    if (e == cudaSuccess) e = gemv_attr_modes<R, true>();
+    PLAMO_ATTR(1) PLAMO_ATTR(2) PLAMO_ATTR(4) PLAMO_ATTR(8) PLAMO_ATTR(16)
+#undef PLAMO_ATTR
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(k_attn_partial, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    return e;
+}
+
+cudaError_t launch_embed_norm(const int* ids, int rows, int vocab, const uint16_t* embed, const uint16_t* w, int d,
+                              uint16_t* x, uint16_t* h, unsigned long long* keys, const int* key_map, int nkeys,
+                              cudaStream_t s) {
+    if (d > 256 * NPT) return cudaErrorInvalidValue;
+    k_embed_norm<<<rows, 256, 0, s>>>(ids, vocab, embed, w, d, x, h, keys, key_map, nkeys);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_norm(const NormArgs& a, cudaStream_t s) {
+    if (a.n > 256 * NPT) return cudaErrorInvalidValue;
+    k_norm<<<a.rows, 256, 0, s>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_qkv(const QkvArgs& a, cudaStream_t s) {
+    const int warps = a.rows * (a.H + a.KV);
+    k_qkv<<<(warps + 3) / 4, 128, 0, s>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s) {
+    if (a.H > 32 || a.H % a.KV) return cudaErrorInvalidValue;
+    const size_t smem = attention_smem(a.H, a.KV, a.per_max);
+    if (smem > 200 * 1024) return cudaErrorInvalidValue;
+    k_attn_partial<<<dim3(a.splits, a.rows), 256, smem, s>>>(a);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    k_attn_merge<<<a.rows * a.H, 128, 0, s>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_finalize(const unsigned long long* keys, const int* key_map, int rows, int* result, int* chain_ids,
+                            RowDesc* advance, int* hist, int* hist_count, int hist_cap, cudaStream_t s) {
+    k_finalize<<<1, 64 * ((rows + 63) / 64), 0, s>>>(keys, key_map, rows, result, chain_ids, advance, hist, hist_count,
+                                                      hist_cap);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_argmax(const uint16_t* logits, int rows, int n, unsigned long long* keys, uint32_t* out,
+                          cudaStream_t s) {
+    cudaError_t e = cudaMemsetAsync(keys, 0, sizeof(unsigned long long) * rows, s);
+    if (e != cudaSuccess) return e;
+    int blocks = (n + 255) / 256;
+    blocks = blocks < 64 ? blocks : 64;
+    k_argmax<<<dim3(blocks, rows), 256, 0, s>>>(logits, n, keys);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    return launch_finalize(keys, nullptr, rows, reinterpret_cast<int*>(out), nullptr, nullptr, nullptr, nullptr, 0, s);
+}
+
+cudaError_t launch_packed_decode(const uint8_t* data, const uint32_t* entries, long long count, uint16_t* out,
+                                 cudaStream_t s) {
+    Linear lin;
+    lin.w = data; lin.offsets = entries;
+    const long long chunks = (count + 15) / 16;
+    k_packed_decode<<<unsigned((chunks + 255) / 256), 256, 0, s>>>(lin, count, out);
+    return cudaGetLastError();
+}
+
+}  // namespace plamo

@@ -1,0 +1,98 @@
+// Kernel launch interface shared by the runtime (runtime.cu) and the kernel-level C ABI.
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace plamo {
+
+// One projection weight: raw bf16 [M][K] (offsets == nullptr) or a .p12 tensor (data region +
+// tagged u32 block table, one entry per 128 weights).
+struct Linear {
+    const uint8_t* w = nullptr;
+    const uint32_t* offsets = nullptr;
+    int M = 0, K = 0;
+};
+
+// Per query row: absolute position, lane (batch slab), and the start/length of the forward call
+// ("chunk") the row belongs to. The chunk start sets the local window base exactly as the
+// reference does for a 16-token chunk (Runtime.swift:389-395).
+struct RowDesc { int pos, lane, cstart, crows; };
+
+// Per query row attention geometry (computed on device by the qkv kernel): keys r in [0,count)
+// live at slot (first + r) % cap of the row's lane slab; the row sees r in [begin, end).
+struct RowGeo { int first, count, begin, end; };
+
+enum GemvMode { GEMV_PLAIN = 0, GEMV_SWIGLU = 1, GEMV_LOGITS = 2 };
+
+struct GemvArgs {
+    Linear lin;
+    const uint16_t* x = nullptr;   // [rows][K] bf16
+    int rows = 1;
+    uint16_t* y = nullptr;         // [out_row][ystride]
+    int ystride = 0;
+    const int* out_map = nullptr;  // optional row -> output row (batch lanes)
+    unsigned long long* keys = nullptr;  // GEMV_LOGITS: argmax keys per output row
+};
+
+struct AttnArgs {
+    const uint16_t* q = nullptr;       // [rows][H*128] rotated queries
+    const uint16_t* keys = nullptr;    // cache base; lane slab = lane * lane_stride elements
+    const uint16_t* values = nullptr;
+    const RowDesc* desc = nullptr;
+    const RowGeo* geo = nullptr;
+    const uint32_t* rope_local = nullptr;  // [rows][64] (cos | sin << 16) bf16 pairs
+    float* part_o = nullptr;           // [rows][splits][H][128]
+    float2* part_ml = nullptr;         // [rows][splits][H]
+    uint16_t* out = nullptr;           // [rows][H*128]
+    long long lane_stride = 0;
+    int rows = 1, H = 16, KV = 1, cap = 0, full = 0, splits = 1, per_max = 0;
+};
+
+struct QkvArgs {
+    const uint16_t* qkv = nullptr;     // [rows][(H+2KV)*128]
+    const uint16_t* q_norm = nullptr;
+    const uint16_t* k_norm = nullptr;
+    uint16_t* q = nullptr;             // [rows][H*128]
+    uint16_t* keys = nullptr;
+    uint16_t* values = nullptr;
+    const RowDesc* desc = nullptr;
+    RowGeo* geo = nullptr;             // written (local or global variant for this layer)
+    const uint32_t* rope_local = nullptr;
+    const uint32_t* rope_global = nullptr;
+    long long lane_stride = 0;
+    int rows = 1, H = 16, KV = 1, cap = 0, W = 2048, full = 0;
+};
+
+struct NormArgs {
+    const uint16_t* w = nullptr;
+    const uint16_t* src = nullptr;     // [rows][n]
+    uint16_t* x = nullptr;             // residual stream (in/out) or plain output when !residual
+    const uint16_t* next_w = nullptr;  // fused next norm (offset 1) or nullptr
+    uint16_t* next = nullptr;
+    uint16_t* y2 = nullptr;            // plain mode: optional second copy at row out_map[r]
+    const int* out_map = nullptr;
+    int rows = 1, n = 0;
+    float offset = 0.f;
+    int residual = 0;
+};
+
+// Launchers (return cudaError_t of the launch).
+cudaError_t launch_embed_norm(const int* ids, int rows, int vocab, const uint16_t* embed, const uint16_t* w, int d,
+                              uint16_t* x, uint16_t* h, unsigned long long* keys, const int* key_map,
+                              int nkeys, cudaStream_t s);
+cudaError_t launch_norm(const NormArgs& a, cudaStream_t s);
+cudaError_t launch_gemv(const GemvArgs& a, int mode, cudaStream_t s);
+cudaError_t launch_qkv(const QkvArgs& a, cudaStream_t s);
+cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s);
+cudaError_t launch_finalize(const unsigned long long* keys, const int* key_map, int rows, int* result,
+                            int* chain_ids, RowDesc* advance, int* hist, int* hist_count, int hist_cap,
+                            cudaStream_t s);
+cudaError_t launch_argmax(const uint16_t* logits, int rows, int n, unsigned long long* keys, uint32_t* out,
+                          cudaStream_t s);
+cudaError_t launch_packed_decode(const uint8_t* data, const uint32_t* entries, long long count, uint16_t* out,
+                                 cudaStream_t s);
+cudaError_t configure_kernels();
+int attention_per_max(int cap, int splits);
+size_t attention_smem(int H, int KV, int per_max);
+
+}  // namespace plamo

@@ -1,0 +1,960 @@
+// Runtime / Batch orchestration behind the C ABI of include/plamo.h.
+//   Runtime.init            Runtime.swift:164-286   -> plamo_open
+//   Runtime.encode/forward  Runtime.swift:321-467   -> Runtime::run / plamo_forward
+//   Runtime.fill/prefill    Runtime.swift:469-483   -> plamo_prefill
+//   Batch.init/prefill/step Batch.swift:33-179      -> plamo_batch_*
+//   decodeBatch             BatchDecode.swift:8-47  -> plamo_batch_generate
+// Device layout: one weight arena (all projection weights, norms, the input embedding and the
+// lm_head, 256-byte aligned; for .p12 the archive payload as is), per-layer KV caches
+// ([capacity][kv_heads][128] bf16; batch slabs [lanes][capacity][kv_heads][128]), RoPE tables and
+// work buffers sized for one 16-token chunk (or the batch's lane count).
+#include "../../include/plamo.h"
+#include "kernels.h"
+#include "loader.h"
+
+#include <dlfcn.h>
+
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstring>
+#include <string>
+#include <vector>
+
+namespace plamo {
+
+thread_local std::string g_error;
+
+static int fail(const std::string& m) {
+    g_error = m;
+    return 1;
+}
+#define CK(call)                                                                                 \
+    do {                                                                                         \
+        cudaError_t _e = (call);                                                                 \
+        if (_e != cudaSuccess) return fail(std::string("CUDA error: ") + cudaGetErrorString(_e)); \
+    } while (0)
+
+static inline uint16_t bits_of(float x) {
+    uint32_t u;
+    memcpy(&u, &x, 4);
+    return uint16_t((u + 0x7fffu + ((u >> 16) & 1u)) >> 16);
+}
+static inline float from_bits(uint16_t b) {
+    uint32_t u = uint32_t(b) << 16;
+    float f;
+    memcpy(&f, &u, 4);
+    return f;
+}
+
+struct Layer {
+    const uint16_t *pre_mixer, *post_mixer, *pre_mlp, *post_mlp, *q_norm, *k_norm;
+    Linear qkv, o, gate_up, down;
+    bool full;
+    int cap, splits, per_max;
+    uint16_t *keys = nullptr, *values = nullptr;
+};
+
+struct CacheView {
+    std::vector<uint16_t*> keys, values;
+    std::vector<long long> stride;
+};
+
+struct Work {
+    int rows_cap = 0;
+    uint16_t *x, *h, *qkv, *q, *att, *proj, *act;
+    RowGeo* geo;
+    RowDesc* desc;
+    int* ids;
+    int* out_map;
+    float* part_o;
+    float2* part_ml;
+    RowDesc* h_desc;
+    int* h_ids;
+    int* h_out_map;
+};
+
+struct Outputs {
+    uint16_t* logits;
+    uint16_t* hidden;
+    unsigned long long* keys;
+    int* result;
+    int* h_result;
+    int n;
+};
+
+}  // namespace plamo
+
+using namespace plamo;
+
+struct plamo_runtime {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    Config c;
+    int context = 0, chunk = 16, local_cap = 0;
+    bool packed = false;
+    std::string name;
+    uint8_t* arena = nullptr;
+    size_t arena_bytes = 0, weight_bytes = 0;
+    const uint16_t* embed = nullptr;
+    const uint16_t* final_norm = nullptr;
+    Linear head;
+    std::vector<Layer> layers;
+    uint32_t *rope_local = nullptr, *rope_global = nullptr;
+    Work work{};
+    Outputs out{};
+    CacheView cache;
+    int* chain_hist = nullptr;
+    int* chain_count = nullptr;
+    int chain_cap = 0;
+    int position = 0, last_rows = 0, last_result = -1;
+    double gpu_seconds = 0, bcast_seconds = 0;
+    size_t device_bytes = 0;
+    cudaEvent_t e0 = nullptr, e1 = nullptr;
+    cudaGraphExec_t graph = nullptr;
+    int step_launches = 0;
+    std::vector<void*> allocs, host_allocs;
+
+    template <typename T>
+    int dalloc(T*& p, size_t count) {
+        void* q = nullptr;
+        const size_t bytes = std::max<size_t>(count * sizeof(T), 256);
+        cudaError_t e = cudaMalloc(&q, bytes);
+        if (e != cudaSuccess) return fail("Cannot allocate " + std::to_string(bytes) + " device bytes");
+        allocs.push_back(q);
+        device_bytes += bytes;
+        p = static_cast<T*>(q);
+        return 0;
+    }
+    template <typename T>
+    int halloc(T*& p, size_t count) {
+        void* q = nullptr;
+        if (cudaMallocHost(&q, std::max<size_t>(count * sizeof(T), 64)) != cudaSuccess) return fail("Cannot allocate pinned memory");
+        host_allocs.push_back(q);
+        p = static_cast<T*>(q);
+        return 0;
+    }
+    ~plamo_runtime() {
+        if (graph) cudaGraphExecDestroy(graph);
+        for (void* p : allocs) cudaFree(p);
+        for (void* p : host_allocs) cudaFreeHost(p);
+        if (e0) cudaEventDestroy(e0);
+        if (e1) cudaEventDestroy(e1);
+        if (stream) cudaStreamDestroy(stream);
+    }
+};
+
+struct plamo_batch {
+    plamo_runtime* rt = nullptr;
+    int lanes = 0;
+    CacheView cache;
+    Work work{};
+    Outputs out{};
+    std::vector<int> positions;
+    bool ready = false;
+    double gpu_seconds = 0;
+    std::vector<void*> allocs, host_allocs;
+    ~plamo_batch() {
+        for (void* p : allocs) cudaFree(p);
+        for (void* p : host_allocs) cudaFreeHost(p);
+    }
+};
+
+namespace plamo {
+
+// ------------------------------------------------------------------------------------------------
+// allocation helpers shared by runtime and batch
+
+template <typename Owner, typename T>
+static int dev_alloc(Owner& o, plamo_runtime& rt, T*& p, size_t count) {
+    void* q = nullptr;
+    const size_t bytes = std::max<size_t>(count * sizeof(T), 256);
+    if (cudaMalloc(&q, bytes) != cudaSuccess) return fail("Cannot allocate " + std::to_string(bytes) + " device bytes");
+    o.allocs.push_back(q);
+    rt.device_bytes += bytes;
+    p = static_cast<T*>(q);
+    return 0;
+}
+template <typename Owner, typename T>
+static int pin_alloc(Owner& o, T*& p, size_t count) {
+    void* q = nullptr;
+    if (cudaMallocHost(&q, std::max<size_t>(count * sizeof(T), 64)) != cudaSuccess) return fail("Cannot allocate pinned memory");
+    o.host_allocs.push_back(q);
+    p = static_cast<T*>(q);
+    return 0;
+}
+
+template <typename Owner>
+static int alloc_work(Owner& o, plamo_runtime& rt, Work& w, int rows) {
+    const Config& c = rt.c;
+    const size_t R = size_t(rows);
+    int max_splits = 1;
+    for (const Layer& L : rt.layers) max_splits = std::max(max_splits, L.splits);
+    w.rows_cap = rows;
+    if (dev_alloc(o, rt, w.x, R * c.d) || dev_alloc(o, rt, w.h, R * c.d) || dev_alloc(o, rt, w.qkv, R * c.qkv_rows()) ||
+        dev_alloc(o, rt, w.q, R * c.q_dim()) || dev_alloc(o, rt, w.att, R * c.q_dim()) || dev_alloc(o, rt, w.proj, R * c.d) ||
+        dev_alloc(o, rt, w.act, R * c.ffn) || dev_alloc(o, rt, w.geo, R) || dev_alloc(o, rt, w.desc, R) ||
+        dev_alloc(o, rt, w.ids, R) || dev_alloc(o, rt, w.out_map, R) ||
+        dev_alloc(o, rt, w.part_o, R * max_splits * c.heads * 128) || dev_alloc(o, rt, w.part_ml, R * max_splits * c.heads) ||
+        pin_alloc(o, w.h_desc, R) || pin_alloc(o, w.h_ids, R) || pin_alloc(o, w.h_out_map, R))
+        return 1;
+    return 0;
+}
+
+template <typename Owner>
+static int alloc_outputs(Owner& o, plamo_runtime& rt, Outputs& out, int n) {
+    out.n = n;
+    if (dev_alloc(o, rt, out.logits, size_t(n) * rt.c.vocab) || dev_alloc(o, rt, out.hidden, size_t(n) * rt.c.d) ||
+        dev_alloc(o, rt, out.keys, size_t(n)) || dev_alloc(o, rt, out.result, size_t(n)) || pin_alloc(o, out.h_result, size_t(n)))
+        return 1;
+    CK(cudaMemset(out.logits, 0, size_t(n) * rt.c.vocab * 2));
+    CK(cudaMemset(out.hidden, 0, size_t(n) * rt.c.d * 2));
+    CK(cudaMemset(out.result, 0, size_t(n) * 4));
+    return 0;
+}
+
+// ------------------------------------------------------------------------------------------------
+// RoPE tables (Kernels.metal:212-219 and :264-267): cos/sin evaluated in double on the fp32 angle,
+// rounded once to fp32 and then to bf16 (the CPU restatement builds the same tables).
+static void build_rope(const Config& c, const float* inv_local, const float* inv_full, int local_rows, int context,
+                       std::vector<uint32_t>& local, std::vector<uint32_t>& global) {
+    local.resize(size_t(local_rows) * 64);
+    for (int p = 0; p < local_rows; p++)
+        for (int i = 0; i < 64; i++) {
+            const float phase = float(p) * inv_local[i];
+            const uint16_t cb = bits_of(float(std::cos(double(phase)))), sb = bits_of(float(std::sin(double(phase))));
+            local[size_t(p) * 64 + i] = uint32_t(cb) | (uint32_t(sb) << 16);
+        }
+    global.resize(size_t(context) * 64);
+    const float mscale = 1.5545177444479562f;
+    for (int p = 0; p < context; p++)
+        for (int i = 0; i < 64; i++) {
+            const float angle = float(p) * inv_full[i];
+            const float cr = from_bits(bits_of(float(std::cos(double(angle)))));
+            const float sr = from_bits(bits_of(float(std::sin(double(angle)))));
+            const uint16_t cb = bits_of(cr * mscale), sb = bits_of(sr * mscale);
+            global[size_t(p) * 64 + i] = uint32_t(cb) | (uint32_t(sb) << 16);
+        }
+    (void)c;
+}
+
+// ------------------------------------------------------------------------------------------------
+// Optional per-launch timing (plamo_profile_decode): every launch is bracketed by two events and its
+// device time is attributed to a kernel class.
+enum KClass { K_GEMV = 0, K_QKV = 1, K_ATTN = 2, K_NORM = 3, K_HEAD = 4, K_CLASSES = 5 };
+struct Profiler {
+    bool on = false;
+    std::vector<cudaEvent_t> ev;
+    std::vector<int> cls;
+    size_t used = 0;
+    int launches = 0;
+};
+static thread_local Profiler* g_prof = nullptr;
+static thread_local int g_launches = 0;
+
+static int prof_begin(cudaStream_t s) {
+    g_launches++;
+    if (!g_prof || !g_prof->on) return 0;
+    if (g_prof->used + 2 > g_prof->ev.size()) {
+        for (int i = 0; i < 64; i++) {
+            cudaEvent_t e;
+            if (cudaEventCreate(&e) != cudaSuccess) return fail("Cannot create profiling events");
+            g_prof->ev.push_back(e);
+        }
+    }
+    CK(cudaEventRecord(g_prof->ev[g_prof->used], s));
+    return 0;
+}
+static int prof_end(cudaStream_t s, int cls) {
+    if (!g_prof || !g_prof->on) return 0;
+    CK(cudaEventRecord(g_prof->ev[g_prof->used + 1], s));
+    g_prof->cls.push_back(cls);
+    g_prof->used += 2;
+    return 0;
+}
+#define LAUNCH(cls, call)                      \
+    do {                                       \
+        if (prof_begin(s)) return 1;           \
+        CK(call);                              \
+        if (prof_end(s, cls)) return 1;        \
+    } while (0)
+
+// ------------------------------------------------------------------------------------------------
+// One decoder pass over `rows` rows whose ids / descriptors / output map are already on the device.
+// out_mode: 0 = no head, 1 = head on the last row only (Runtime.swift:453-458), 2 = head on every
+// row (Batch.swift:163-165). chain: also feed the argmax back as the next step's input id and
+// advance the row descriptors (device-chained decode).
+static int enqueue_forward(plamo_runtime& rt, Work& w, int rows, const CacheView& cv, int out_mode, Outputs& o,
+                           bool chain) {
+    const Config& c = rt.c;
+    cudaStream_t s = rt.stream;
+    const int nout = out_mode == 2 ? rows : (out_mode == 1 ? 1 : 0);
+    LAUNCH(K_NORM, launch_embed_norm(w.ids, rows, c.vocab, rt.embed, rt.layers[0].pre_mixer, c.d, w.x, w.h, nout ? o.keys : nullptr,
+                                     w.out_map, nout, s));
+    const float post_mlp_offset = float(1.0 / std::pow(5.0, 1.5));  // Runtime.swift:450
+    for (int l = 0; l < c.layers; l++) {
+        const Layer& L = rt.layers[l];
+        GemvArgs g;
+        g.lin = L.qkv; g.x = w.h; g.rows = rows; g.y = w.qkv; g.ystride = c.qkv_rows();
+        LAUNCH(K_GEMV, launch_gemv(g, GEMV_PLAIN, s));
+        QkvArgs q;
+        q.qkv = w.qkv; q.q_norm = L.q_norm; q.k_norm = L.k_norm; q.q = w.q; q.keys = cv.keys[l]; q.values = cv.values[l];
+        q.desc = w.desc; q.geo = w.geo; q.rope_local = rt.rope_local; q.rope_global = rt.rope_global;
+        q.lane_stride = cv.stride[l]; q.rows = rows; q.H = c.heads; q.KV = c.kv_heads; q.cap = L.cap; q.W = c.window;
+        q.full = L.full;
+        LAUNCH(K_QKV, launch_qkv(q, s));
+        AttnArgs a;
+        a.q = w.q; a.keys = cv.keys[l]; a.values = cv.values[l]; a.desc = w.desc; a.geo = w.geo; a.rope_local = rt.rope_local;
+        a.part_o = w.part_o; a.part_ml = w.part_ml; a.out = w.att; a.lane_stride = cv.stride[l]; a.rows = rows;
+        a.H = c.heads; a.KV = c.kv_heads; a.cap = L.cap; a.full = L.full; a.splits = L.splits; a.per_max = L.per_max;
+        LAUNCH(K_ATTN, launch_attention(a, s));
+        g = GemvArgs();
+        g.lin = L.o; g.x = w.att; g.rows = rows; g.y = w.proj; g.ystride = c.d;
+        LAUNCH(K_GEMV, launch_gemv(g, GEMV_PLAIN, s));
+        NormArgs n;
+        n.w = L.post_mixer; n.src = w.proj; n.x = w.x; n.next_w = L.pre_mlp; n.next = w.h; n.rows = rows; n.n = c.d;
+        n.offset = 0.2f; n.residual = 1;
+        LAUNCH(K_NORM, launch_norm(n, s));
+        g = GemvArgs();
+        g.lin = L.gate_up; g.x = w.h; g.rows = rows; g.y = w.act; g.ystride = c.ffn;
+        LAUNCH(K_GEMV, launch_gemv(g, GEMV_SWIGLU, s));
+        g = GemvArgs();
+        g.lin = L.down; g.x = w.act; g.rows = rows; g.y = w.proj; g.ystride = c.d;
+        LAUNCH(K_GEMV, launch_gemv(g, GEMV_PLAIN, s));
+        n = NormArgs();
+        n.w = L.post_mlp; n.src = w.proj; n.x = w.x; n.rows = rows; n.n = c.d; n.offset = post_mlp_offset; n.residual = 1;
+        if (l + 1 < c.layers) { n.next_w = rt.layers[l + 1].pre_mixer; n.next = w.h; }
+        LAUNCH(K_NORM, launch_norm(n, s));
+    }
+    if (!nout) return 0;
+    NormArgs n;
+    n.w = rt.final_norm; n.src = w.x + size_t(rows - nout) * c.d; n.x = w.h; n.y2 = o.hidden; n.out_map = w.out_map;
+    n.rows = nout; n.n = c.d; n.offset = 1.0f; n.residual = 0;
+    LAUNCH(K_NORM, launch_norm(n, s));
+    GemvArgs g;
+    g.lin = rt.head; g.x = w.h; g.rows = nout; g.y = o.logits; g.ystride = c.vocab; g.out_map = w.out_map; g.keys = o.keys;
+    LAUNCH(K_GEMV, launch_gemv(g, GEMV_LOGITS, s));
+    LAUNCH(K_HEAD, launch_finalize(o.keys, w.out_map, nout, o.result, chain ? w.ids : nullptr, chain ? w.desc : nullptr,
+                                   chain ? rt.chain_hist : nullptr, chain ? rt.chain_count : nullptr, rt.chain_cap, s));
+    return 0;
+}
+
+static int upload_inputs(plamo_runtime& rt, Work& w, int rows) {
+    CK(cudaMemcpyAsync(w.ids, w.h_ids, sizeof(int) * rows, cudaMemcpyHostToDevice, rt.stream));
+    CK(cudaMemcpyAsync(w.desc, w.h_desc, sizeof(RowDesc) * rows, cudaMemcpyHostToDevice, rt.stream));
+    CK(cudaMemcpyAsync(w.out_map, w.h_out_map, sizeof(int) * rows, cudaMemcpyHostToDevice, rt.stream));
+    return 0;
+}
+
+static int finish(plamo_runtime& rt, double* seconds) {
+    CK(cudaEventRecord(rt.e1, rt.stream));
+    cudaError_t e = cudaStreamSynchronize(rt.stream);
+    if (e != cudaSuccess) return fail(std::string("CUDA execution failed: ") + cudaGetErrorString(e));
+    float ms = 0;
+    CK(cudaEventElapsedTime(&ms, rt.e0, rt.e1));
+    *seconds += ms * 1e-3;
+    return 0;
+}
+
+static int capture_decode_graph(plamo_runtime& rt) {
+    cudaGraph_t g = nullptr;
+    CK(cudaStreamBeginCapture(rt.stream, cudaStreamCaptureModeThreadLocal));
+    g_launches = 0;
+    const int rc = enqueue_forward(rt, rt.work, 1, rt.cache, 1, rt.out, true);
+    rt.step_launches = g_launches;
+    cudaError_t e = cudaStreamEndCapture(rt.stream, &g);
+    if (rc) { if (g) cudaGraphDestroy(g); return rc; }
+    if (e != cudaSuccess) return fail(std::string("CUDA graph capture failed: ") + cudaGetErrorString(e));
+    e = cudaGraphInstantiate(&rt.graph, g, 0);
+    cudaGraphDestroy(g);
+    if (e != cudaSuccess) { rt.graph = nullptr; return fail(std::string("CUDA graph instantiate failed: ") + cudaGetErrorString(e)); }
+    return 0;
+}
+
+// Runtime.encode (Runtime.swift:327-467) for the scalar cache.
+static int forward_impl(plamo_runtime& rt, const int32_t* ids, int n, bool output, int32_t* next) {
+    if (n < 1 || n > rt.chunk || rt.position + n > rt.context) return fail("Invalid tokens or context exhausted");
+    for (int i = 0; i < n; i++)
+        if (ids[i] < 0 || ids[i] >= rt.c.vocab) return fail("Invalid tokens or context exhausted");
+    Work& w = rt.work;
+    for (int i = 0; i < n; i++) {
+        w.h_ids[i] = ids[i];
+        w.h_desc[i] = RowDesc{rt.position + i, 0, rt.position, n};
+        w.h_out_map[i] = 0;
+    }
+    if (upload_inputs(rt, w, n)) return 1;
+    CK(cudaEventRecord(rt.e0, rt.stream));
+    if (n == 1 && output) {
+        if (!rt.graph && capture_decode_graph(rt)) return 1;
+        CK(cudaGraphLaunch(rt.graph, rt.stream));
+    } else {
+        if (enqueue_forward(rt, w, n, rt.cache, output ? 1 : 0, rt.out, false)) return 1;
+    }
+    if (output) CK(cudaMemcpyAsync(rt.out.h_result, rt.out.result, sizeof(int), cudaMemcpyDeviceToHost, rt.stream));
+    if (finish(rt, &rt.gpu_seconds)) return 1;
+    rt.position += n;
+    rt.last_rows = output ? 1 : 0;
+    if (output) rt.last_result = rt.out.h_result[0];
+    if (next) *next = output ? rt.out.h_result[0] : -1;
+    return 0;
+}
+
+}  // namespace plamo
+
+// ================================================================================================
+// C ABI
+
+extern "C" {
+
+const char* plamo_last_error(void) { return plamo::g_error.c_str(); }
+
+static int setup_runtime(plamo_runtime* rt, const ModelFiles* mf, bool upload, size_t* arena_out);
+
+static int open_common(const char* model_dir, int context, int packed, int device, plamo_runtime** out,
+                       const void* nccl_id, int rank, int world);
+
+int plamo_open(const char* model_dir, int context, int packed, int device, plamo_runtime** out) {
+    return open_common(model_dir, context, packed, device, out, nullptr, 0, 1);
+}
+
+int plamo_open_broadcast(const char* model_dir, int context, int packed, int device, const void* nccl_id, int rank,
+                         int world, plamo_runtime** out) {
+    if (!nccl_id || world < 1 || rank < 0 || rank >= world) return fail("Invalid broadcast arguments");
+    return open_common(model_dir, context, packed, device, out, nccl_id, rank, world);
+}
+
+// --- NCCL loaded on demand (no link-time dependency; reuses an already loaded libnccl) --------
+typedef struct { char internal[128]; } nccl_uid;
+typedef int (*nccl_get_uid_fn)(nccl_uid*);
+typedef int (*nccl_init_rank_fn)(void**, int, nccl_uid, int);
+typedef int (*nccl_bcast_fn)(const void*, void*, size_t, int, int, void*, cudaStream_t);
+typedef int (*nccl_destroy_fn)(void*);
+typedef const char* (*nccl_err_fn)(int);
+struct NcclApi {
+    void* h = nullptr;
+    nccl_get_uid_fn get_uid = nullptr;
+    nccl_init_rank_fn init_rank = nullptr;
+    nccl_bcast_fn bcast = nullptr;
+    nccl_destroy_fn destroy = nullptr;
+    nccl_err_fn err = nullptr;
+};
+static bool nccl_api(NcclApi& api) {
+    static NcclApi cached;
+    static bool tried = false;
+    if (!tried) {
+        tried = true;
+        void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+        if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+        if (h) {
+            cached.h = h;
+            cached.get_uid = (nccl_get_uid_fn)dlsym(h, "ncclGetUniqueId");
+            cached.init_rank = (nccl_init_rank_fn)dlsym(h, "ncclCommInitRank");
+            cached.bcast = (nccl_bcast_fn)dlsym(h, "ncclBroadcast");
+            cached.destroy = (nccl_destroy_fn)dlsym(h, "ncclCommDestroy");
+            cached.err = (nccl_err_fn)dlsym(h, "ncclGetErrorString");
+        }
+    }
+    api = cached;
+    return api.h && api.get_uid && api.init_rank && api.bcast && api.destroy;
+}
+
+int plamo_nccl_unique_id(void* out) {
+    NcclApi api;
+    if (!out || !nccl_api(api)) return fail("NCCL is not available");
+    nccl_uid id;
+    int e = api.get_uid(&id);
+    if (e) return fail(std::string("ncclGetUniqueId failed: ") + (api.err ? api.err(e) : "?"));
+    memcpy(out, &id, sizeof(id));
+    return 0;
+}
+
+static int open_common(const char* model_dir, int context, int packed, int device, plamo_runtime** out,
+                       const void* nccl_id, int rank, int world) {
+    if (!out) return fail("Invalid output handle");
+    *out = nullptr;
+    if (context < 1 || context > 32768) return fail("Context must be 1...32768");
+    int count = 0;
+    if (cudaGetDeviceCount(&count) != cudaSuccess || device < 0 || device >= count) return fail("A CUDA device is required");
+    CK(cudaSetDevice(device));
+    cudaDeviceProp prop;
+    CK(cudaGetDeviceProperties(&prop, device));
+    if (prop.major < 10) return fail("libplamo_cuda requires an sm_100a (B200-class) device");
+    auto* mf = new ModelFiles();
+    std::string err;
+    if (!mf->load(model_dir ? model_dir : "", packed != 0, err)) { delete mf; return fail(err); }
+    auto* rt = new plamo_runtime();
+    rt->device = device;
+    rt->name = prop.name;
+    rt->c = mf->cfg;
+    rt->context = context;
+    rt->packed = packed != 0;
+    rt->chunk = std::min(context, 16);                                   // Runtime.swift:173
+    rt->local_cap = std::min(context, rt->c.window + rt->chunk);         // Runtime.swift:240
+    int rc = configure_kernels() == cudaSuccess ? 0 : fail("Cannot configure kernels");
+    if (!rc && (cudaStreamCreateWithFlags(&rt->stream, cudaStreamNonBlocking) != cudaSuccess ||
+                cudaEventCreate(&rt->e0) != cudaSuccess || cudaEventCreate(&rt->e1) != cudaSuccess))
+        rc = fail("Cannot create CUDA stream");
+    size_t arena = 0;
+    if (!rc) rc = setup_runtime(rt, mf, nccl_id == nullptr || rank == 0, &arena);
+    if (!rc && nccl_id) {
+        NcclApi api;
+        if (!nccl_api(api)) rc = fail("NCCL is not available");
+        void* comm = nullptr;
+        if (!rc) {
+            nccl_uid id;
+            memcpy(&id, nccl_id, sizeof(id));
+            int e = api.init_rank(&comm, world, id, rank);
+            if (e) rc = fail(std::string("ncclCommInitRank failed: ") + (api.err ? api.err(e) : "?"));
+        }
+        if (!rc) {
+            auto t0 = std::chrono::steady_clock::now();
+            int e = api.bcast(rt->arena, rt->arena, rt->arena_bytes, /*ncclUint8*/ 1, 0, comm, rt->stream);
+            if (e) rc = fail(std::string("ncclBroadcast failed: ") + (api.err ? api.err(e) : "?"));
+            if (!rc && cudaStreamSynchronize(rt->stream) != cudaSuccess) rc = fail("weight broadcast failed");
+            rt->bcast_seconds = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+        }
+        if (comm) api.destroy(comm);
+    }
+    delete mf;  // weights are resident; the mappings are no longer needed
+    if (rc) { delete rt; return rc; }
+    *out = rt;
+    return 0;
+}
+
+// Builds the weight arena (uploading it unless another rank will broadcast it), KV caches, RoPE
+// tables and work buffers.
+static int setup_runtime(plamo_runtime* rt, const ModelFiles* mf, bool upload, size_t* arena_out) {
+    const Config& c = rt->c;
+    std::string err;
+    struct Item { std::string name; std::vector<long long> shape; bool p12; TensorRef ref; size_t off; };
+    std::vector<Item> items;
+    auto add = [&](const std::string& name, std::vector<long long> shape, bool p12) { items.push_back({name, shape, p12, {}, 0}); };
+    const long long d = c.d, V = c.vocab;
+    add("model.embed_tokens.weight", {V, d}, false);
+    add("lm_head.weight", {V, d}, rt->packed);
+    add("model.norm.weight", {d}, rt->packed);
+    for (int i = 0; i < c.layers; i++) {
+        const std::string p = "model.layers.layers." + std::to_string(i) + ".";
+        add(p + "pre_mixer_norm.weight", {d}, rt->packed);
+        add(p + "post_mixer_norm.weight", {d}, rt->packed);
+        add(p + "pre_mlp_norm.weight", {d}, rt->packed);
+        add(p + "post_mlp_norm.weight", {d}, rt->packed);
+        add(p + "mixer.qkv_proj.weight", {c.qkv_rows(), d}, rt->packed);
+        add(p + "mixer.o_proj.weight", {d, c.q_dim()}, rt->packed);
+        add(p + "mixer.q_norm.weight", {128}, rt->packed);
+        add(p + "mixer.k_norm.weight", {128}, rt->packed);
+        add(p + "mlp.gate_up_proj.weight", {2LL * c.ffn, d}, rt->packed);
+        add(p + "mlp.down_proj.weight", {d, c.ffn}, rt->packed);
+    }
+    for (auto& it : items)
+        if (!mf->tensor(it.name, it.shape, it.p12, it.ref, err)) return fail(err);
+    // Arena layout: raw tensors each 256-byte aligned; in packed mode the whole .p12 payload (its
+    // regions are already 64-byte aligned) followed by the bf16 input embedding.
+    size_t off = 0;
+    size_t payload_off = 0;
+    if (rt->packed) { payload_off = 0; off = (mf->p12_payload + 255) & ~size_t(255); }
+    for (auto& it : items) {
+        if (it.p12) continue;
+        it.off = off;
+        off += (it.ref.bytes + 255) & ~size_t(255);
+    }
+    rt->arena_bytes = off;
+    if (rt->dalloc(rt->arena, off)) return 1;
+    if (upload) {
+        // staged through a pinned buffer (pageable copies of mmapped files are slow)
+        const size_t stage_bytes = size_t(64) << 20;
+        uint8_t* stage = nullptr;
+        if (cudaMallocHost(&stage, stage_bytes) != cudaSuccess) return fail("Cannot allocate pinned staging");
+        auto copy = [&](size_t dst, const uint8_t* src, size_t bytes) -> int {
+            for (size_t done = 0; done < bytes; done += stage_bytes) {
+                const size_t n = std::min(stage_bytes, bytes - done);
+                memcpy(stage, src + done, n);
+                if (cudaMemcpy(rt->arena + dst + done, stage, n, cudaMemcpyHostToDevice) != cudaSuccess) return 1;
+            }
+            return 0;
+        };
+        int bad = 0;
+        if (rt->packed) bad |= copy(payload_off, mf->p12.data + mf->p12_data_start, mf->p12_payload);
+        for (auto& it : items)
+            if (!it.p12) bad |= copy(it.off, it.ref.data, it.ref.bytes);
+        cudaFreeHost(stage);
+        if (bad) return fail("Weight upload failed");
+    }
+    *arena_out = off;
+    rt->weight_bytes = off;
+    auto ptr = [&](const Item& it) -> const uint8_t* {
+        if (!it.p12) return rt->arena + it.off;
+        if (it.ref.packed) return rt->arena + payload_off + it.ref.data_off;
+        return rt->arena + payload_off + it.ref.raw_off;
+    };
+    auto lin = [&](const Item& it, int M, int K) {
+        Linear l;
+        l.M = M; l.K = K;
+        l.w = ptr(it);
+        l.offsets = it.p12 ? reinterpret_cast<const uint32_t*>(rt->arena + payload_off + it.ref.table_off) : nullptr;
+        return l;
+    };
+    size_t k = 0;
+    rt->embed = reinterpret_cast<const uint16_t*>(ptr(items[k++]));
+    rt->head = lin(items[k++], c.vocab, c.d);
+    rt->final_norm = reinterpret_cast<const uint16_t*>(ptr(items[k++]));
+    rt->layers.resize(c.layers);
+    int max_splits = 1;
+    for (int i = 0; i < c.layers; i++) {
+        Layer& L = rt->layers[i];
+        L.pre_mixer = reinterpret_cast<const uint16_t*>(ptr(items[k++]));
+        L.post_mixer = reinterpret_cast<const uint16_t*>(ptr(items[k++]));
+        L.pre_mlp = reinterpret_cast<const uint16_t*>(ptr(items[k++]));
+        L.post_mlp = reinterpret_cast<const uint16_t*>(ptr(items[k++]));
+        L.qkv = lin(items[k++], c.qkv_rows(), c.d);
+        L.o = lin(items[k++], c.d, c.q_dim());
+        L.q_norm = reinterpret_cast<const uint16_t*>(ptr(items[k++]));
+        L.k_norm = reinterpret_cast<const uint16_t*>(ptr(items[k++]));
+        L.gate_up = lin(items[k++], 2 * c.ffn, c.d);
+        L.down = lin(items[k++], c.d, c.ffn);
+        L.full = c.is_global(i);
+        L.cap = L.full ? rt->context : rt->local_cap;  // Runtime.swift:240
+        // split-K width: ~64 keys per split for the local window, <= 256 keys for global history
+        L.splits = L.full ? std::max(32, (L.cap + 255) / 256) : std::max(1, std::min(32, (L.cap + 63) / 64));
+        L.per_max = attention_per_max(L.cap, L.splits);
+        max_splits = std::max(max_splits, L.splits);
+        const size_t n = size_t(L.cap) * c.kv_heads * 128;
+        if (rt->dalloc(L.keys, n) || rt->dalloc(L.values, n)) return 1;
+        CK(cudaMemset(L.keys, 0, n * 2));
+        CK(cudaMemset(L.values, 0, n * 2));
+        rt->cache.keys.push_back(L.keys);
+        rt->cache.values.push_back(L.values);
+        rt->cache.stride.push_back(0);
+    }
+    std::vector<uint32_t> lo, gl;
+    const int local_rows = std::min(rt->context, c.window + 16);  // Runtime.swift:266
+    build_rope(c, mf->inv_local, mf->inv_full, local_rows, rt->context, lo, gl);
+    if (rt->dalloc(rt->rope_local, lo.size()) || rt->dalloc(rt->rope_global, gl.size())) return 1;
+    CK(cudaMemcpy(rt->rope_local, lo.data(), lo.size() * 4, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(rt->rope_global, gl.data(), gl.size() * 4, cudaMemcpyHostToDevice));
+    if (alloc_work(*rt, *rt, rt->work, 16) || alloc_outputs(*rt, *rt, rt->out, 1)) return 1;
+    rt->chain_cap = rt->context;
+    if (rt->dalloc(rt->chain_hist, size_t(rt->chain_cap)) || rt->dalloc(rt->chain_count, 1)) return 1;
+    return 0;
+}
+
+void plamo_close(plamo_runtime* rt) {
+    if (!rt) return;
+    cudaSetDevice(rt->device);
+    if (rt->stream) cudaStreamSynchronize(rt->stream);
+    delete rt;
+}
+
+int plamo_forward(plamo_runtime* rt, const int32_t* ids, int n, int output, int32_t* next_id) {
+    if (!rt || (!ids && n)) return fail("Invalid tokens or context exhausted");
+    CK(cudaSetDevice(rt->device));
+    return forward_impl(*rt, ids, n, output != 0, next_id);
+}
+
+int plamo_prefill(plamo_runtime* rt, const int32_t* ids, int n, int32_t* next_id) {
+    if (!rt || !ids || n < 1 || rt->position + n > rt->context) return fail("Input exceeds context");  // Runtime.swift:474
+    CK(cudaSetDevice(rt->device));
+    int32_t next = -1;
+    for (int start = 0; start < n; start += rt->chunk) {  // Runtime.swift:476-479
+        const int end = std::min(start + rt->chunk, n);
+        if (forward_impl(*rt, ids + start, end - start, end == n, &next)) return 1;
+    }
+    if (next_id) *next_id = next;
+    return 0;
+}
+
+int plamo_decode_chain(plamo_runtime* rt, int steps, int32_t* out_ids) {
+    if (!rt || steps < 1 || !out_ids) return fail("Invalid decode chain arguments");
+    if (rt->last_rows < 1 || rt->last_result < 0 || rt->last_result >= rt->c.vocab || rt->position + steps > rt->context)
+        return fail("Invalid tokens or context exhausted");
+    CK(cudaSetDevice(rt->device));
+    Work& w = rt->work;
+    w.h_ids[0] = rt->last_result;
+    w.h_desc[0] = RowDesc{rt->position, 0, rt->position, 1};
+    w.h_out_map[0] = 0;
+    if (upload_inputs(*rt, w, 1)) return 1;
+    CK(cudaMemsetAsync(rt->chain_count, 0, sizeof(int), rt->stream));
+    if (!rt->graph && capture_decode_graph(*rt)) return 1;
+    CK(cudaEventRecord(rt->e0, rt->stream));
+    for (int i = 0; i < steps; i++) CK(cudaGraphLaunch(rt->graph, rt->stream));
+    CK(cudaMemcpyAsync(out_ids, rt->chain_hist, sizeof(int) * steps, cudaMemcpyDeviceToHost, rt->stream));
+    if (finish(*rt, &rt->gpu_seconds)) return 1;
+    rt->position += steps;
+    rt->last_rows = 1;
+    rt->last_result = out_ids[steps - 1];
+    rt->out.h_result[0] = rt->last_result;
+    return 0;
+}
+
+int plamo_step_launches(plamo_runtime* rt) {
+    if (!rt) return 0;
+    cudaSetDevice(rt->device);
+    if (!rt->graph && capture_decode_graph(*rt)) return -1;
+    return rt->step_launches;
+}
+
+// Runs `steps` batch-1 decode steps (same kernels as the decode graph, launched directly) with
+// every launch bracketed by CUDA events; class_ms[c] / launches[c] receive the summed device time
+// and launch count per kernel class (0 GEMV, 1 QK-norm/RoPE/KV, 2 attention, 3 norms, 4 argmax).
+int plamo_profile_decode(plamo_runtime* rt, int steps, double* class_ms, int32_t* launches) {
+    if (!rt || steps < 1 || !class_ms || !launches) return fail("Invalid profile arguments");
+    if (rt->last_rows < 1 || rt->position + steps > rt->context) return fail("Invalid tokens or context exhausted");
+    CK(cudaSetDevice(rt->device));
+    Work& w = rt->work;
+    w.h_ids[0] = rt->last_result;
+    w.h_desc[0] = RowDesc{rt->position, 0, rt->position, 1};
+    w.h_out_map[0] = 0;
+    if (upload_inputs(*rt, w, 1)) return 1;
+    CK(cudaMemsetAsync(rt->chain_count, 0, sizeof(int), rt->stream));
+    Profiler prof;
+    prof.on = true;
+    g_prof = &prof;
+    int rc = 0;
+    for (int i = 0; i < steps && !rc; i++) rc = enqueue_forward(*rt, w, 1, rt->cache, 1, rt->out, true);
+    g_prof = nullptr;
+    if (!rc && cudaStreamSynchronize(rt->stream) != cudaSuccess) rc = fail("CUDA execution failed");
+    for (int c = 0; c < K_CLASSES; c++) { class_ms[c] = 0; launches[c] = 0; }
+    for (size_t i = 0; !rc && i < prof.cls.size(); i++) {
+        float ms = 0;
+        cudaEventElapsedTime(&ms, prof.ev[2 * i], prof.ev[2 * i + 1]);
+        class_ms[prof.cls[i]] += ms;
+        launches[prof.cls[i]] += 1;
+    }
+    for (cudaEvent_t e : prof.ev) cudaEventDestroy(e);
+    if (rc) return rc;
+    int last = 0;
+    CK(cudaMemcpy(&last, rt->chain_hist + (steps - 1), sizeof(int), cudaMemcpyDeviceToHost));
+    rt->position += steps;
+    rt->last_result = last;
+    return 0;
+}
+
+int plamo_logits(plamo_runtime* rt, int slot, float* out) {
+    if (!rt || !out || slot < 0 || slot >= std::max(1, rt->last_rows)) return fail("Invalid logits slot");
+    CK(cudaSetDevice(rt->device));
+    std::vector<uint16_t> tmp(rt->c.vocab);
+    CK(cudaMemcpy(tmp.data(), rt->out.logits + size_t(slot) * rt->c.vocab, tmp.size() * 2, cudaMemcpyDeviceToHost));
+    for (int i = 0; i < rt->c.vocab; i++) out[i] = from_bits(tmp[i]);
+    return 0;
+}
+
+int plamo_hidden(plamo_runtime* rt, float* out) {
+    if (!rt || !out) return fail("Invalid arguments");
+    CK(cudaSetDevice(rt->device));
+    std::vector<uint16_t> tmp(rt->c.d);
+    CK(cudaMemcpy(tmp.data(), rt->out.hidden, tmp.size() * 2, cudaMemcpyDeviceToHost));
+    for (int i = 0; i < rt->c.d; i++) out[i] = from_bits(tmp[i]);
+    return 0;
+}
+
+void plamo_reset(plamo_runtime* rt) {
+    if (!rt) return;
+    rt->position = 0; rt->gpu_seconds = 0; rt->last_rows = 0;  // Runtime.swift:319
+}
+
+int plamo_position(const plamo_runtime* rt) { return rt ? rt->position : 0; }
+double plamo_gpu_seconds(const plamo_runtime* rt) { return rt ? rt->gpu_seconds : 0; }
+size_t plamo_weight_bytes(const plamo_runtime* rt) { return rt ? rt->weight_bytes : 0; }
+size_t plamo_device_bytes(const plamo_runtime* rt) { return rt ? rt->device_bytes : 0; }
+const char* plamo_device_name(const plamo_runtime* rt) { return rt ? rt->name.c_str() : ""; }
+double plamo_broadcast_seconds(const plamo_runtime* rt) { return rt ? rt->bcast_seconds : 0; }
+
+int plamo_dims(const plamo_runtime* rt, int32_t out[10]) {
+    if (!rt || !out) return fail("Invalid arguments");
+    const Config& c = rt->c;
+    const int32_t v[10] = {c.d, c.layers, c.heads, c.kv_heads, c.head_dim, c.ffn, c.vocab, c.window, c.pattern, rt->context};
+    memcpy(out, v, sizeof(v));
+    return 0;
+}
+
+int plamo_debug_kv(plamo_runtime* rt, int layer, uint16_t* keys, uint16_t* values) {
+    if (!rt || layer < 0 || layer >= rt->c.layers) return fail("Invalid layer");
+    CK(cudaSetDevice(rt->device));
+    const Layer& L = rt->layers[layer];
+    const size_t n = size_t(L.cap) * rt->c.kv_heads * 128 * 2;
+    CK(cudaMemcpy(keys, L.keys, n, cudaMemcpyDeviceToHost));
+    CK(cudaMemcpy(values, L.values, n, cudaMemcpyDeviceToHost));
+    return 0;
+}
+
+// ---- Batch ---------------------------------------------------------------------------------------
+
+int plamo_batch_open(plamo_runtime* rt, int lanes, plamo_batch** out) {
+    if (!rt || !out) return fail("Invalid arguments");
+    *out = nullptr;
+    if (rt->context >= 8192) return fail("Batch requires dense greedy inference with context below 8192");  // Batch.swift:34-35
+    if (lanes < 1 || lanes > 64) return fail("Batch lanes must be 1...64");
+    CK(cudaSetDevice(rt->device));
+    auto* b = new plamo_batch();
+    b->rt = rt;
+    b->lanes = lanes;
+    int rc = 0;
+    for (int i = 0; i < rt->c.layers && !rc; i++) {
+        const Layer& L = rt->layers[i];
+        const long long stride = (long long)L.cap * rt->c.kv_heads * 128;
+        uint16_t *k = nullptr, *v = nullptr;
+        rc = dev_alloc(*b, *rt, k, size_t(stride) * lanes) || dev_alloc(*b, *rt, v, size_t(stride) * lanes);
+        if (!rc) {
+            cudaMemset(k, 0, size_t(stride) * lanes * 2);
+            cudaMemset(v, 0, size_t(stride) * lanes * 2);
+        }
+        b->cache.keys.push_back(k);
+        b->cache.values.push_back(v);
+        b->cache.stride.push_back(stride);
+    }
+    if (!rc) rc = alloc_work(*b, *rt, b->work, std::max(16, lanes));
+    if (!rc) rc = alloc_outputs(*b, *rt, b->out, lanes);
+    if (rc) { delete b; return rc; }
+    *out = b;
+    return 0;
+}
+
+void plamo_batch_close(plamo_batch* b) {
+    if (!b) return;
+    cudaSetDevice(b->rt->device);
+    cudaStreamSynchronize(b->rt->stream);
+    delete b;
+}
+
+void plamo_batch_reset(plamo_batch* b) {
+    if (!b) return;
+    b->ready = false; b->positions.clear(); b->gpu_seconds = 0;  // Batch.swift:182
+}
+
+double plamo_batch_gpu_seconds(const plamo_batch* b) { return b ? b->gpu_seconds : 0; }
+
+int plamo_batch_prefill(plamo_batch* b, const int32_t* const* prompts, const int32_t* lens, int n, int32_t* next_ids) {
+    if (!b || !prompts || !lens) return fail("Expected one to four valid prompts");
+    plamo_runtime& rt = *b->rt;
+    if (n < 1 || n > b->lanes) return fail("Expected one to four valid prompts");  // Batch.swift:81-83
+    for (int l = 0; l < n; l++) {
+        if (!prompts[l] || lens[l] < 1 || lens[l] > rt.context) return fail("Expected one to four valid prompts");
+        for (int i = 0; i < lens[l]; i++)
+            if (prompts[l][i] < 0 || prompts[l][i] >= rt.c.vocab) return fail("Expected one to four valid prompts");
+    }
+    CK(cudaSetDevice(rt.device));
+    b->ready = false;
+    b->gpu_seconds = 0;
+    Work& w = b->work;
+    for (int l = 0; l < n; l++) {
+        // Each prompt is prefilled in 16-token chunks straight into its lane slab (the reference
+        // prefills through the scalar runtime and copies the KV rows, Batch.swift:86-101).
+        for (int start = 0; start < lens[l]; start += rt.chunk) {
+            const int cn = std::min(rt.chunk, lens[l] - start);
+            const bool last = start + cn == lens[l];
+            for (int i = 0; i < cn; i++) {
+                w.h_ids[i] = prompts[l][start + i];
+                w.h_desc[i] = RowDesc{start + i, l, start, cn};
+            }
+            w.h_out_map[0] = l;
+            if (upload_inputs(rt, w, cn)) return 1;
+            CK(cudaEventRecord(rt.e0, rt.stream));
+            if (enqueue_forward(rt, w, cn, b->cache, last ? 1 : 0, b->out, false)) return 1;
+            if (finish(rt, &b->gpu_seconds)) return 1;
+        }
+    }
+    CK(cudaMemcpy(b->out.h_result, b->out.result, sizeof(int) * n, cudaMemcpyDeviceToHost));
+    b->positions.assign(lens, lens + n);
+    b->ready = true;
+    for (int l = 0; l < n; l++) next_ids[l] = b->out.h_result[l];
+    return 0;
+}
+
+int plamo_batch_step(plamo_batch* b, const int32_t* tokens, int n, int32_t* next_ids) {
+    const char* msg = "Invalid quad step or context exhausted";  // Batch.swift:110-112
+    if (!b || !tokens || !b->ready || n != int(b->positions.size())) return fail(msg);
+    plamo_runtime& rt = *b->rt;
+    Work& w = b->work;
+    int rows = 0;
+    for (int l = 0; l < n; l++) {
+        if (tokens[l] < 0) continue;
+        if (tokens[l] >= rt.c.vocab || b->positions[l] >= rt.context) return fail(msg);
+        w.h_ids[rows] = tokens[l];
+        w.h_desc[rows] = RowDesc{b->positions[l], l, b->positions[l], 1};
+        w.h_out_map[rows] = l;
+        rows++;
+    }
+    if (!rows) return fail(msg);
+    CK(cudaSetDevice(rt.device));
+    if (upload_inputs(rt, w, rows)) return 1;
+    CK(cudaEventRecord(rt.e0, rt.stream));
+    if (enqueue_forward(rt, w, rows, b->cache, 2, b->out, false)) { b->ready = false; return 1; }
+    CK(cudaMemcpyAsync(b->out.h_result, b->out.result, sizeof(int) * n, cudaMemcpyDeviceToHost, rt.stream));
+    if (finish(rt, &b->gpu_seconds)) { b->ready = false; return 1; }
+    for (int l = 0; l < n; l++)
+        if (tokens[l] >= 0) b->positions[l] += 1;
+    for (int l = 0; l < n; l++) next_ids[l] = b->out.h_result[l];
+    return 0;
+}
+
+int plamo_batch_logits(plamo_batch* b, int lane, float* out) {
+    if (!b || !out || lane < 0 || lane >= b->lanes) return fail("Invalid lane");
+    CK(cudaSetDevice(b->rt->device));
+    const int V = b->rt->c.vocab;
+    std::vector<uint16_t> tmp(V);
+    CK(cudaMemcpy(tmp.data(), b->out.logits + size_t(lane) * V, size_t(V) * 2, cudaMemcpyDeviceToHost));
+    for (int i = 0; i < V; i++) out[i] = from_bits(tmp[i]);
+    return 0;
+}
+
+int plamo_batch_hidden(plamo_batch* b, int lane, float* out) {
+    if (!b || !out || lane < 0 || lane >= b->lanes) return fail("Invalid lane");
+    CK(cudaSetDevice(b->rt->device));
+    const int d = b->rt->c.d;
+    std::vector<uint16_t> tmp(d);
+    CK(cudaMemcpy(tmp.data(), b->out.hidden + size_t(lane) * d, size_t(d) * 2, cudaMemcpyDeviceToHost));
+    for (int i = 0; i < d; i++) out[i] = from_bits(tmp[i]);
+    return 0;
+}
+
+int plamo_batch_debug_kv(plamo_batch* b, int layer, int lane, uint16_t* keys, uint16_t* values) {
+    if (!b || layer < 0 || layer >= b->rt->c.layers || lane < 0 || lane >= b->lanes) return fail("Invalid layer or lane");
+    CK(cudaSetDevice(b->rt->device));
+    const long long stride = b->cache.stride[layer];
+    CK(cudaMemcpy(keys, b->cache.keys[layer] + size_t(lane) * stride, size_t(stride) * 2, cudaMemcpyDeviceToHost));
+    CK(cudaMemcpy(values, b->cache.values[layer] + size_t(lane) * stride, size_t(stride) * 2, cudaMemcpyDeviceToHost));
+    return 0;
+}
+
+// decodeBatch + Batch.generate (BatchDecode.swift:8-47)
+int plamo_batch_generate(plamo_batch* b, const int32_t* const* prompts, const int32_t* lens, const int32_t* limits, int n,
+                         int stop_on_truncation, int32_t* out_ids, int out_stride, int32_t* out_lens, int32_t* reasons,
+                         int32_t* out_count) {
+    if (!b || !limits || !out_ids || !out_lens || !reasons || !out_count || n < 1 || n > b->lanes)
+        return fail("Quad output budget exceeds context");
+    for (int i = 0; i < n; i++)
+        if (limits[i] < 0 || limits[i] > 8191 || !lens || lens[i] + limits[i] > b->rt->context || limits[i] > out_stride)
+            return fail("Quad output budget exceeds context");
+    std::vector<int32_t> next(n);
+    if (plamo_batch_prefill(b, prompts, lens, n, next.data())) { plamo_batch_reset(b); return 1; }
+    std::vector<int> count(n, 0), reason(n, -1);
+    int last = n - 1;
+    std::vector<int32_t> tokens(n), preds(n);
+    for (;;) {
+        bool pending = false;
+        for (int l = 0; l <= last; l++) pending |= reason[l] < 0;
+        if (!pending) break;
+        bool any = false;
+        for (int l = 0; l < n; l++) {
+            tokens[l] = -1;
+            if (l > last || reason[l] >= 0) continue;
+            if (count[l] == limits[l]) reason[l] = 1;
+            else if (next[l] == 1 || next[l] == 16) reason[l] = 0;
+            else {
+                out_ids[size_t(l) * out_stride + count[l]] = next[l];
+                count[l]++;
+                if (count[l] == limits[l]) reason[l] = 1;
+                else { tokens[l] = next[l]; any = true; }
+            }
+            if (reason[l] == 1 && stop_on_truncation) last = std::min(last, l);
+        }
+        if (!any) break;
+        if (plamo_batch_step(b, tokens.data(), n, preds.data())) { plamo_batch_reset(b); return 1; }
+        for (int l = 0; l < n; l++) next[l] = preds[l];
+    }
+    for (int l = 0; l <= last; l++) { out_lens[l] = count[l]; reasons[l] = reason[l] < 0 ? 1 : reason[l]; }
+    *out_count = last + 1;
+    return 0;
+}
+
+}  // extern "C"
