@@ -324,6 +324,48 @@ class OracleBatch:
 
 
 # ---------------------------------------------------------------------------------------
+# noise floor of the restatement itself
+
+def _reordered(fn):
+    """Runs fn with every projection sum walked backwards and every global-layer attention row
+    through 16-key split-K partitions: the same arithmetic in another fp32 summation order."""
+    L = lib()
+    L.oracle_set_split_partition.argtypes = [ctypes.c_int]
+    L.oracle_set_dot_reverse.argtypes = [ctypes.c_int]
+    L.oracle_set_split_partition(16)
+    L.oracle_set_dot_reverse(1)
+    try:
+        return fn()
+    finally:
+        L.oracle_set_split_partition(0)
+        L.oracle_set_dot_reverse(0)
+
+
+def noise_floor(directory, context: int, prompt, steps: int, model: Model | None = None) -> dict:
+    """Teacher-forced logit differences between the restatement and its reordered twin.
+
+    A model whose activations are rounded to bf16 after every op amplifies fp32 reordering into
+    bf16 rounding flips; this measures how far two correct implementations drift on a given model,
+    which sets the scale for comparing the CUDA path (which sums in yet another order)."""
+    model = model or Model(directory)
+    a = OracleRuntime(directory, context, model=model)
+    b = OracleRuntime(directory, context, model=model)
+    nxt = a.prefill(prompt)
+    _reordered(lambda: b.prefill(prompt))
+    rmse, maxabs = [], []
+    for step in range(steps + 1):
+        e = a.logits() - b.logits()
+        rmse.append(float(np.sqrt(np.mean(e * e))))
+        maxabs.append(float(np.max(np.abs(e))))
+        if step == steps:
+            break
+        tok = nxt
+        nxt = a.forward([tok])
+        _reordered(lambda: b.forward([tok]))
+    return dict(rmse=max(rmse), maxabs=max(maxabs), rmse_mean=float(np.mean(rmse)))
+
+
+# ---------------------------------------------------------------------------------------
 # kernel-level restatements
 
 def linear(w: np.ndarray, x: np.ndarray, logits: bool = False) -> np.ndarray:

@@ -31,6 +31,9 @@
 namespace {
 
 thread_local std::string g_error;
+// When > 0, every attention row uses the split-K path with this partition size. The two paths
+// differ only in fp32 summation order; comparing them measures the restatement's own noise floor.
+int g_split_part = 0;
 
 // ---- bf16 helpers: K:5-10 -------------------------------------------------------------
 inline float bf(uint16_t x) { uint32_t u = uint32_t(x) << 16; float f; std::memcpy(&f, &u, 4); return f; }
@@ -57,8 +60,17 @@ constexpr float GLOBAL_MSCALE = 1.5545177444479562f; // K:266-267
 // ---- GEMV / GEMM rows: K:92-114 (linear), K:149-200 (matrix) --------------------------
 // y[t][m] = sum_k W[m][k] * x[t][k], fp32 accumulation, output bf16-rounded (or bf16 bits
 // for the lm_head, K:111,196).
+int g_dot_reverse = 0;  // noise-floor experiments: walk K backwards (same sum, other fp32 order)
+
 inline float dot_bf16(const uint16_t* w, const float* x, int K) {
     float acc[16] = {0};
+    if (g_dot_reverse) {
+        for (int k = K - 16; k >= 0; k -= 16)
+            for (int j = 0; j < 16; j++) acc[j] += bf(w[k + j]) * x[k + j];
+        for (int s = 8; s > 0; s >>= 1)
+            for (int j = 0; j < s; j++) acc[j] += acc[j + s];
+        return acc[0];
+    }
     for (int k = 0; k < K; k += 16)
         for (int j = 0; j < 16; j++) acc[j] += bf(w[k + j]) * x[k + j];
     for (int s = 8; s > 0; s >>= 1)
@@ -358,7 +370,9 @@ void decoder(State& s, Work& wk, int rows, GeoFn geo, void* ctx, bool split_ok) 
 #pragma omp parallel for schedule(dynamic) if (rows > 1)
         for (int t = 0; t < rows; t++) {
             RowGeo g = geo(ctx, li, t);
-            if (split_ok && rows == 1 && full && g.count >= 8192)  // R:424
+            if (g_split_part > 0 && full)  // noise-floor experiments: every global row through split-K
+                attend_row_split(s, &wk.q[size_t(t) * qd], g, &wk.attended[size_t(t) * qd], g_split_part);
+            else if (split_ok && rows == 1 && full && g.count >= 8192)  // R:424
                 attend_row_split(s, &wk.q[size_t(t) * qd], g, &wk.attended[size_t(t) * qd]);
             else
                 attend_row(s, full, &wk.q[size_t(t) * qd], g, &wk.attended[size_t(t) * qd]);
@@ -468,6 +482,8 @@ struct oracle_config { int d, layers, heads, kv_heads, ffn, vocab, window, patte
 struct oracle_layer { const uint16_t *pre_mixer, *post_mixer, *pre_mlp, *post_mlp, *qkv, *o, *q_norm, *k_norm, *gate_up, *down; };
 
 const char* oracle_last_error() { return g_error.c_str(); }
+void oracle_set_split_partition(int part) { g_split_part = part; }
+void oracle_set_dot_reverse(int on) { g_dot_reverse = on; }
 
 void oracle_set_threads(int n) {
 #ifdef _OPENMP

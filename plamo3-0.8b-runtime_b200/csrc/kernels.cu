@@ -12,6 +12,7 @@
 #include "common.cuh"
 #include "kernels.h"
 
+#include <algorithm>
 #include <cfloat>
 
 namespace plamo {
@@ -513,8 +514,10 @@ __global__ void k_finalize(const unsigned long long* keys, const int* key_map, i
     if (advance) { advance[r].pos += 1; advance[r].cstart += 1; }
     if (hist && r == 0) {
         const int c = *hist_count;
-        if (c < hist_cap) hist[c] = int(id);
-        *hist_count = c + 1;
+        if (c >= 0 && c < hist_cap) {
+            hist[c] = int(id);
+            *hist_count = c + 1;
+        }
     }
 }
 
@@ -546,7 +549,8 @@ __global__ void k_packed_decode(Linear lin, long long count, uint16_t* out) {
 // --------------------------------------------------------------------------------------------
 // launchers
 
-constexpr size_t GEMV_SMEM_MAX = 227 * 1024;
+// Staged-activation budget per GEMV CTA (below the 227 KB opt-in limit minus static scratch).
+constexpr size_t GEMV_SMEM_MAX = 224 * 1024;
 
 template <int R, bool P, int M>
 static cudaError_t gemv_launch(const GemvArgs& a, cudaStream_t s) {
@@ -596,9 +600,18 @@ cudaError_t launch_gemv(const GemvArgs& a, int mode, cudaStream_t s) {
     return cudaSuccess;
 }
 
+// The opt-in dynamic shared memory limit leaves room for each instantiation's static shared
+// memory (the argmax scratch of the logits mode).
 template <int R, bool P, int M>
 static cudaError_t gemv_attr() {
-    return cudaFuncSetAttribute(k_gemv<R, P, M>, cudaFuncAttributeMaxDynamicSharedMemorySize, GEMV_SMEM_MAX);
+    int dev = 0, optin = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    cudaFuncAttributes fa;
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, k_gemv<R, P, M>);
+    if (e != cudaSuccess) return e;
+    const size_t dyn = std::min(GEMV_SMEM_MAX, size_t(optin) - fa.sharedSizeBytes);
+    return cudaFuncSetAttribute(k_gemv<R, P, M>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(dyn));
 }
 template <int R, bool P>
 static cudaError_t gemv_attr_modes() {

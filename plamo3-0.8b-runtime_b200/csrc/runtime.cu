@@ -18,6 +18,8 @@
 #include <chrono>
 #include <cmath>
 #include <cstring>
+#include <mutex>
+#include <set>
 #include <string>
 #include <vector>
 
@@ -122,6 +124,7 @@ struct plamo_runtime {
         cudaError_t e = cudaMalloc(&q, bytes);
         if (e != cudaSuccess) return fail("Cannot allocate " + std::to_string(bytes) + " device bytes");
         allocs.push_back(q);
+        if (cudaMemset(q, 0, bytes) != cudaSuccess) return fail("Cannot clear device memory");
         device_bytes += bytes;
         p = static_cast<T*>(q);
         return 0;
@@ -162,6 +165,11 @@ struct plamo_batch {
 
 namespace plamo {
 
+// Live handles: closing is idempotent and a runtime's close also closes its batches.
+static std::mutex g_handles_mu;
+static std::set<plamo_runtime*> g_runtimes;
+static std::set<plamo_batch*> g_batches;
+
 // ------------------------------------------------------------------------------------------------
 // allocation helpers shared by runtime and batch
 
@@ -171,6 +179,7 @@ static int dev_alloc(Owner& o, plamo_runtime& rt, T*& p, size_t count) {
     const size_t bytes = std::max<size_t>(count * sizeof(T), 256);
     if (cudaMalloc(&q, bytes) != cudaSuccess) return fail("Cannot allocate " + std::to_string(bytes) + " device bytes");
     o.allocs.push_back(q);
+    if (cudaMemset(q, 0, bytes) != cudaSuccess) return fail("Cannot clear device memory");
     rt.device_bytes += bytes;
     p = static_cast<T*>(q);
     return 0;
@@ -517,6 +526,10 @@ static int open_common(const char* model_dir, int context, int packed, int devic
     }
     delete mf;  // weights are resident; the mappings are no longer needed
     if (rc) { delete rt; return rc; }
+    {
+        std::lock_guard<std::mutex> lock(g_handles_mu);
+        g_runtimes.insert(rt);
+    }
     *out = rt;
     return 0;
 }
@@ -635,13 +648,25 @@ static int setup_runtime(plamo_runtime* rt, const ModelFiles* mf, bool upload, s
     if (alloc_work(*rt, *rt, rt->work, 16) || alloc_outputs(*rt, *rt, rt->out, 1)) return 1;
     rt->chain_cap = rt->context;
     if (rt->dalloc(rt->chain_hist, size_t(rt->chain_cap)) || rt->dalloc(rt->chain_count, 1)) return 1;
+    CK(cudaMemset(rt->chain_count, 0, sizeof(int)));
     return 0;
 }
 
 void plamo_close(plamo_runtime* rt) {
-    if (!rt) return;
+    // Closing a runtime also closes the batches opened on it; closing an unknown or already
+    // closed handle is a no-op (so finalizers may run in any order).
+    std::vector<plamo_batch*> batches;
+    {
+        std::lock_guard<std::mutex> lock(g_handles_mu);
+        if (!rt || !g_runtimes.erase(rt)) return;
+        for (auto it = g_batches.begin(); it != g_batches.end();) {
+            if ((*it)->rt == rt) { batches.push_back(*it); it = g_batches.erase(it); }
+            else ++it;
+        }
+    }
     cudaSetDevice(rt->device);
     if (rt->stream) cudaStreamSynchronize(rt->stream);
+    for (plamo_batch* b : batches) delete b;
     delete rt;
 }
 
@@ -805,12 +830,19 @@ int plamo_batch_open(plamo_runtime* rt, int lanes, plamo_batch** out) {
     if (!rc) rc = alloc_work(*b, *rt, b->work, std::max(16, lanes));
     if (!rc) rc = alloc_outputs(*b, *rt, b->out, lanes);
     if (rc) { delete b; return rc; }
+    {
+        std::lock_guard<std::mutex> lock(g_handles_mu);
+        g_batches.insert(b);
+    }
     *out = b;
     return 0;
 }
 
 void plamo_batch_close(plamo_batch* b) {
-    if (!b) return;
+    {
+        std::lock_guard<std::mutex> lock(g_handles_mu);
+        if (!b || !g_batches.erase(b)) return;
+    }
     cudaSetDevice(b->rt->device);
     cudaStreamSynchronize(b->rt->stream);
     delete b;

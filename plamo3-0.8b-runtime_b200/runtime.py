@@ -14,7 +14,9 @@ the built library (or without a CUDA device at open time) raises.
 """
 from __future__ import annotations
 
+import atexit
 import ctypes
+import weakref
 from pathlib import Path
 
 import numpy as np
@@ -32,6 +34,19 @@ class PlamoError(RuntimeError):
 
 
 _lib = None
+
+# Open handles, closed batches-first at interpreter exit (before the CUDA runtime tears down), so
+# finalizers never run in an unsafe order.
+_open_batches = weakref.WeakSet()
+_open_runtimes = weakref.WeakSet()
+
+
+@atexit.register
+def _close_all():
+    for b in list(_open_batches):
+        b.close()
+    for r in list(_open_runtimes):
+        r.close()
 
 
 def library() -> ctypes.CDLL:
@@ -112,6 +127,7 @@ class Runtime:
             self._h = _handle
         else:
             _check(L.plamo_open(str(directory).encode(), int(context), int(bool(packed)), int(device), ctypes.byref(self._h)))
+        _open_runtimes.add(self)
         dims = np.zeros(10, dtype=np.int32)
         _check(L.plamo_dims(self._h, dims.ctypes.data_as(_i32p)))
         (self.hidden_size, self.layers, self.heads, self.kv_heads, self.head_dim, self.ffn, self.vocab,
@@ -230,11 +246,13 @@ class Batch:
         self.lanes = lanes
         self._h = _vp()
         _check(library().plamo_batch_open(runtime._h, int(lanes), ctypes.byref(self._h)))
+        _open_batches.add(self)
 
     def close(self):
-        if self._h:
+        # plamo_close already released the batches of a closed runtime
+        if self._h and self.runtime._h:
             library().plamo_batch_close(self._h)
-            self._h = _vp()
+        self._h = _vp()
 
     def __del__(self):
         try:

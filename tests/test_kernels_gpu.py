@@ -23,16 +23,35 @@ def rt(pkg):
     return pkg.runtime
 
 
+# Device buffers handed to the C ABI as raw pointers must outlive the kernels that use them: a
+# temporary tensor whose only use is `.data_ptr()` is released to torch's caching allocator at
+# once and its memory can be handed to the next temporary. Every buffer made by dev() is kept
+# alive until the end of the test (after a device synchronisation).
+_ALIVE = []
+
+
+@pytest.fixture(autouse=True)
+def _keep_device_buffers_alive():
+    yield
+    import torch as t
+    if t.cuda.is_available():
+        t.cuda.synchronize()
+    _ALIVE.clear()
+
+
 def dev(torch, a):
-    """numpy -> CUDA tensor with the same bytes."""
+    """numpy -> CUDA tensor with the same bytes (kept alive for the rest of the test)."""
     a = np.ascontiguousarray(a)
     if a.dtype == np.uint16:
-        return torch.from_numpy(a.view(np.int16)).cuda()
-    if a.dtype == np.uint32:
-        return torch.from_numpy(a.view(np.int32)).cuda()
-    if a.dtype == np.uint64:
-        return torch.from_numpy(a.view(np.int64)).cuda()
-    return torch.from_numpy(a).cuda()
+        t = torch.from_numpy(a.view(np.int16)).cuda()
+    elif a.dtype == np.uint32:
+        t = torch.from_numpy(a.view(np.int32)).cuda()
+    elif a.dtype == np.uint64:
+        t = torch.from_numpy(a.view(np.int64)).cuda()
+    else:
+        t = torch.from_numpy(a).cuda()
+    _ALIVE.append(t)
+    return t
 
 
 def host(t, dtype):
@@ -41,6 +60,12 @@ def host(t, dtype):
 
 def bf16_bits(oracle, x):
     return oracle.f32_to_bf16(np.asarray(x, dtype=np.float32))
+
+
+def bf16_ulp(x):
+    """Spacing of bf16 numbers at magnitude x (x >= 0): 2^(exponent(x) - 7)."""
+    e = np.floor(np.log2(np.maximum(x, 2.0 ** -126)))
+    return np.exp2(e - 7)
 
 
 def test_packed_decode_golden(torch, rt):
@@ -85,9 +110,12 @@ def test_linear_matches_oracle_and_packed_equals_raw(torch, rt, pkg, oracle, row
         torch.cuda.synchronize()
         got, gotp = host(y, np.uint16).reshape(rows, M), host(yp, np.uint16).reshape(rows, M)
         assert np.array_equal(got, gotp), (M, K)
-        diff = np.abs(oracle.bf16_to_f32(got) - oracle.bf16_to_f32(ref))
-        ulp = np.abs(oracle.bf16_to_f32(ref)) * 2.0 ** -7 + 1e-30
-        assert np.all(diff <= ulp), (M, K, float(diff.max()))
+        g32, r32 = oracle.bf16_to_f32(got), oracle.bf16_to_f32(ref)
+        # fp32 sums in a different order round to bf16 values at most one bf16 ulp apart, plus the
+        # fp32 accumulation error itself where cancellation leaves a result near zero
+        bound = bf16_ulp(np.maximum(np.abs(g32), np.abs(r32))) + 1e-5
+        bad = np.abs(g32 - r32) > bound
+        assert not bad.any(), (M, K, int(bad.sum()), g32[bad][:4], r32[bad][:4])
 
 
 def test_linear_reference_pattern(torch, rt, oracle):

