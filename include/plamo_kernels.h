@@ -57,6 +57,11 @@ PLAMO_API int plamo_k_attention(const uint16_t* q, const uint16_t* keys, const u
                       int cap, int first, int count, int begin, int end, int full, const uint32_t* rope_local,
                       int splits, uint16_t* out, void* stream);
 
+/* The fp32 exponential used by the softmax and SwiGLU kernels (Kernels.metal:209, :386 use exp):
+ * y[i] = e^x[i] from IEEE operations only (Cody-Waite reduction, degree-7 Taylor polynomial), so a
+ * CPU restatement reproduces it exactly. n floats, device pointers. */
+PLAMO_API int plamo_k_exp(const float* x, float* y, long long n, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

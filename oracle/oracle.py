@@ -85,6 +85,7 @@ def lib():
         L.oracle_rope_tables.argtypes = [_f32p, _f32p, ctypes.c_int, ctypes.c_int, _u16p, _u16p]
         L.oracle_attention.argtypes = [_u16p, _u16p, _f32p] + [ctypes.c_int] * 8 + [_f32p, ctypes.c_int, ctypes.c_int, _f32p]
         L.oracle_packed_decode.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, _u16p]
+        L.oracle_exp.argtypes = [_f32p, _f32p, ctypes.c_longlong]
         L.oracle_set_threads.argtypes = [ctypes.c_int]
         L.oracle_threads.restype = ctypes.c_int
         _lib = L
@@ -420,6 +421,14 @@ def attention(keys, values, q, heads, kv_heads, cap, first, count, begin, end, f
     lib().oracle_attention(_p(keys, _u16p), _p(values, _u16p), _p(q, _f32p), heads, kv_heads, cap, first, count,
                            begin, end, int(full), _p(il, _f32p), local_rows, split, _p(out, _f32p))
     return out
+
+
+def exp(x: np.ndarray) -> np.ndarray:
+    """The restatement's software exp (the same IEEE operation sequence as the CUDA path)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    y = np.empty_like(x)
+    lib().oracle_exp(_p(x, _f32p), _p(y, _f32p), x.size)
+    return y
 
 
 def packed_decode(data: np.ndarray, entries: np.ndarray, count: int) -> np.ndarray:

@@ -9,8 +9,14 @@
 //   Sources/Plamo/Batch.metal     (BM:)  batched kernels
 //   Sources/Plamo/Runtime.swift   (R:)   scalar orchestration
 //   Sources/Plamo/Batch.swift     (B:)   batched orchestration
-// fp32 accumulation order is this file's own (fixed, deterministic); the reference's order is
-// Apple simdgroup order, so parity with it is within floating-point tolerance, not bitwise.
+// fp32 summation order: the reference sums in Apple simdgroup order, which cannot be reproduced
+// here. This restatement instead fixes the order to the summation trees of the CUDA path
+// (per-lane chunks and butterfly trees for dot products and norms, 32/64/256-key split-K
+// attention with a log-sum-exp merge, and the same software exp), so the CUDA path can be checked
+// bit for bit. The random-init test models are chaotic under reordering (RMSE ~0.2 of logits from
+// reversing the dot order alone, see noise_floor in oracle.py), so only an order-exact restatement
+// can pin them at the north-star tolerance. Build with -ffp-contract=off: every fused multiply-add
+// below is an explicit std::fma.
 //
 // Parity status: the reference forward (Metal, or PFN's MLX module) cannot run on Linux, so the
 // model-level restatement is "parity unpinned" against the reference itself. The packed-weight
@@ -31,9 +37,9 @@
 namespace {
 
 thread_local std::string g_error;
-// When > 0, every attention row uses the split-K path with this partition size. The two paths
-// differ only in fp32 summation order; comparing them measures the restatement's own noise floor.
-int g_split_part = 0;
+// When > 0, every layer's attention uses this many split-K partitions instead of the CUDA path's
+// count: the same arithmetic in another fp32 order (noise-floor experiments only).
+int g_split_override = 0;
 
 // ---- bf16 helpers: K:5-10 -------------------------------------------------------------
 inline float bf(uint16_t x) { uint32_t u = uint32_t(x) << 16; float f; std::memcpy(&f, &u, 4); return f; }
@@ -62,20 +68,60 @@ constexpr float GLOBAL_MSCALE = 1.5545177444479562f; // K:266-267
 // for the lm_head, K:111,196).
 int g_dot_reverse = 0;  // noise-floor experiments: walk K backwards (same sum, other fp32 order)
 
-inline float dot_bf16(const uint16_t* w, const float* x, int K) {
-    float acc[16] = {0};
-    if (g_dot_reverse) {
-        for (int k = K - 16; k >= 0; k -= 16)
-            for (int j = 0; j < 16; j++) acc[j] += bf(w[k + j]) * x[k + j];
-        for (int s = 8; s > 0; s >>= 1)
-            for (int j = 0; j < s; j++) acc[j] += acc[j + s];
-        return acc[0];
+// Sum over 32 "lanes" by the xor-butterfly tree (offsets 16, 8, 4, 2, 1).
+inline float butterfly32(float (&v)[32]) {
+    for (int off = 16; off >= 1; off >>= 1) {
+        float t[32];
+        for (int l = 0; l < 32; l++) t[l] = v[l] + v[l ^ off];
+        for (int l = 0; l < 32; l++) v[l] = t[l];
     }
-    for (int k = 0; k < K; k += 16)
-        for (int j = 0; j < 16; j++) acc[j] += bf(w[k + j]) * x[k + j];
-    for (int s = 8; s > 0; s >>= 1)
-        for (int j = 0; j < s; j++) acc[j] += acc[j + s];
-    return acc[0];
+    return v[0];
+}
+
+// Dot product in the GEMV order: lane l owns weights [g*512 + 16l, +16) of each 512-weight group g
+// and sums even / odd elements into two accumulators; lane sums meet in the butterfly tree.
+inline float dot_bf16(const uint16_t* w, const float* x, int K) {
+    const int G = (K + 511) / 512;
+    float lanes[32];
+    for (int l = 0; l < 32; l++) {
+        float a0 = 0.f, a1 = 0.f;
+        for (int gi = 0; gi < G; gi++) {
+            const int g = g_dot_reverse ? G - 1 - gi : gi;
+            const int e0 = g * 512 + 16 * l;
+            if (e0 >= K) continue;
+            for (int k = 0; k < 8; k++) {
+                a0 = std::fma(bf(w[e0 + 2 * k]), x[e0 + 2 * k], a0);
+                a1 = std::fma(bf(w[e0 + 2 * k + 1]), x[e0 + 2 * k + 1], a1);
+            }
+        }
+        lanes[l] = a0 + a1;
+    }
+    return butterfly32(lanes);
+}
+
+// e^x from IEEE operations only: Cody-Waite reduction x = n*ln2 + r (ln2 = 355/512 + rest),
+// degree-7 Taylor polynomial of e^r in Horner form, scale by 2^n via the exponent field. The CUDA
+// path evaluates the same sequence, so both give identical bits.
+inline float f_of(uint32_t u) { float f; std::memcpy(&f, &u, 4); return f; }
+inline float pexp(float x) {
+    if (x != x) return x;
+    if (x > 88.72283935546875f) return std::numeric_limits<float>::infinity();
+    if (x < -103.972084045410156f) return 0.0f;
+    const float n = std::rint(x * 1.44269502162933349609375f);
+    float r = std::fma(-n, 0.693359375f, x);
+    r = std::fma(-n, -2.12194440e-4f, r);
+    float p = 1.98412698e-4f;
+    p = std::fma(p, r, 1.38888889e-3f);
+    p = std::fma(p, r, 8.33333377e-3f);
+    p = std::fma(p, r, 4.16666679e-2f);
+    p = std::fma(p, r, 1.66666672e-1f);
+    p = std::fma(p, r, 0.5f);
+    p = std::fma(p, r, 1.0f);
+    p = std::fma(p, r, 1.0f);
+    const int k = int(n);
+    if (k > 127) return (p * f_of(254u << 23)) * f_of(uint32_t(k - 127 + 127) << 23);
+    if (k < -126) return (p * f_of(uint32_t(k + 100 + 127) << 23)) * f_of(uint32_t(127 - 100) << 23);
+    return p * f_of(uint32_t(k + 127) << 23);
 }
 
 void linear_rows(const uint16_t* w, const float* x, int rows, int K, int M, float* y, uint16_t* y_bits) {
@@ -93,13 +139,29 @@ void linear_rows(const uint16_t* w, const float* x, int rows, int K, int M, floa
 // ---- RMSNorm: K:46-90 ------------------------------------------------------------------
 // z = bf(bf(x*rsqrt(mean(x^2)+eps)) * bf(w+offset)); optional residual x <- bf(x+z) (K:71)
 // and optional fused next norm with offset 1 over the new x (K:75-89).
+// Sum of squares in the norm kernel's order: 256 threads, thread t sums x[t + 256j] (j < 16) by
+// fma, each warp of 32 threads by the butterfly tree, the 8 warp sums by a second butterfly (the
+// other 24 lanes contribute zeros).
 inline float rms_scale(const float* x, int n) {
-    float acc[8] = {0};
-    for (int i = 0; i < n; i += 8)
-        for (int j = 0; j < 8; j++) acc[j] += x[i + j] * x[i + j];
-    for (int s = 4; s > 0; s >>= 1)
-        for (int j = 0; j < s; j++) acc[j] += acc[j + s];
-    return 1.0f / std::sqrt(acc[0] / float(n) + EPS);
+    float warps[8];
+    for (int w = 0; w < 8; w++) {
+        float lanes[32];
+        for (int l = 0; l < 32; l++) {
+            const int t = w * 32 + l;
+            float ss = 0.f;
+            for (int j = 0; j < 16; j++) {
+                const int i = t + 256 * j;
+                const float v = i < n ? x[i] : 0.f;
+                ss = std::fma(v, v, ss);
+            }
+            lanes[l] = ss;
+        }
+        warps[w] = butterfly32(lanes);
+    }
+    float lanes[32];
+    for (int l = 0; l < 32; l++) lanes[l] = l < 8 ? warps[l] : 0.f;
+    const float total = butterfly32(lanes);
+    return 1.0f / std::sqrt(total / float(n) + EPS);
 }
 
 void norm_row(const uint16_t* w, const float* x, float* y, int n, float offset,
@@ -124,7 +186,7 @@ void swiglu_rows(const float* gates, float* out, int rows, int F) {
         for (int i = 0; i < F; i++) {
             float g = gates[size_t(t) * 2 * F + i];
             float u = gates[size_t(t) * 2 * F + F + i];
-            out[size_t(t) * F + i] = roundbf(roundbf(g / (1.0f + std::exp(-g))) * u);
+            out[size_t(t) * F + i] = roundbf(roundbf(g / (1.0f + pexp(-g))) * u);
         }
 }
 
@@ -210,6 +272,12 @@ struct State {
     std::vector<uint32_t> result;
     bool full_layer(int i) const { return i % c.pattern == c.pattern - 1; }
     int cap_of(int i) const { return full_layer(i) ? c.context : local_cap; }
+    // split-K partition count of a layer (the CUDA runtime's choice: ~64 keys per partition of the
+    // local window, at most 256 keys per partition of the global history, at least 32 partitions)
+    int splits_of(int i) const {
+        const int cap = cap_of(i);
+        return full_layer(i) ? std::max(32, (cap + 255) / 256) : std::max(1, std::min(32, (cap + 63) / 64));
+    }
 };
 
 // ---- QK-norm + RoPE + KV append: K:223-259 (qkv), BM:1-39 (qkv_mapped) ------------------
@@ -217,9 +285,13 @@ void qkv_row(const State& s, const LayerW& w, bool full, const float* qkv, float
     const int H = s.c.heads, KV = s.c.kv_heads;
     for (int h = 0; h < H + KV; h++) {
         const float* v = qkv + h * HD;
-        float acc[4] = {0, 0, 0, 0};
-        for (int d = 0; d < HD; d += 4) for (int j = 0; j < 4; j++) acc[j] += v[d + j] * v[d + j];
-        float sum = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+        float lanes[32];  // lane l holds v[l + 32j], j < 4 (Kernels.metal:237-241 layout)
+        for (int l = 0; l < 32; l++) {
+            float ss = 0.f;
+            for (int j = 0; j < 4; j++) ss = std::fma(v[l + 32 * j], v[l + 32 * j], ss);
+            lanes[l] = ss;
+        }
+        float sum = butterfly32(lanes);
         float scale = 1.0f / std::sqrt(sum / 128.0f + EPS);
         const uint16_t* nw = h < H ? w.q_norm : w.k_norm;
         float z[HD];
@@ -281,58 +353,78 @@ void attend_row(const State& s, bool full, const float* q, const RowGeo& g, floa
     }
 }
 
-// ---- split-K attention + merge (K:440-562), used by the reference for a batch-1 global
-// layer once count >= 8192 (R:131,424-430). 256-key partitions, (max, sum) statistics,
-// log-sum-exp merge, bf16-rounded output.
-void attend_row_split(const State& s, const float* q, const RowGeo& g, float* out, int part = 256) {
+// ---- split-K attention + merge (K:440-562) in the CUDA kernel's order ---------------------
+// `splits` key partitions of per = roundup32(ceil(count / splits)) window positions, each clipped
+// to the row's visible range; per partition and head: scores by an fma chain over d, scaled;
+// max; e = exp(score - max) summed per lane (i mod 32, increasing i) then by the butterfly tree;
+// P.V by an fma chain over keys. Merge: M = max of partition maxima, weights exp(m_s - M),
+// L = fma chain of w_s * l_s, output fma chain of O_s * w_s, bf16-rounded O / L.
+void attend_row_splitk(const State& s, bool full, const float* q, const RowGeo& g, float* out, int splits) {
     const int H = s.c.heads, KV = s.c.kv_heads, group = H / KV;
-    int parts = (g.count + part - 1) / part;
-    std::vector<float> po(size_t(parts) * H * HD), pm(size_t(parts) * H), pl(size_t(parts) * H);
-#pragma omp parallel for schedule(static)
-    for (int pi = 0; pi < parts; pi++) {
-        int first = pi * part, length = std::min(part, g.count - first);
-        std::vector<float> sc(length);
+    int per = (g.count + splits - 1) / splits;
+    per = (per + 31) & ~31;
+    std::vector<float> po(size_t(splits) * H * HD, 0.f), pm(size_t(splits) * H), pl(size_t(splits) * H);
+#pragma omp parallel for schedule(dynamic)
+    for (int sp = 0; sp < splits; sp++) {
+        const int k0 = sp * per, k1 = std::min(k0 + per, g.count);
+        const int lo = std::max(k0, g.begin), hi = std::min(k1, g.end);
+        if (lo >= hi) {
+            for (int h = 0; h < H; h++) { pm[size_t(sp) * H + h] = -INFINITY; pl[size_t(sp) * H + h] = 0.f; }
+            continue;
+        }
+        const int n = hi - lo;
+        std::vector<float> kr(size_t(n) * KV * HD), sc(n);
+        for (int i = 0; i < n; i++) {
+            const int key = lo + i, phys = (g.first + key) % g.cap;
+            for (int kvh = 0; kvh < KV; kvh++) {
+                const uint16_t* k = g.keys + (size_t(phys) * KV + kvh) * HD;
+                for (int d = 0; d < HD; d++) {
+                    const int partner = d < 64 ? d + 64 : d - 64;
+                    kr[(size_t(i) * KV + kvh) * HD + d] =
+                        full ? bf(k[d]) : s.rope.rotated(bf(k[d]), bf(k[partner]), d, key, false);
+                }
+            }
+        }
         for (int h = 0; h < H; h++) {
-            int kvh = h / group;
+            const int kvh = h / group;
             const float* qh = q + h * HD;
             float m = -INFINITY;
-            for (int i = 0; i < length; i++) {
-                int key = first + i, phys = (g.first + key) % g.cap;
-                const uint16_t* k = g.keys + (size_t(phys) * KV + kvh) * HD;
-                float acc[8] = {0};
-                for (int d = 0; d < HD; d += 8) for (int j = 0; j < 8; j++) acc[j] += qh[d + j] * bf(k[d + j]);
-                for (int st = 4; st > 0; st >>= 1) for (int j = 0; j < st; j++) acc[j] += acc[j + st];
-                float v = (key >= g.begin && key < g.end) ? acc[0] * ATTN_SCALE : -INFINITY;
-                sc[i] = v; m = std::max(m, v);
+            for (int i = 0; i < n; i++) {
+                const float* kv = &kr[(size_t(i) * KV + kvh) * HD];
+                float acc = 0.f;
+                for (int d = 0; d < HD; d++) acc = std::fma(qh[d], kv[d], acc);
+                sc[i] = acc * ATTN_SCALE;
+                m = std::max(m, sc[i]);
             }
-            float total = 0;
-            for (int i = 0; i < length; i++) { float e = std::isfinite(m) ? std::exp(sc[i] - m) : 0.0f; sc[i] = e; total += e; }
-            float o[HD] = {0};
-            for (int i = 0; i < length; i++) {
-                if (sc[i] == 0.0f) continue;
-                int phys = (g.first + first + i) % g.cap;
+            float lanes[32] = {0};
+            for (int i = 0; i < n; i++) {
+                const float e = pexp(sc[i] - m);
+                sc[i] = e;
+                lanes[i % 32] += e;
+            }
+            const float l = butterfly32(lanes);
+            float* o = &po[(size_t(sp) * H + h) * HD];
+            for (int i = 0; i < n; i++) {
+                const int phys = (g.first + lo + i) % g.cap;
                 const uint16_t* v = g.values + (size_t(phys) * KV + kvh) * HD;
-                for (int d = 0; d < HD; d++) o[d] += sc[i] * bf(v[d]);
+                for (int d = 0; d < HD; d++) o[d] = std::fma(sc[i], bf(v[d]), o[d]);
             }
-            for (int d = 0; d < HD; d++) po[(size_t(pi) * H + h) * HD + d] = o[d];
-            pm[size_t(pi) * H + h] = m; pl[size_t(pi) * H + h] = total;
+            pm[size_t(sp) * H + h] = m;
+            pl[size_t(sp) * H + h] = l;
         }
     }
     for (int h = 0; h < H; h++) {
-        float m = -INFINITY;
-        for (int pi = 0; pi < parts; pi++) m = std::max(m, pm[size_t(pi) * H + h]);
-        float total = 0;
-        std::vector<float> ratio(parts);
-        for (int pi = 0; pi < parts; pi++) {
-            float l = pl[size_t(pi) * H + h];
-            ratio[pi] = l > 0 ? std::exp(pm[size_t(pi) * H + h] - m) : 0.0f;
-            total += ratio[pi] * l;
+        float M = -INFINITY;
+        for (int sp = 0; sp < splits; sp++) M = std::max(M, pm[size_t(sp) * H + h]);
+        float L = 0.f, o[HD] = {0};
+        for (int sp = 0; sp < splits; sp++) {
+            const float l = pl[size_t(sp) * H + h];
+            if (!(l > 0.f)) continue;
+            const float w = pexp(pm[size_t(sp) * H + h] - M);
+            L = std::fma(w, l, L);
+            for (int d = 0; d < HD; d++) o[d] = std::fma(po[(size_t(sp) * H + h) * HD + d], w, o[d]);
         }
-        for (int d = 0; d < HD; d++) {
-            float acc = 0;
-            for (int pi = 0; pi < parts; pi++) acc += po[(size_t(pi) * H + h) * HD + d] * ratio[pi];
-            out[h * HD + d] = roundbf(acc / total);
-        }
+        for (int d = 0; d < HD; d++) out[h * HD + d] = roundbf(o[d] / L);
     }
 }
 
@@ -370,12 +462,8 @@ void decoder(State& s, Work& wk, int rows, GeoFn geo, void* ctx, bool split_ok) 
 #pragma omp parallel for schedule(dynamic) if (rows > 1)
         for (int t = 0; t < rows; t++) {
             RowGeo g = geo(ctx, li, t);
-            if (g_split_part > 0 && full)  // noise-floor experiments: every global row through split-K
-                attend_row_split(s, &wk.q[size_t(t) * qd], g, &wk.attended[size_t(t) * qd], g_split_part);
-            else if (split_ok && rows == 1 && full && g.count >= 8192)  // R:424
-                attend_row_split(s, &wk.q[size_t(t) * qd], g, &wk.attended[size_t(t) * qd]);
-            else
-                attend_row(s, full, &wk.q[size_t(t) * qd], g, &wk.attended[size_t(t) * qd]);
+            attend_row_splitk(s, full, &wk.q[size_t(t) * qd], g, &wk.attended[size_t(t) * qd],
+                              g_split_override > 0 ? g_split_override : s.splits_of(li));
         }
         linear_rows(w.o, wk.attended.data(), rows, qd, d, wk.projected.data(), nullptr);  // R:445
         for (int t = 0; t < rows; t++)  // R:446
@@ -482,7 +570,7 @@ struct oracle_config { int d, layers, heads, kv_heads, ffn, vocab, window, patte
 struct oracle_layer { const uint16_t *pre_mixer, *post_mixer, *pre_mlp, *post_mlp, *qkv, *o, *q_norm, *k_norm, *gate_up, *down; };
 
 const char* oracle_last_error() { return g_error.c_str(); }
-void oracle_set_split_partition(int part) { g_split_part = part; }
+void oracle_set_split_partition(int splits) { g_split_override = splits; }
 void oracle_set_dot_reverse(int on) { g_dot_reverse = on; }
 
 void oracle_set_threads(int n) {
@@ -679,6 +767,7 @@ void oracle_norm(const uint16_t* w, const float* x, float* y, int rows, int n, f
 }
 void oracle_swiglu(const float* gates, float* out, int rows, int F) { swiglu_rows(gates, out, rows, F); }
 uint32_t oracle_argmax_bits(const uint16_t* v, int n) { return argmax_bits(v, n); }
+void oracle_exp(const float* x, float* y, long long n) { for (long long i = 0; i < n; i++) y[i] = pexp(x[i]); }
 uint32_t oracle_argmax_f32(const float* v, int n) { return argmax_f32(v, n); }
 void oracle_rope_tables(const float* inv_local, const float* inv_full, int local_rows, int context,
                         uint16_t* local_out, uint16_t* global_out) {
@@ -697,7 +786,7 @@ void oracle_attention(const uint16_t* keys, const uint16_t* values, const float*
     std::vector<float> zeros(64, 0.0f);
     s.rope.build(inv_local, zeros.data(), local_rows, 1);
     RowGeo g{const_cast<uint16_t*>(keys), const_cast<uint16_t*>(values), cap, 0, 0, first, count, begin, end};
-    if (split > 0) attend_row_split(s, q, g, out, split);
+    if (split > 0) attend_row_splitk(s, full != 0, q, g, out, split);
     else attend_row(s, full != 0, q, g, out);
 }
 

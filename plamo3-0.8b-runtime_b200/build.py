@@ -20,7 +20,9 @@ BUILD = PKG / "_build"
 LIB = PKG / "lib" / "libplamo_cuda.so"
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
+# -fmad=false: no implicit multiply-add contraction; every fused multiply-add in the kernels is an
+# explicit fmaf, so the CPU restatement can reproduce the arithmetic bit for bit.
+NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-fmad=false", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
               "--expt-relaxed-constexpr", "-I", str(INCLUDE), "-I", str(CSRC)]
 SOURCES = ["kernels.cu", "runtime.cu", "kernel_api.cu", "loader.cpp"]
 

@@ -28,6 +28,31 @@ __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
     return r;
 }
 
+// e^x in fp32 from IEEE operations only (so the CPU restatement reproduces it bit for bit):
+// Cody-Waite reduction x = n*ln2 + r with ln2 split as 355/512 + (ln2 - 355/512), |r| <= ln2/2,
+// then the degree-7 Taylor polynomial of e^r in Horner form (truncation < 6e-9 relative), scaled
+// by 2^n through the exponent field (two steps at the ends of the range so subnormals round once).
+__device__ __forceinline__ float pexp(float x) {
+    if (x != x) return x;
+    if (x > 88.72283935546875f) return __int_as_float(0x7f800000);
+    if (x < -103.972084045410156f) return 0.0f;
+    const float n = rintf(__fmul_rn(x, 1.44269502162933349609375f));
+    float r = fmaf(-n, 0.693359375f, x);
+    r = fmaf(-n, -2.12194440e-4f, r);
+    float p = 1.98412698e-4f;          // 1/5040
+    p = fmaf(p, r, 1.38888889e-3f);    // 1/720
+    p = fmaf(p, r, 8.33333377e-3f);    // 1/120
+    p = fmaf(p, r, 4.16666679e-2f);    // 1/24
+    p = fmaf(p, r, 1.66666672e-1f);    // 1/6
+    p = fmaf(p, r, 0.5f);
+    p = fmaf(p, r, 1.0f);
+    p = fmaf(p, r, 1.0f);
+    const int k = int(n);
+    if (k > 127) return __fmul_rn(__fmul_rn(p, __int_as_float(254 << 23)), __int_as_float((k - 127 + 127) << 23));
+    if (k < -126) return __fmul_rn(__fmul_rn(p, __int_as_float((k + 100 + 127) << 23)), __int_as_float((127 - 100) << 23));
+    return __fmul_rn(p, __int_as_float((k + 127) << 23));
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(FULL_MASK, v, o);

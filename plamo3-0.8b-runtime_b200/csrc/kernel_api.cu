@@ -1,6 +1,7 @@
 // Kernel-level C ABI (include/plamo_kernels.h): thin launchers over kernels.cu on caller-owned
 // device buffers.
 #include "../../include/plamo_kernels.h"
+#include "common.cuh"
 #include "kernels.h"
 
 #include <mutex>
@@ -28,6 +29,11 @@ static bool configured() {
 }
 
 namespace {
+__global__ void k_exp(const float* x, float* y, long long n) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) y[i] = pexp(x[i]);
+}
+
 __global__ void k_keys_to_index(const unsigned long long* keys, int rows, uint32_t* out) {
     const int r = blockIdx.x * blockDim.x + threadIdx.x;
     if (r < rows) {
@@ -58,6 +64,13 @@ int plamo_k_linear(const void* w, const uint32_t* offsets, const uint16_t* x, in
     a.ystride = mode == 1 ? M / 2 : M;
     a.keys = reinterpret_cast<unsigned long long*>(argmax_keys);
     cudaError_t e = launch_gemv(a, mode, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? 0 : kfail(e);
+}
+
+int plamo_k_exp(const float* x, float* y, long long n, void* stream) {
+    if (!x || !y || n < 1) { g_error = "Invalid exp arguments"; return 1; }
+    k_exp<<<unsigned((n + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(x, y, n);
+    cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? 0 : kfail(e);
 }
 

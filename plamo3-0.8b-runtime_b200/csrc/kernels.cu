@@ -183,7 +183,7 @@ __global__ void __launch_bounds__(256) k_gemv(GemvArgs a) {
             const float u = __shfl_down_sync(FULL_MASK, res, 16);
             if (holder && idx < R && idx < a.rows) {
                 const float gq = rbf(res), uq = rbf(u);
-                const float act = rbf(rbf(gq / (1.0f + expf(-gq))) * uq);
+                const float act = rbf(rbf(gq / (1.0f + pexp(-gq))) * uq);
                 const int orow = a.out_map ? a.out_map[idx] : idx;
                 a.y[size_t(orow) * a.ystride + m] = uint16_t(f2bf(act));
             }
@@ -448,7 +448,7 @@ __global__ void __launch_bounds__(256) k_attn_partial(AttnArgs a) {
         for (int i = lane; i < n; i += 32) m = fmaxf(m, p[i]);
         m = warp_max(m);
         float l = 0.f;
-        for (int i = lane; i < n; i += 32) { const float e = expf(p[i] - m); p[i] = e; l += e; }
+        for (int i = lane; i < n; i += 32) { const float e = pexp(p[i] - m); p[i] = e; l += e; }
         l = warp_sum(l);
         if (lane == 0) ml[h] = make_float2(m, l);
     }
@@ -492,8 +492,8 @@ __global__ void __launch_bounds__(128) k_attn_merge(AttnArgs a) {
     for (int s = 0; s < a.splits; s++) {
         const float2 st = ml[s * a.H + h];
         if (st.y > 0.f) {
-            const float w = expf(st.x - M);
-            L += w * st.y;
+            const float w = pexp(st.x - M);
+            L = fmaf(w, st.y, L);
             o = fmaf(a.part_o[((size_t(r) * a.splits + s) * a.H + h) * 128 + d], w, o);
         }
     }
