@@ -78,23 +78,30 @@ inline float butterfly32(float (&v)[32]) {
     return v[0];
 }
 
-// Dot product in the GEMV order: lane l owns weights [g*512 + 16l, +16) of each 512-weight group g
-// and sums even / odd elements into two accumulators; lane sums meet in the butterfly tree.
+// Dot product in the GEMV order. K is cut into segments of 1536 weights (three 512-weight groups;
+// the last segment may be shorter). Within a segment, lane l owns weights [g*512 + 16l, +16) of
+// each group g and sums even / odd elements into two fma chains; the lane's segment partial
+// (even + odd) is added to its running total segment by segment; the 32 lane totals meet in the
+// butterfly tree.
 inline float dot_bf16(const uint16_t* w, const float* x, int K) {
-    const int G = (K + 511) / 512;
+    const int G = (K + 511) / 512, S = (G + 2) / 3;
     float lanes[32];
     for (int l = 0; l < 32; l++) {
-        float a0 = 0.f, a1 = 0.f;
-        for (int gi = 0; gi < G; gi++) {
-            const int g = g_dot_reverse ? G - 1 - gi : gi;
-            const int e0 = g * 512 + 16 * l;
-            if (e0 >= K) continue;
-            for (int k = 0; k < 8; k++) {
-                a0 = std::fma(bf(w[e0 + 2 * k]), x[e0 + 2 * k], a0);
-                a1 = std::fma(bf(w[e0 + 2 * k + 1]), x[e0 + 2 * k + 1], a1);
+        float t = 0.f;
+        for (int si = 0; si < S; si++) {
+            const int seg = g_dot_reverse ? S - 1 - si : si;
+            float a0 = 0.f, a1 = 0.f;
+            for (int g = 3 * seg; g < std::min(G, 3 * seg + 3); g++) {
+                const int e0 = g * 512 + 16 * l;
+                if (e0 >= K) continue;
+                for (int k = 0; k < 8; k++) {
+                    a0 = std::fma(bf(w[e0 + 2 * k]), x[e0 + 2 * k], a0);
+                    a1 = std::fma(bf(w[e0 + 2 * k + 1]), x[e0 + 2 * k + 1], a1);
+                }
             }
+            t = t + (a0 + a1);
         }
-        lanes[l] = a0 + a1;
+        lanes[l] = t;
     }
     return butterfly32(lanes);
 }
@@ -276,7 +283,7 @@ struct State {
     // local window, at most 256 keys per partition of the global history, at least 32 partitions)
     int splits_of(int i) const {
         const int cap = cap_of(i);
-        return full_layer(i) ? std::max(32, (cap + 255) / 256) : std::max(1, std::min(32, (cap + 63) / 64));
+        return full_layer(i) ? std::max(32, (cap + 255) / 256) : std::max(1, (cap + 63) / 64);
     }
 };
 

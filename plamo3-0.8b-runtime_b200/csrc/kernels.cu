@@ -112,7 +112,9 @@ __global__ void __launch_bounds__(256) k_gemv(GemvArgs a) {
     // is the same for every R and mode, so a batched step equals the batch-1 path bit for bit.
     constexpr int A = 2;
     constexpr int NV = NW * R;
-    constexpr int UG = R <= 4 ? 4 : 2;
+    // One load batch = one 1536-weight segment (3 groups of 512); segment partials are folded into
+    // the running total in order (the summation order of the restatement's dot_bf16).
+    constexpr int UG = 3;
     const int K = a.lin.K, K8 = K >> 3, KP8 = (K8 + 63) & ~63;
     const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
     for (int i = t; i < R * K8; i += 256) {
@@ -130,13 +132,15 @@ __global__ void __launch_bounds__(256) k_gemv(GemvArgs a) {
     const bool holder = (lane % STRIDE) == 0;
     unsigned long long best = 0ull;
     for (int m = blockIdx.x * 8 + warp; m < Mout; m += gridDim.x * 8) {
-        float acc[NW][R][A];
+        float acc[NW][R][A], tot[NW][R];
 #pragma unroll
         for (int wr = 0; wr < NW; wr++)
 #pragma unroll
-            for (int r = 0; r < R; r++)
+            for (int r = 0; r < R; r++) {
+                tot[wr][r] = 0.f;
 #pragma unroll
                 for (int q = 0; q < A; q++) acc[wr][r][q] = 0.f;
+            }
         for (int g0 = 0; g0 < G; g0 += UG) {
             uint32_t wp[UG][NW][8];
 #pragma unroll
@@ -171,13 +175,21 @@ __global__ void __launch_bounds__(256) k_gemv(GemvArgs a) {
                     }
                 }
             }
+#pragma unroll
+            for (int wr = 0; wr < NW; wr++)
+#pragma unroll
+                for (int r = 0; r < R; r++) {
+                    tot[wr][r] = tot[wr][r] + (acc[wr][r][0] + acc[wr][r][1]);
+                    acc[wr][r][0] = 0.f;
+                    acc[wr][r][1] = 0.f;
+                }
         }
         float v[NV];
 #pragma unroll
         for (int wr = 0; wr < NW; wr++)
 #pragma unroll
             for (int r = 0; r < R; r++)
-                v[wr * R + r] = acc[wr][r][0] + acc[wr][r][1];
+                v[wr * R + r] = tot[wr][r];
         const float res = warp_reduce_transposed<NV>(v, lane);
         if (MODE == GEMV_SWIGLU) {
             const float u = __shfl_down_sync(FULL_MASK, res, 16);
@@ -380,14 +392,28 @@ __global__ void __launch_bounds__(128) k_qkv(QkvArgs a) {
 // local softmax statistics and the unnormalised P.V partial; k_attn_merge combines the splits
 // (log-sum-exp) and rounds to bf16 (Kernels.metal:440-562).
 constexpr int QS = 132;
+constexpr int AT = 64;  // keys per staged K / V tile
 
 int attention_per_max(int cap, int splits) { return ((cap + splits - 1) / splits + 31) & ~31; }
 size_t attention_smem(int H, int KV, int per_max) {
-    return sizeof(float) * (size_t(H) * QS + 32 * size_t(KV * 128 + 1) + size_t(H) * per_max);
+    return sizeof(float) * (size_t(H) * QS + size_t(AT) * (KV * 128 + 1) + size_t(AT) * 64 + size_t(H) * per_max) +
+           size_t(AT) * KV * 128 * 2;
+}
+
+// Stages rows [k0, k0 + tk) of the key (or value) cache window into shared memory as raw bf16 with
+// 16-byte loads: one round trip per tile.
+__device__ __forceinline__ void stage_rows(uint4* dst, const uint16_t* base, int first, int k0, int tk, int cap,
+                                           int KV) {
+    const int rowv = KV * 16;
+    for (int i = threadIdx.x; i < tk * rowv; i += blockDim.x) {
+        const int j = i / rowv, c = i - j * rowv;
+        const int phys = (first + k0 + j) % cap;
+        dst[i] = __ldg(reinterpret_cast<const uint4*>(base + size_t(phys) * KV * 128) + c);
+    }
 }
 
 __global__ void __launch_bounds__(256) k_attn_partial(AttnArgs a) {
-    extern __shared__ float smem[];
+    extern __shared__ __align__(16) float smem[];
     const int r = blockIdx.y, s = blockIdx.x, t = threadIdx.x;
     const RowGeo g = a.geo[r];
     const int lane_id = a.desc[r].lane;
@@ -401,38 +427,44 @@ __global__ void __launch_bounds__(256) k_attn_partial(AttnArgs a) {
         for (int h = t; h < H; h += 256) ml[h] = make_float2(-INFINITY, 0.f);
         return;
     }
-    float* qs = smem;
-    float* ks = qs + H * QS;
-    float* sc = ks + 32 * KS;
+    float* qs = smem;                                   // [H][QS]
+    float* kr = qs + H * QS;                            // [AT][KS] rotated keys (fp32)
+    uint32_t* rope = reinterpret_cast<uint32_t*>(kr + AT * KS);  // [AT][64]
+    float* sc = reinterpret_cast<float*>(rope + AT * 64);        // [H][per_max]
+    uint4* raw = reinterpret_cast<uint4*>(sc + H * a.per_max);   // [AT][KV*128] bf16
+    const uint16_t* raw16 = reinterpret_cast<const uint16_t*>(raw);
     const uint16_t* kbase = a.keys + size_t(lane_id) * a.lane_stride;
     const uint16_t* vbase = a.values + size_t(lane_id) * a.lane_stride;
     for (int i = t; i < H * 128; i += 256) qs[(i >> 7) * QS + (i & 127)] = bf2f(a.q[size_t(r) * H * 128 + i]);
     const int n = hi - lo;
-    for (int t0 = 0; t0 < n; t0 += 32) {
+    // pass 1: scores of every visible key of this split
+    for (int t0 = 0; t0 < n; t0 += AT) {
+        const int tk = min(AT, n - t0);
         __syncthreads();
-        const int tk = min(32, n - t0);
-        for (int i = t; i < 32 * KV * 128; i += 256) {
+        stage_rows(raw, kbase, g.first, lo + t0, tk, a.cap, KV);
+        if (!a.full)
+            for (int i = t; i < tk * 16; i += 256)
+                reinterpret_cast<uint4*>(rope)[i] =
+                    __ldg(reinterpret_cast<const uint4*>(a.rope_local + size_t(lo + t0 + (i >> 4)) * 64) + (i & 15));
+        __syncthreads();
+        for (int i = t; i < tk * KV * 128; i += 256) {
             const int j = i / (KV * 128), e = i - j * (KV * 128);
-            float val = 0.f;
-            if (j < tk) {
-                const int key = lo + t0 + j;
-                const int phys = (g.first + key) % a.cap;
-                const uint16_t* kr = kbase + size_t(phys) * KV * 128;
-                if (a.full) {
-                    val = bf2f(kr[e]);
-                } else {  // window-relative re-rotation of raw local keys (Kernels.metal:277-285)
-                    const int d = e & 127, kvoff = e - d, partner = d < 64 ? d + 64 : d - 64;
-                    val = rope_rotate(bf2f(kr[kvoff + d]), bf2f(kr[kvoff + partner]), d, a.rope_local[key * 64 + (d & 63)]);
-                }
+            const uint16_t* kr16 = raw16 + j * KV * 128;
+            float val;
+            if (a.full) {
+                val = bf2f(kr16[e]);
+            } else {  // window-relative re-rotation of raw local keys (Kernels.metal:277-285)
+                const int d = e & 127, kvoff = e - d, partner = d < 64 ? d + 64 : d - 64;
+                val = rope_rotate(bf2f(kr16[kvoff + d]), bf2f(kr16[kvoff + partner]), d, rope[j * 64 + (d & 63)]);
             }
-            ks[j * KS + e] = val;
+            kr[j * KS + e] = val;
         }
         __syncthreads();
-        const int j = t & 31;
+        const int j = t & (AT - 1);
         if (j < tk) {
-            for (int h = t >> 5; h < H; h += 8) {
+            for (int h = t >> 6; h < H; h += 4) {
                 const float* qh = qs + h * QS;
-                const float* kj = ks + j * KS + (h / group) * 128;
+                const float* kj = kr + j * KS + (h / group) * 128;
                 float acc = 0.f;
 #pragma unroll 16
                 for (int d = 0; d < 128; d++) acc = fmaf(qh[d], kj[d], acc);
@@ -441,6 +473,7 @@ __global__ void __launch_bounds__(256) k_attn_partial(AttnArgs a) {
         }
     }
     __syncthreads();
+    // pass 2: split-local softmax statistics per head
     const int warp = t >> 5, lane = t & 31;
     for (int h = warp; h < H; h += 8) {
         float* p = sc + h * a.per_max;
@@ -452,26 +485,31 @@ __global__ void __launch_bounds__(256) k_attn_partial(AttnArgs a) {
         l = warp_sum(l);
         if (lane == 0) ml[h] = make_float2(m, l);
     }
-    __syncthreads();
+    // pass 3: unnormalised P.V over staged value tiles
     const int d = t & 127, hh = t >> 7;
     float acc[16];
 #pragma unroll
     for (int q = 0; q < 16; q++) acc[q] = 0.f;
-    for (int i = 0; i < n; i++) {
-        const int phys = (g.first + lo + i) % a.cap;
-        const uint16_t* vr = vbase + size_t(phys) * KV * 128;
-        if (KV == 1) {
-            const float v = bf2f(vr[d]);
+    for (int t0 = 0; t0 < n; t0 += AT) {
+        const int tk = min(AT, n - t0);
+        __syncthreads();
+        stage_rows(raw, vbase, g.first, lo + t0, tk, a.cap, KV);
+        __syncthreads();
+        for (int i = 0; i < tk; i++) {
+            const uint16_t* vr = raw16 + i * KV * 128;
+            if (KV == 1) {
+                const float v = bf2f(vr[d]);
 #pragma unroll
-            for (int q = 0; q < 16; q++) {
-                const int h = hh + 2 * q;
-                if (h < H) acc[q] = fmaf(sc[h * a.per_max + i], v, acc[q]);
-            }
-        } else {
+                for (int q = 0; q < 16; q++) {
+                    const int h = hh + 2 * q;
+                    if (h < H) acc[q] = fmaf(sc[h * a.per_max + t0 + i], v, acc[q]);
+                }
+            } else {
 #pragma unroll
-            for (int q = 0; q < 16; q++) {
-                const int h = hh + 2 * q;
-                if (h < H) acc[q] = fmaf(sc[h * a.per_max + i], bf2f(vr[(h / group) * 128 + d]), acc[q]);
+                for (int q = 0; q < 16; q++) {
+                    const int h = hh + 2 * q;
+                    if (h < H) acc[q] = fmaf(sc[h * a.per_max + t0 + i], bf2f(vr[(h / group) * 128 + d]), acc[q]);
+                }
             }
         }
     }

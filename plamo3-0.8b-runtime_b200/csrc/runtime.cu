@@ -628,7 +628,7 @@ static int setup_runtime(plamo_runtime* rt, const ModelFiles* mf, bool upload, s
         L.full = c.is_global(i);
         L.cap = L.full ? rt->context : rt->local_cap;  // Runtime.swift:240
         // split-K width: ~64 keys per split for the local window, <= 256 keys for global history
-        L.splits = L.full ? std::max(32, (L.cap + 255) / 256) : std::max(1, std::min(32, (L.cap + 63) / 64));
+        L.splits = L.full ? std::max(32, (L.cap + 255) / 256) : std::max(1, (L.cap + 63) / 64);
         L.per_max = attention_per_max(L.cap, L.splits);
         max_splits = std::max(max_splits, L.splits);
         const size_t n = size_t(L.cap) * c.kv_heads * 128;
