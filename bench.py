@@ -12,8 +12,9 @@ from HBM; the 1.45 GB of weights are far larger than the 126 MB L2, so no flush 
          independent replicas (weak scaling), max time over ranks, value = N*K / time.
   e2e    the same metric through the public C ABI (plamo_forward per token: host id in via a
          pinned H2D copy, next id out via D2H), wall clock per call sequence.
-  roofline  the dominant kernel class (the projection GEMVs) timed live with CUDA events around
-         every launch; algorithmic bytes = weight bytes streamed per launch.
+  roofline  the dominant kernel timed live with CUDA events around every launch: the persistent
+         decode kernel (one launch per token) when it is active, else the projection GEMVs;
+         algorithmic bytes = weight bytes streamed per launch.
   cpu_baseline  the CPU restatement of the same forward (oracle/, OpenMP on all host cores) on a
          bounded sample of the same workload (rank 0, N=1).
 
@@ -277,14 +278,18 @@ def main():
     # ---- roofline of the dominant kernel class, timed live ---------------------------------
     prof = rt.profile_decode(args.profile_steps)
     wbytes = linear_bytes(model, args.packed)
-    gemv = prof["gemv"]
-    per_launch_bytes = (wbytes * args.profile_steps) / max(1, gemv["launches"])
-    per_launch_s = gemv["ms"] * 1e-3 / max(1, gemv["launches"])
+    # persistent path: one kernel per token streams every weight; multi-kernel path: the GEMVs
+    dom_key = "persistent" if "persistent" in prof else "gemv"
+    dom = prof[dom_key]
+    dom_name = ("k_decode_mega (persistent decode step: every projection, attention, norms, lm_head)"
+                if dom_key == "persistent" else "k_gemv (all projection GEMVs of a decode step)")
+    per_launch_bytes = (wbytes * args.profile_steps) / max(1, dom["launches"])
+    per_launch_s = dom["ms"] * 1e-3 / max(1, dom["launches"])
     pk = peaks()
     achieved = per_launch_bytes / per_launch_s / 1e9
     total_ms = sum(v["ms"] for v in prof.values())
     traffic = None
-    tf = REPO / "profiles" / ("gemv_decode_traffic_p12.json" if args.packed else "gemv_decode_traffic.json")
+    tf = REPO / "profiles" / f"{dom_key}_decode_traffic{'_p12' if args.packed else ''}.json"
     if tf.exists():
         traffic = json.loads(tf.read_text()).get("dram_bytes_per_launch")
 
@@ -322,7 +327,7 @@ def main():
             config=workload_config(args),
             e2e=dict(value=world * args.steps / e2e_elapsed, unit="tok/s", h2d_bytes_per_step=24, d2h_bytes_per_step=4),
             gpu_launches=launches * args.steps,
-            roofline=dict(bound="hbm", kernel="k_gemv (all projection GEMVs of a decode step)", achieved=achieved,
+            roofline=dict(bound="hbm", kernel=dom_name, achieved=achieved,
                           peak=pk["hbm"], unit="GB/s", frac=achieved / pk["hbm"], traffic=traffic,
                           peak_source=pk["source"], bytes_per_launch=per_launch_bytes,
                           launch_us=per_launch_s * 1e6,

@@ -110,14 +110,29 @@ PLAMO_API int plamo_batch_debug_kv(plamo_batch*, int layer, int lane, uint16_t* 
  * prediction. Writes the generated ids to out_ids. Equivalent to `steps` plamo_forward calls. */
 PLAMO_API int plamo_decode_chain(plamo_runtime*, int steps, int32_t* out_ids);
 
-/* Number of kernel launches in one batch-1 decode step (the nodes of the captured decode graph). */
+/* Number of kernel launches in one batch-1 decode step: 1 with the persistent decode kernel, else
+ * the nodes of the captured multi-kernel decode graph. */
 PLAMO_API int plamo_step_launches(plamo_runtime*);
 
-/* Profiling: runs `steps` batch-1 decode steps (as plamo_decode_chain, launched without the graph)
- * with every kernel launch bracketed by CUDA events. class_ms[5] / launches[5] receive the summed
- * device milliseconds and launch counts per kernel class: 0 GEMV (projections, lm_head), 1 QK-norm +
- * RoPE + KV append, 2 attention, 3 norms + embedding, 4 argmax finalisation. */
+/* 1 when batch-1 decode runs as one persistent cooperative kernel per token (the default on
+ * sm_100a; PLAMO_PERSISTENT=0 in the environment selects the multi-kernel graph instead). */
+PLAMO_API int plamo_persistent_decode(const plamo_runtime*);
+
+/* Profiling: runs `steps` batch-1 decode steps (as plamo_decode_chain) with every kernel launch
+ * bracketed by CUDA events. class_ms[6] / launches[6] receive the summed device milliseconds and
+ * launch counts per kernel class: 0 GEMV (projections, lm_head), 1 QK-norm + RoPE + KV append,
+ * 2 attention, 3 norms + embedding, 4 argmax finalisation (multi-kernel path), 5 the persistent
+ * decode kernel (whole step). */
 PLAMO_API int plamo_profile_decode(plamo_runtime*, int steps, double* class_ms, int32_t* launches);
+
+/* Tracing: one batch-1 decode step (as plamo_decode_chain with steps = 1) of the persistent decode
+ * kernel with its device timeline recorded. shape = {CTAs, phases, 3, D}; out receives, per CTA, per
+ * phase, the %globaltimer nanoseconds at [wait begin, work begin, work end], then one record per CTA
+ * [step begin, head epilogue begin, step end] — CTAs x (phases + 1) x 3 entries — followed by D
+ * stamps per CTA inside its first attention split of layer 0 (0 where unused); cap must hold
+ * CTAs x ((phases + 1) x 3 + D) entries. Phases per layer: QKV, attention, o_proj, gate/up (SwiGLU),
+ * down_proj; then the lm_head. */
+PLAMO_API int plamo_trace_decode(plamo_runtime*, uint64_t* out, size_t cap, int32_t* shape);
 
 PLAMO_API const char* plamo_last_error(void);
 

@@ -102,4 +102,53 @@ __device__ __forceinline__ uint32_t argmax_index(unsigned long long key) {
     return key == 0ull ? 0xffffffffu : 0xffffffffu - static_cast<uint32_t>(key & 0xffffffffull);
 }
 
+// Decodes 16 consecutive weights of one packed block into 8 bf16 pairs.
+// sm: 16 sign|mantissa bytes; codes: 16 4-bit exponent codes (low nibble first); minimum: block
+// minimum exponent (108..170). bits = (sm & 127) | (sm & 128) << 8 | (code == 15 ? 0 : min+code) << 7.
+__device__ __forceinline__ void decode16(uint4 sm, uint2 codes, uint32_t minimum, uint32_t (&wp)[8]) {
+    const uint32_t zx = ((codes.x & 0x77777777u) + 0x11111111u) & codes.x & 0x88888888u;
+    const uint32_t zy = ((codes.y & 0x77777777u) + 0x11111111u) & codes.y & 0x88888888u;
+    const uint32_t s[4] = {sm.x, sm.y, sm.z, sm.w};
+    if ((zx | zy) == 0u) {
+        // No signed-zero codes: two weights per 32-bit operation.
+        const uint32_t min7 = (minimum << 7) * 0x00010001u;
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            const uint32_t w = h ? codes.y : codes.x;
+            const uint32_t lo = w & 0x0F0F0F0Fu, hi = (w >> 4) & 0x0F0F0F0Fu;
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                // [code(2k) | 0 | code(2k+1) | 0] as two 16-bit halves (sign-replicate gives 0x00)
+                const uint32_t c2 = prmt(lo, hi, uint32_t(k) | (uint32_t(8 | k) << 4) | (uint32_t(4 + k) << 8) |
+                                                     (uint32_t(8 | (4 + k)) << 12));
+                const uint32_t e7 = c2 * 128u + min7;
+                const uint32_t p = 2u * (k & 1);
+                const uint32_t dup = prmt(s[2 * h + (k >> 1)], 0u, p | (p << 4) | ((p + 1) << 8) | ((p + 1) << 12));
+                wp[4 * h + k] = (dup & 0x807F807Fu) | e7;
+            }
+        }
+    } else {
+#pragma unroll
+        for (int e = 0; e < 16; e += 2) {
+            uint32_t out = 0;
+#pragma unroll
+            for (int q = 0; q < 2; q++) {
+                const uint32_t i = e + q;
+                const uint32_t b = (s[i >> 2] >> (8 * (i & 3))) & 255u;
+                const uint32_t cw = i < 8 ? codes.x : codes.y;
+                const uint32_t code = (cw >> (4 * (i & 7))) & 15u;
+                const uint32_t ex = code == 15u ? 0u : minimum + code;
+                out |= ((b & 127u) | ((b & 128u) << 8) | (ex << 7)) << (16 * q);
+            }
+            wp[e >> 1] = out;
+        }
+    }
+}
+
+// Rotate-half RoPE with a bf16 (cos, sin) pair (Kernels.metal:261-274).
+__device__ __forceinline__ float rope_rotate(float x, float other, int d, uint32_t cs) {
+    const float c = lo_bf(cs), s = hi_bf(cs);
+    return rbf(rbf(x * c) + rbf((d < 64 ? -other : other) * s));
+}
+
 }  // namespace plamo

@@ -31,49 +31,6 @@ __device__ __forceinline__ uint2 ld_stream2(const void* p) {
     return v;
 }
 
-// Decodes 16 consecutive weights of one packed block into 8 bf16 pairs.
-// sm: 16 sign|mantissa bytes; codes: 16 4-bit exponent codes (low nibble first); minimum: block
-// minimum exponent (108..170). bits = (sm & 127) | (sm & 128) << 8 | (code == 15 ? 0 : min+code) << 7.
-__device__ __forceinline__ void decode16(uint4 sm, uint2 codes, uint32_t minimum, uint32_t (&wp)[8]) {
-    const uint32_t zx = ((codes.x & 0x77777777u) + 0x11111111u) & codes.x & 0x88888888u;
-    const uint32_t zy = ((codes.y & 0x77777777u) + 0x11111111u) & codes.y & 0x88888888u;
-    const uint32_t s[4] = {sm.x, sm.y, sm.z, sm.w};
-    if ((zx | zy) == 0u) {
-        // No signed-zero codes: two weights per 32-bit operation.
-        const uint32_t min7 = (minimum << 7) * 0x00010001u;
-#pragma unroll
-        for (int h = 0; h < 2; h++) {
-            const uint32_t w = h ? codes.y : codes.x;
-            const uint32_t lo = w & 0x0F0F0F0Fu, hi = (w >> 4) & 0x0F0F0F0Fu;
-#pragma unroll
-            for (int k = 0; k < 4; k++) {
-                // [code(2k) | 0 | code(2k+1) | 0] as two 16-bit halves (sign-replicate gives 0x00)
-                const uint32_t c2 = prmt(lo, hi, uint32_t(k) | (uint32_t(8 | k) << 4) | (uint32_t(4 + k) << 8) |
-                                                     (uint32_t(8 | (4 + k)) << 12));
-                const uint32_t e7 = c2 * 128u + min7;
-                const uint32_t p = 2u * (k & 1);
-                const uint32_t dup = prmt(s[2 * h + (k >> 1)], 0u, p | (p << 4) | ((p + 1) << 8) | ((p + 1) << 12));
-                wp[4 * h + k] = (dup & 0x807F807Fu) | e7;
-            }
-        }
-    } else {
-#pragma unroll
-        for (int e = 0; e < 16; e += 2) {
-            uint32_t out = 0;
-#pragma unroll
-            for (int q = 0; q < 2; q++) {
-                const uint32_t i = e + q;
-                const uint32_t b = (s[i >> 2] >> (8 * (i & 3))) & 255u;
-                const uint32_t cw = i < 8 ? codes.x : codes.y;
-                const uint32_t code = (cw >> (4 * (i & 7))) & 15u;
-                const uint32_t ex = code == 15u ? 0u : minimum + code;
-                out |= ((b & 127u) | ((b & 128u) << 8) | (ex << 7)) << (16 * q);
-            }
-            wp[e >> 1] = out;
-        }
-    }
-}
-
 // 16 consecutive weights starting at flat element `el` (multiple of 16) as bf16 pairs.
 template <bool PACKED>
 __device__ __forceinline__ void load16(const Linear& lin, size_t el, uint32_t (&wp)[8]) {
@@ -329,11 +286,6 @@ __global__ void __launch_bounds__(256) k_embed_norm(const int* ids, int vocab, c
 }
 
 // --------------------------------------------------------------------------------------------
-// Rotate-half RoPE with a bf16 (cos, sin) pair (Kernels.metal:261-274).
-__device__ __forceinline__ float rope_rotate(float x, float other, int d, uint32_t cs) {
-    const float c = lo_bf(cs), s = hi_bf(cs);
-    return rbf(rbf(x * c) + rbf((d < 64 ? -other : other) * s));
-}
 
 // Per (row, head) warp: QK RMSNorm (w + 1), RoPE of queries, KV append into the ring slot
 // pos % cap of the row's lane slab (global layers store rotated keys, local layers raw keys).
@@ -539,14 +491,16 @@ __global__ void __launch_bounds__(128) k_attn_merge(AttnArgs a) {
 }
 
 // --------------------------------------------------------------------------------------------
-// Converts argmax keys to ids. Device-chained decode also feeds the id back as the next input,
-// advances the row descriptor and appends the id to a bounded history.
-__global__ void k_finalize(const unsigned long long* keys, const int* key_map, int rows, int* result,
+// Converts argmax keys to ids and clears each key after reading it (every forward leaves the keys
+// zeroed, whichever decode path runs next). Device-chained decode also feeds the id back as the
+// next input, advances the row descriptor and appends the id to a bounded history.
+__global__ void k_finalize(unsigned long long* keys, const int* key_map, int rows, int* result,
                            int* chain_ids, RowDesc* advance, int* hist, int* hist_count, int hist_cap) {
     const int r = threadIdx.x;
     if (r >= rows) return;
     const int k = key_map ? key_map[r] : r;
     const uint32_t id = argmax_index(keys[k]);
+    keys[k] = 0ull;
     result[k] = int(id);
     if (chain_ids) chain_ids[r] = int(id);
     if (advance) { advance[r].pos += 1; advance[r].cstart += 1; }
@@ -702,7 +656,7 @@ cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s) {
     return cudaGetLastError();
 }
 
-cudaError_t launch_finalize(const unsigned long long* keys, const int* key_map, int rows, int* result, int* chain_ids,
+cudaError_t launch_finalize(unsigned long long* keys, const int* key_map, int rows, int* result, int* chain_ids,
                             RowDesc* advance, int* hist, int* hist_count, int hist_cap, cudaStream_t s) {
     k_finalize<<<1, 64 * ((rows + 63) / 64), 0, s>>>(keys, key_map, rows, result, chain_ids, advance, hist, hist_count,
                                                       hist_cap);

@@ -84,7 +84,7 @@ cudaError_t launch_norm(const NormArgs& a, cudaStream_t s);
 cudaError_t launch_gemv(const GemvArgs& a, int mode, cudaStream_t s);
 cudaError_t launch_qkv(const QkvArgs& a, cudaStream_t s);
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s);
-cudaError_t launch_finalize(const unsigned long long* keys, const int* key_map, int rows, int* result,
+cudaError_t launch_finalize(unsigned long long* keys, const int* key_map, int rows, int* result,
                             int* chain_ids, RowDesc* advance, int* hist, int* hist_count, int hist_cap,
                             cudaStream_t s);
 cudaError_t launch_argmax(const uint16_t* logits, int rows, int n, unsigned long long* keys, uint32_t* out,

@@ -11,11 +11,13 @@
 #include "../../include/plamo.h"
 #include "kernels.h"
 #include "loader.h"
+#include "mega.h"
 
 #include <dlfcn.h>
 
 #include <algorithm>
 #include <chrono>
+#include <cstdlib>
 #include <cmath>
 #include <cstring>
 #include <mutex>
@@ -115,6 +117,15 @@ struct plamo_runtime {
     cudaEvent_t e0 = nullptr, e1 = nullptr;
     cudaGraphExec_t graph = nullptr;
     int step_launches = 0;
+    // persistent decode kernel (decode_mega.cu)
+    bool mega = false;
+    MegaArgs margs{};
+    uint64_t* trace = nullptr;  // phase timeline buffer (plamo_trace_decode), allocated on first use
+    int mega_grid = 0;
+    size_t mega_smem = 0;
+    cudaGraphExec_t mega_graph = nullptr;
+    bool mega_graph_tried = false;
+    int* h_error = nullptr;
     std::vector<void*> allocs, host_allocs;
 
     template <typename T>
@@ -139,6 +150,7 @@ struct plamo_runtime {
     }
     ~plamo_runtime() {
         if (graph) cudaGraphExecDestroy(graph);
+        if (mega_graph) cudaGraphExecDestroy(mega_graph);
         for (void* p : allocs) cudaFree(p);
         for (void* p : host_allocs) cudaFreeHost(p);
         if (e0) cudaEventDestroy(e0);
@@ -380,6 +392,162 @@ static int capture_decode_graph(plamo_runtime& rt) {
     return 0;
 }
 
+// Prepares the persistent decode kernel (decode_mega.cu): the phase table, per-row block offsets of
+// .p12 tensors, exchange buffers and counters. Leaves rt.mega false when the model shape does not
+// fit its shared-memory plan or cooperative launch is unavailable (the multi-kernel path remains).
+static int setup_mega(plamo_runtime& rt) {
+    const char* env = getenv("PLAMO_PERSISTENT");
+    if (env && env[0] == '0') return 0;
+    const Config& c = rt.c;
+    int dev = rt.device, sms = 0, coop = 0, optin = 0;
+    CK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    CK(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev));
+    CK(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
+    if (!coop || c.d > 4096 || c.heads > 16 || c.kv_heads > 8) return 0;
+    int per_max = 0, splits_max = 0;
+    for (const Layer& L : rt.layers) { per_max = std::max(per_max, L.per_max); splits_max = std::max(splits_max, L.splits); }
+    const int kmax = std::max(std::max(c.d, c.q_dim()), c.ffn);
+    const size_t smem = mega_smem_bytes(c.heads, c.kv_heads, per_max, kmax);
+    if (smem + 2048 > size_t(optin) || !mega_merge_fits(c.heads, c.kv_heads, splits_max)) return 0;
+    auto tile_rows = [](int K) { return mega_tile_rows(K); };
+    for (int K : {c.d, c.q_dim(), c.ffn})  // a tile holds at least one row; split rows take <= 8 warps
+        if (K * 2 > MEGA_SLOT_DATA || (K + 511) / 512 > 24 || mega_tile_rows(K) < 1) return 0;
+    // block-table copies must be 16-byte aligned and sized: rows x (K/128) x 4 bytes
+    auto table_ok = [&](int K, int tr, int up_rows) {
+        return (size_t(tr) * (K / 128) * 4) % 16 == 0 && (size_t(up_rows) * (K / 128) * 4) % 16 == 0;
+    };
+    if (rt.packed && !(table_ok(c.d, tile_rows(c.d), c.ffn) && table_ok(c.q_dim(), tile_rows(c.q_dim()), 0) &&
+                       table_ok(c.ffn, tile_rows(c.ffn), 0)))
+        return 0;
+    if (sms < c.heads) return 0;  // one merging CTA per head
+    if (configure_mega(smem, rt.packed, mega_npt(c.d)) != cudaSuccess) { cudaGetLastError(); return 0; }
+    // per-row first-block byte offsets of a packed matrix (M + 1 entries), from its block table
+    auto rowoff = [&](const Linear& lin, const uint32_t*& out) -> int {
+        out = nullptr;
+        if (!lin.offsets) return 0;
+        const size_t bpr = size_t(lin.K) / 128, blocks = size_t(lin.M) * bpr;
+        std::vector<uint32_t> tab(blocks);
+        CK(cudaMemcpy(tab.data(), lin.offsets, blocks * 4, cudaMemcpyDeviceToHost));
+        std::vector<uint32_t> ro(size_t(lin.M) + 1);
+        for (size_t m = 0; m < size_t(lin.M); m++) ro[m] = tab[m * bpr] & ~63u;
+        const uint32_t last = tab[blocks - 1];
+        ro[lin.M] = (last & ~63u) + ((last & 63u) ? 192u : 256u);
+        uint32_t* d = nullptr;
+        if (rt.dalloc(d, ro.size())) return 1;
+        CK(cudaMemcpy(d, ro.data(), ro.size() * 4, cudaMemcpyHostToDevice));
+        out = d;
+        return 0;
+    };
+    std::vector<MegaPhase> phases;
+    std::vector<MegaLayer> layers;
+    for (int l = 0; l < c.layers; l++) {
+        const Layer& L = rt.layers[l];
+        MegaLayer ml{L.pre_mixer, L.post_mixer, L.pre_mlp, L.post_mlp, L.q_norm, L.k_norm,
+                     L.keys, L.values, L.cap, L.splits, L.per_max, L.full ? 1 : 0};
+        layers.push_back(ml);
+        MegaPhase p{};
+        p.layer = l;
+        p.kind = MK_QKV; p.lin = L.qkv; p.out_rows = c.qkv_rows(); p.tile_rows = tile_rows(c.d);
+        if (rowoff(L.qkv, p.rowoff)) return 1;
+        phases.push_back(p);
+        p = MegaPhase{}; p.layer = l; p.kind = MK_ATT; phases.push_back(p);
+        p = MegaPhase{}; p.layer = l; p.kind = MK_O; p.lin = L.o; p.out_rows = c.d; p.tile_rows = tile_rows(c.q_dim());
+        if (rowoff(L.o, p.rowoff)) return 1;
+        phases.push_back(p);
+        p = MegaPhase{}; p.layer = l; p.kind = MK_GU; p.lin = L.gate_up; p.out_rows = c.ffn; p.tile_rows = tile_rows(c.d);
+        if (rowoff(L.gate_up, p.rowoff)) return 1;
+        phases.push_back(p);
+        p = MegaPhase{}; p.layer = l; p.kind = MK_DOWN; p.lin = L.down; p.out_rows = c.d; p.tile_rows = tile_rows(c.ffn);
+        if (rowoff(L.down, p.rowoff)) return 1;
+        phases.push_back(p);
+    }
+    MegaPhase hp{};
+    hp.kind = MK_HEAD; hp.layer = c.layers; hp.lin = rt.head; hp.out_rows = c.vocab; hp.tile_rows = tile_rows(c.d);
+    if (rowoff(rt.head, hp.rowoff)) return 1;
+    phases.push_back(hp);
+    MegaArgs& a = rt.margs;
+    MegaPhase* dph = nullptr;
+    MegaLayer* dly = nullptr;
+    if (rt.dalloc(dph, phases.size()) || rt.dalloc(dly, layers.size())) return 1;
+    CK(cudaMemcpy(dph, phases.data(), phases.size() * sizeof(MegaPhase), cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(dly, layers.data(), layers.size() * sizeof(MegaLayer), cudaMemcpyHostToDevice));
+    a.phases = dph;
+    a.nphases = int(phases.size());
+    a.layers = dly;
+    a.L = c.layers;
+    a.embed = rt.embed;
+    a.final_norm = rt.final_norm;
+    a.rope_local = rt.rope_local;
+    a.rope_global = rt.rope_global;
+    a.d = c.d; a.H = c.heads; a.KV = c.kv_heads; a.F = c.ffn; a.V = c.vocab; a.W = c.window;
+    a.post_mlp_offset = float(1.0 / std::pow(5.0, 1.5));
+    a.phases_packed = rt.packed;
+    a.attn_per_max = per_max;
+    a.xs_bytes = int(mega_xs_bytes(kmax));
+    const char* pf = getenv("PLAMO_PREFETCH_KB");
+    a.prefetch_bytes = (pf ? std::max(0, atoi(pf)) : 384) * 1024;
+    a.ids = rt.work.ids;
+    a.desc = rt.work.desc;
+    if (rt.dalloc(a.qkv, c.qkv_rows()) || rt.dalloc(a.att, c.q_dim()) ||
+        rt.dalloc(a.po, c.d) || rt.dalloc(a.pd, c.d) || rt.dalloc(a.act, c.ffn) ||
+        rt.dalloc(a.part_o, size_t(splits_max) * c.heads * 128) || rt.dalloc(a.part_ml, size_t(splits_max) * c.heads) ||
+        rt.dalloc(a.sync, size_t(a.nphases + a.L + 1)) || rt.dalloc(a.error, 1) || rt.halloc(rt.h_error, 1))
+        return 1;
+    a.logits = rt.out.logits;
+    a.hidden = rt.out.hidden;
+    a.amkey = rt.out.keys;
+    a.result = rt.out.result;
+    a.hist = rt.chain_hist;
+    a.hist_count = rt.chain_count;
+    a.hist_cap = rt.chain_cap;
+    *rt.h_error = 0;
+    if (mega_occupancy(smem, rt.packed, mega_npt(c.d)) < 1) return 0;  // a cooperative grid needs one CTA on every SM
+    rt.mega_grid = sms;
+    rt.mega_smem = smem;
+    rt.mega = true;
+    return 0;
+}
+
+// One cooperative launch of the persistent decode kernel; captured in a CUDA graph when the
+// driver allows cooperative launches in graphs, launched directly otherwise.
+static int mega_launch(plamo_runtime& rt) {
+    if (!rt.mega_graph && !rt.mega_graph_tried) {
+        rt.mega_graph_tried = true;
+        cudaGraph_t g = nullptr;
+        if (cudaStreamBeginCapture(rt.stream, cudaStreamCaptureModeThreadLocal) == cudaSuccess) {
+            const cudaError_t le = launch_mega(rt.margs, rt.mega_grid, rt.mega_smem, rt.stream);
+            const cudaError_t ce = cudaStreamEndCapture(rt.stream, &g);
+            if (le == cudaSuccess && ce == cudaSuccess && g && cudaGraphInstantiate(&rt.mega_graph, g, 0) != cudaSuccess)
+                rt.mega_graph = nullptr;
+            if (g) cudaGraphDestroy(g);
+            cudaGetLastError();  // a refused capture only means direct launches
+        }
+    }
+    if (rt.mega_graph) CK(cudaGraphLaunch(rt.mega_graph, rt.stream));
+    else CK(launch_mega(rt.margs, rt.mega_grid, rt.mega_smem, rt.stream));
+    return 0;
+}
+
+// One batch-1 decode step whose id / descriptor are already on the device.
+static int decode_step(plamo_runtime& rt) {
+    if (rt.mega) return mega_launch(rt);
+    if (!rt.graph && capture_decode_graph(rt)) return 1;
+    CK(cudaGraphLaunch(rt.graph, rt.stream));
+    return 0;
+}
+
+// After a synchronised persistent-kernel step: a bounded device wait that timed out aborts the
+// call with an error (and re-arms the counters), it never hangs the stream.
+static int mega_check(plamo_runtime& rt) {
+    if (!rt.mega || *rt.h_error == 0) return 0;
+    const int code = *rt.h_error;
+    *rt.h_error = 0;
+    cudaMemset(rt.margs.error, 0, sizeof(int));
+    cudaMemset(rt.margs.sync, 0, sizeof(unsigned) * size_t(rt.margs.nphases + rt.margs.L + 1));
+    cudaMemset(rt.margs.amkey, 0, sizeof(unsigned long long));
+    return fail("decode step aborted: a bounded device wait timed out (code " + std::to_string(code) + ")");
+}
+
 // Runtime.encode (Runtime.swift:327-467) for the scalar cache.
 static int forward_impl(plamo_runtime& rt, const int32_t* ids, int n, bool output, int32_t* next) {
     if (n < 1 || n > rt.chunk || rt.position + n > rt.context) return fail("Invalid tokens or context exhausted");
@@ -393,14 +561,16 @@ static int forward_impl(plamo_runtime& rt, const int32_t* ids, int n, bool outpu
     }
     if (upload_inputs(rt, w, n)) return 1;
     CK(cudaEventRecord(rt.e0, rt.stream));
-    if (n == 1 && output) {
-        if (!rt.graph && capture_decode_graph(rt)) return 1;
-        CK(cudaGraphLaunch(rt.graph, rt.stream));
+    const bool step = n == 1 && output;
+    if (step) {
+        if (decode_step(rt)) return 1;
+        if (rt.mega) CK(cudaMemcpyAsync(rt.h_error, rt.margs.error, sizeof(int), cudaMemcpyDeviceToHost, rt.stream));
     } else {
         if (enqueue_forward(rt, w, n, rt.cache, output ? 1 : 0, rt.out, false)) return 1;
     }
     if (output) CK(cudaMemcpyAsync(rt.out.h_result, rt.out.result, sizeof(int), cudaMemcpyDeviceToHost, rt.stream));
     if (finish(rt, &rt.gpu_seconds)) return 1;
+    if (step && mega_check(rt)) return 1;
     rt.position += n;
     rt.last_rows = output ? 1 : 0;
     if (output) rt.last_result = rt.out.h_result[0];
@@ -649,7 +819,7 @@ static int setup_runtime(plamo_runtime* rt, const ModelFiles* mf, bool upload, s
     rt->chain_cap = rt->context;
     if (rt->dalloc(rt->chain_hist, size_t(rt->chain_cap)) || rt->dalloc(rt->chain_count, 1)) return 1;
     CK(cudaMemset(rt->chain_count, 0, sizeof(int)));
-    return 0;
+    return setup_mega(*rt);
 }
 
 void plamo_close(plamo_runtime* rt) {
@@ -699,11 +869,14 @@ int plamo_decode_chain(plamo_runtime* rt, int steps, int32_t* out_ids) {
     w.h_out_map[0] = 0;
     if (upload_inputs(*rt, w, 1)) return 1;
     CK(cudaMemsetAsync(rt->chain_count, 0, sizeof(int), rt->stream));
-    if (!rt->graph && capture_decode_graph(*rt)) return 1;
+    if (!rt->mega && !rt->graph && capture_decode_graph(*rt)) return 1;
     CK(cudaEventRecord(rt->e0, rt->stream));
-    for (int i = 0; i < steps; i++) CK(cudaGraphLaunch(rt->graph, rt->stream));
+    for (int i = 0; i < steps; i++)
+        if (decode_step(*rt)) return 1;
+    if (rt->mega) CK(cudaMemcpyAsync(rt->h_error, rt->margs.error, sizeof(int), cudaMemcpyDeviceToHost, rt->stream));
     CK(cudaMemcpyAsync(out_ids, rt->chain_hist, sizeof(int) * steps, cudaMemcpyDeviceToHost, rt->stream));
     if (finish(*rt, &rt->gpu_seconds)) return 1;
+    if (mega_check(*rt)) return 1;
     rt->position += steps;
     rt->last_rows = 1;
     rt->last_result = out_ids[steps - 1];
@@ -713,9 +886,48 @@ int plamo_decode_chain(plamo_runtime* rt, int steps, int32_t* out_ids) {
 
 int plamo_step_launches(plamo_runtime* rt) {
     if (!rt) return 0;
+    if (rt->mega) return 1;
     cudaSetDevice(rt->device);
     if (!rt->graph && capture_decode_graph(*rt)) return -1;
     return rt->step_launches;
+}
+
+int plamo_persistent_decode(const plamo_runtime* rt) { return rt && rt->mega ? 1 : 0; }
+
+// One device-chained decode step of the persistent kernel with its phase timeline recorded
+// (launched directly, outside the captured graph, with the trace pointer set).
+int plamo_trace_decode(plamo_runtime* rt, uint64_t* out, size_t cap, int32_t* shape) {
+    if (!rt || !out || !shape) return fail("Invalid trace arguments");
+    if (!rt->mega) return fail("The persistent decode kernel is not active");
+    if (rt->last_rows < 1 || rt->position + 1 > rt->context) return fail("Invalid tokens or context exhausted");
+    const size_t per = size_t(rt->margs.nphases + 1) * MEGA_TRACE_STAMPS + MEGA_TRACE_DETAIL,
+                 n = per * size_t(rt->mega_grid);
+    shape[0] = rt->mega_grid;
+    shape[1] = rt->margs.nphases;
+    shape[2] = MEGA_TRACE_STAMPS;
+    shape[3] = MEGA_TRACE_DETAIL;
+    if (cap < n) return fail("Trace buffer too small: " + std::to_string(n) + " entries needed");
+    CK(cudaSetDevice(rt->device));
+    if (!rt->trace && rt->dalloc(rt->trace, n)) return 1;
+    Work& w = rt->work;
+    w.h_ids[0] = rt->last_result;
+    w.h_desc[0] = RowDesc{rt->position, 0, rt->position, 1};
+    w.h_out_map[0] = 0;
+    if (upload_inputs(*rt, w, 1)) return 1;
+    CK(cudaMemsetAsync(rt->chain_count, 0, sizeof(int), rt->stream));
+    CK(cudaMemsetAsync(rt->trace, 0, n * sizeof(uint64_t), rt->stream));
+    MegaArgs a = rt->margs;
+    a.trace = reinterpret_cast<unsigned long long*>(rt->trace);
+    CK(launch_mega(a, rt->mega_grid, rt->mega_smem, rt->stream));
+    CK(cudaMemcpyAsync(rt->h_error, rt->margs.error, sizeof(int), cudaMemcpyDeviceToHost, rt->stream));
+    CK(cudaStreamSynchronize(rt->stream));
+    if (mega_check(*rt)) return 1;
+    CK(cudaMemcpy(out, rt->trace, n * sizeof(uint64_t), cudaMemcpyDeviceToHost));
+    int last = 0;
+    CK(cudaMemcpy(&last, rt->chain_hist, sizeof(int), cudaMemcpyDeviceToHost));
+    rt->position += 1;
+    rt->last_result = last;
+    return 0;
 }
 
 // Runs `steps` batch-1 decode steps (same kernels as the decode graph, launched directly) with
@@ -731,6 +943,32 @@ int plamo_profile_decode(plamo_runtime* rt, int steps, double* class_ms, int32_t
     w.h_out_map[0] = 0;
     if (upload_inputs(*rt, w, 1)) return 1;
     CK(cudaMemsetAsync(rt->chain_count, 0, sizeof(int), rt->stream));
+    for (int c = 0; c <= K_CLASSES; c++) { class_ms[c] = 0; launches[c] = 0; }
+    if (rt->mega) {  // the persistent kernel is the whole step: time each launch
+        std::vector<cudaEvent_t> ev(2 * size_t(steps));
+        for (auto& e : ev) CK(cudaEventCreate(&e));
+        int rc = 0;
+        for (int i = 0; i < steps && !rc; i++) {
+            cudaEventRecord(ev[2 * i], rt->stream);
+            rc = mega_launch(*rt);
+            cudaEventRecord(ev[2 * i + 1], rt->stream);
+        }
+        if (!rc) CK(cudaMemcpyAsync(rt->h_error, rt->margs.error, sizeof(int), cudaMemcpyDeviceToHost, rt->stream));
+        if (!rc && cudaStreamSynchronize(rt->stream) != cudaSuccess) rc = fail("CUDA execution failed");
+        for (int i = 0; i < steps && !rc; i++) {
+            float ms = 0;
+            cudaEventElapsedTime(&ms, ev[2 * i], ev[2 * i + 1]);
+            class_ms[K_CLASSES] += ms;
+            launches[K_CLASSES] += 1;
+        }
+        for (auto& e : ev) cudaEventDestroy(e);
+        if (rc || mega_check(*rt)) return 1;
+        int last = 0;
+        CK(cudaMemcpy(&last, rt->chain_hist + (steps - 1), sizeof(int), cudaMemcpyDeviceToHost));
+        rt->position += steps;
+        rt->last_result = last;
+        return 0;
+    }
     Profiler prof;
     prof.on = true;
     g_prof = &prof;
@@ -738,7 +976,6 @@ int plamo_profile_decode(plamo_runtime* rt, int steps, double* class_ms, int32_t
     for (int i = 0; i < steps && !rc; i++) rc = enqueue_forward(*rt, w, 1, rt->cache, 1, rt->out, true);
     g_prof = nullptr;
     if (!rc && cudaStreamSynchronize(rt->stream) != cudaSuccess) rc = fail("CUDA execution failed");
-    for (int c = 0; c < K_CLASSES; c++) { class_ms[c] = 0; launches[c] = 0; }
     for (size_t i = 0; !rc && i < prof.cls.size(); i++) {
         float ms = 0;
         cudaEventElapsedTime(&ms, prof.ev[2 * i], prof.ev[2 * i + 1]);

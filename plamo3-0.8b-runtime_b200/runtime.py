@@ -90,6 +90,8 @@ def library() -> ctypes.CDLL:
         "plamo_decode_chain": (ctypes.c_int, [_vp, ctypes.c_int, _i32p]),
         "plamo_step_launches": (ctypes.c_int, [_vp]),
         "plamo_profile_decode": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.POINTER(ctypes.c_double), _i32p]),
+        "plamo_persistent_decode": (ctypes.c_int, [_vp]),
+        "plamo_trace_decode": (ctypes.c_int, [_vp, _vp, ctypes.c_size_t, _i32p]),
         "plamo_last_error": (ctypes.c_char_p, []),
         # kernel-level entry points (include/plamo_kernels.h)
         "plamo_k_linear": (ctypes.c_int, [_vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp, _vp, _vp]),
@@ -186,11 +188,38 @@ class Runtime:
 
     def profile_decode(self, steps: int):
         """Per-kernel-class device ms and launch counts over `steps` decode steps."""
-        ms = (ctypes.c_double * 5)()
-        n = np.zeros(5, dtype=np.int32)
+        ms = (ctypes.c_double * 6)()
+        n = np.zeros(6, dtype=np.int32)
         _check(library().plamo_profile_decode(self._h, int(steps), ms, n.ctypes.data_as(_i32p)))
-        names = ["gemv", "qkv", "attention", "norm", "argmax"]
-        return {k: dict(ms=float(ms[i]), launches=int(n[i])) for i, k in enumerate(names)}
+        names = ["gemv", "qkv", "attention", "norm", "argmax", "persistent"]
+        return {k: dict(ms=float(ms[i]), launches=int(n[i])) for i, k in enumerate(names) if n[i]}
+
+    def trace_decode(self):
+        """One decode step of the persistent kernel with its device timeline. Returns (phases,
+        detail): phases is [CTAs, phases + 1, 3] nanoseconds relative to the earliest step begin
+        (per phase [wait begin, work begin, work end]; the last record [step begin, head epilogue,
+        step end]); detail is [CTAs, D] stamps inside the CTA's first layer-0 attention split
+        (same origin; negative where unused)."""
+        shape = np.zeros(4, dtype=np.int32)
+        cap = 148 * 512 * 3
+        while True:
+            buf = np.zeros(cap, dtype=np.uint64)
+            rc = library().plamo_trace_decode(self._h, buf.ctypes.data_as(ctypes.c_void_p), cap, shape.ctypes.data_as(_i32p))
+            need = int(shape[0]) * ((int(shape[1]) + 1) * int(shape[2]) + int(shape[3]))
+            if rc != 0 and need > cap:
+                cap = need
+                continue
+            _check(rc)
+            break
+        G, P, S, D = (int(x) for x in shape)
+        t = buf[: G * (P + 1) * S].reshape(G, P + 1, S).astype(np.int64)
+        det = buf[G * (P + 1) * S: need].reshape(G, D).astype(np.int64)
+        origin = t[:, -1, 0].min()
+        return t - origin, np.where(det > 0, det - origin, -1)
+
+    @property
+    def persistent(self) -> bool:
+        return bool(library().plamo_persistent_decode(self._h))
 
     def logits(self, slot: int = 0) -> np.ndarray:
         out = np.empty(self.vocab, dtype=np.float32)

@@ -117,6 +117,33 @@ def test_decode_chain_equals_forward_loop(cuda, pkg, tiny_dir):
     assert rt.position == len(prompt) + 50
 
 
+@pytest.mark.parametrize("packed", [False, True])
+def test_persistent_equals_multikernel(cuda, pkg, tiny_dir, monkeypatch, packed):
+    """The persistent decode kernel (one cooperative launch per token) against the multi-kernel
+    graph of the same runtime: ids, logits, final hidden rows and KV caches bit-identical, through
+    prefill (multi-kernel chunks) followed by per-token steps and device-chained steps."""
+    mega = pkg.Runtime(tiny_dir, context=240, packed=packed)
+    monkeypatch.setenv("PLAMO_PERSISTENT", "0")
+    multi = pkg.Runtime(tiny_dir, context=240, packed=packed)
+    monkeypatch.delenv("PLAMO_PERSISTENT")
+    assert mega.persistent and not multi.persistent
+    assert mega.step_launches() == 1 and multi.step_launches() > 1
+    prompt = pkg.synthetic.seeded_tokens(45, mega.vocab, seed=4)
+    a, b = mega.prefill(prompt), multi.prefill(prompt)
+    for step in range(90):
+        assert a == b, step
+        assert np.array_equal(mega.logits().view(np.uint32), multi.logits().view(np.uint32)), step
+        assert np.array_equal(mega.hidden().view(np.uint32), multi.hidden().view(np.uint32)), step
+        a, b = mega.forward([a]), multi.forward([b])
+    assert mega.decode_chain(60) == multi.decode_chain(60)
+    for layer in range(mega.layers):
+        mk, mv = mega.debug_kv(layer)
+        gk, gv = multi.debug_kv(layer)
+        assert np.array_equal(mk, gk) and np.array_equal(mv, gv), layer
+    prof = mega.profile_decode(4)
+    assert set(prof) == {"persistent"} and prof["persistent"]["launches"] == 4
+
+
 def test_reset_and_errors(cuda, pkg, tiny_dir):
     """PlamoTests.swift:204-209 (reset gives bit-identical logits) and the API edge validation
     (Runtime.swift:328-330, :474)."""
