@@ -57,6 +57,20 @@ PLAMO_API int plamo_k_attention(const uint16_t* q, const uint16_t* keys, const u
                       int cap, int first, int count, int begin, int end, int full, const uint32_t* rope_local,
                       int splits, uint16_t* out, void* stream);
 
+/* plamo_k_attention without any device allocation. No counterpart in the reference (whose Metal
+ * encoder owns its buffers); for callers that must not allocate device memory during a call, such
+ * as a serving loop that reserved its memory up front and can afford neither an out-of-memory
+ * failure mid-stream nor the device-wide wait of the cudaFree with which plamo_k_attention grows
+ * its scratch. Same arguments and results as plamo_k_attention. The partial results live in one
+ * fixed 2 MiB device array per device (splits x heads at most 4032; larger requests fail with an
+ * error and launch nothing). The first call on a device looks the array up (cudaGetSymbolAddress,
+ * with that device current): make it before any stream capture. Calls are asynchronous on
+ * `stream` (they return once enqueued) and all calls on a device share the array, which keeps the
+ * last call's contents: calls whose execution may overlap (other streams, other threads) race. */
+PLAMO_API int plamo_k_attention_static(const uint16_t* q, const uint16_t* keys, const uint16_t* values, int heads,
+                                       int kv_heads, int cap, int first, int count, int begin, int end, int full,
+                                       const uint32_t* rope_local, int splits, uint16_t* out, void* stream);
+
 /* The fp32 exponential used by the softmax and SwiGLU kernels (Kernels.metal:209, :386 use exp):
  * y[i] = e^x[i] from IEEE operations only (Cody-Waite reduction, degree-7 Taylor polynomial), so a
  * CPU restatement reproduces it exactly. n floats, device pointers. */

@@ -34,6 +34,13 @@ __global__ void k_exp(const float* x, float* y, long long n) {
     if (i < n) y[i] = pexp(x[i]);
 }
 
+// Writes the row descriptor and window geometry of a single attention row into device memory;
+// they travel as kernel parameters, so no host buffer has to outlive the call.
+__global__ void k_set_attention_row(RowDesc* desc, RowGeo* geo, RowDesc d, RowGeo g) {
+    *desc = d;
+    *geo = g;
+}
+
 __global__ void k_keys_to_index(const unsigned long long* keys, int rows, uint32_t* out) {
     const int r = blockIdx.x * blockDim.x + threadIdx.x;
     if (r < rows) {
@@ -161,6 +168,68 @@ int plamo_k_attention(const uint16_t* q, const uint16_t* keys, const uint16_t* v
     if (e != cudaSuccess) return kfail(e);
     // the host-side descriptors must outlive the async copies
     e = cudaStreamSynchronize(s);
+    return e == cudaSuccess ? 0 : kfail(e);
+}
+
+// Fixed device scratch of plamo_k_attention_static: a file-scope device array (every device has
+// its own instance), found once per device with cudaGetSymbolAddress, shared by all calls on the
+// device. Layout: RowDesc at 0, RowGeo at 64, partial outputs at 256, then the (max, sum) pairs.
+constexpr size_t STATIC_ATTN_BYTES = size_t(2) << 20;
+static __device__ __align__(256) unsigned char g_attn_static[STATIC_ATTN_BYTES];
+static void* g_attn_static_ptr[64];
+static std::mutex g_attn_static_mu;
+
+int plamo_k_attention_static(const uint16_t* q, const uint16_t* keys, const uint16_t* values, int heads, int kv_heads,
+                             int cap, int first, int count, int begin, int end, int full, const uint32_t* rope_local,
+                             int splits, uint16_t* out, void* stream) {
+    if (!q || !keys || !values || !out || heads < 1 || heads > 32 || kv_heads < 1 || heads % kv_heads || cap < 1 ||
+        first < 0 || count < 1 || count > cap || begin < 0 || end > count || begin >= end || splits < 1 ||
+        splits > 4096 || (!full && !rope_local)) {
+        g_error = "Invalid attention arguments";
+        return 1;
+    }
+    const int per_max = attention_per_max(count, splits);
+    if (attention_smem(heads, kv_heads, per_max) > 200 * 1024) { g_error = "Too few attention splits"; return 1; }
+    const size_t part_o = size_t(splits) * heads * 128 * sizeof(float);
+    const size_t part_ml = size_t(splits) * heads * sizeof(float2);
+    if (256 + part_o + part_ml > STATIC_ATTN_BYTES) {
+        g_error = "Attention scratch exceeds the static 2 MiB buffer: splits x heads must be at most " +
+                  std::to_string((STATIC_ATTN_BYTES - 256) / (128 * sizeof(float) + sizeof(float2)));
+        return 1;
+    }
+    int dev = -1;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return kfail(e);
+    if (dev < 0 || dev >= 64) { g_error = "Device ordinal out of range"; return 1; }
+    if (!configured()) { g_error = "Cannot configure kernels"; return 1; }
+    void* scratch = nullptr;
+    {
+        std::lock_guard<std::mutex> lock(g_attn_static_mu);
+        if (!g_attn_static_ptr[dev]) {
+            void* p = nullptr;
+            e = cudaGetSymbolAddress(&p, g_attn_static);
+            if (e != cudaSuccess) return kfail(e);
+            g_attn_static_ptr[dev] = p;
+        }
+        scratch = g_attn_static_ptr[dev];
+    }
+    uint8_t* base = static_cast<uint8_t*>(scratch);
+    RowDesc* desc = reinterpret_cast<RowDesc*>(base);
+    RowGeo* geo = reinterpret_cast<RowGeo*>(base + 64);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    // every statistic the merge reads is written by the partial kernel of the same call (splits
+    // without visible keys write (-inf, 0) and their stale partial outputs are skipped), so the
+    // previous call's contents need no clearing
+    k_set_attention_row<<<1, 1, 0, s>>>(desc, geo, RowDesc{0, 0, 0, 1}, RowGeo{first, count, begin, end});
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return kfail(e);
+    AttnArgs a;
+    a.q = q; a.keys = keys; a.values = values; a.desc = desc; a.geo = geo; a.rope_local = rope_local;
+    a.part_o = reinterpret_cast<float*>(base + 256);
+    a.part_ml = reinterpret_cast<float2*>(base + 256 + part_o);
+    a.out = out; a.lane_stride = 0; a.rows = 1; a.H = heads; a.KV = kv_heads; a.cap = cap; a.full = full;
+    a.splits = splits; a.per_max = per_max;
+    e = launch_attention(a, s);
     return e == cudaSuccess ? 0 : kfail(e);
 }
 

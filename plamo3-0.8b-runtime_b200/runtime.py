@@ -100,6 +100,7 @@ def library() -> ctypes.CDLL:
         "plamo_k_argmax": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int, _vp, _vp, _vp]),
         "plamo_k_packed_decode": (ctypes.c_int, [_vp, _vp, ctypes.c_longlong, _vp, _vp]),
         "plamo_k_attention": (ctypes.c_int, [_vp, _vp, _vp] + [ctypes.c_int] * 8 + [_vp, ctypes.c_int, _vp, _vp]),
+        "plamo_k_attention_static": (ctypes.c_int, [_vp, _vp, _vp] + [ctypes.c_int] * 8 + [_vp, ctypes.c_int, _vp, _vp]),
         "plamo_k_exp": (ctypes.c_int, [_vp, _vp, ctypes.c_longlong, _vp]),
     }
     for name, (res, args) in sig.items():
@@ -381,6 +382,13 @@ def k_packed_decode(data, entries, count, out, stream=0):
 def k_attention(q, keys, values, heads, kv_heads, cap, first, count, begin, end, full, rope_local, splits, out, stream=0):
     _check(library().plamo_k_attention(q, keys, values, heads, kv_heads, cap, first, count, begin, end, int(full),
                                        rope_local or None, splits, out, stream or None))
+
+
+def k_attention_static(q, keys, values, heads, kv_heads, cap, first, count, begin, end, full, rope_local, splits, out,
+                       stream=0):
+    """plamo_k_attention on a fixed device scratch array (no device allocation; asynchronous)."""
+    _check(library().plamo_k_attention_static(q, keys, values, heads, kv_heads, cap, first, count, begin, end, int(full),
+                                              rope_local or None, splits, out, stream or None))
 
 
 def k_exp(x, y, n, stream=0):
