@@ -1,10 +1,13 @@
 // Persistent batch-1 decode step for sm_100a: one cooperative launch per token, one CTA per SM.
 //
-// Every CTA owns a contiguous share of the output rows of every projection. Its producer warp
-// streams the CTA's weight tiles for the whole step (all 16 layers and the lm_head) through a
-// 6-slot shared-memory ring with TMA bulk copies (cp.async.bulk + mbarrier complete_tx) and keeps
-// an L2 prefetch run-ahead, independently of the data dependencies, so HBM keeps streaming while
-// the consumer warps wait at phase boundaries. The 8 consumer warps run the phases of the step:
+// Every CTA owns a contiguous share of the output rows of every projection and streams its weight
+// tiles for the whole step (all 16 layers and the lm_head) through a 6-slot shared-memory ring
+// with TMA bulk copies (cp.async.bulk + mbarrier complete_tx). The ring runs ahead of the data
+// dependencies: the last of the 8 warps to release a slot refills it with the tile six ahead in
+// the step's order, so the next phase's first tiles are already resident while the warps wait at
+// a phase boundary. (No dedicated producer warp: with 8 warps every thread may hold 255
+// registers, with a ninth the register file's per-scheduler split would cap it at 168.) The 8
+// warps run the phases of the step:
 //   QKV  (prologue: residual + post-MLP norm of the previous layer, pre-mixer norm)  Runtime.swift:377,450
 //   ATT  (QK-norm + RoPE + KV append fused, split-K attention, merge by the last split) Kernels.metal:223-562
 //   O    (o_proj)                                                                      Runtime.swift:445
@@ -56,8 +59,13 @@ __device__ __forceinline__ void tma_load(void* dst, const void* src, uint32_t by
                  "l"(src), "r"(bytes), "r"(smem_u32(bar))
                  : "memory");
 }
-__device__ __forceinline__ void l2_prefetch(const void* src, uint32_t bytes) {
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+// Tiled tensor copy (3-D map, no multicast) global -> this CTA's shared memory, completion on `bar`.
+__device__ __forceinline__ void tma_load_3d(void* dst, const void* tmap, int c0, int c1, int c2, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(
+            smem_u32(dst)),
+        "l"(tmap), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
+        : "memory");
 }
 __device__ __forceinline__ void consumers_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 // orders this thread's earlier generic-proxy accesses (and the data it acquired) before its next
@@ -66,11 +74,11 @@ __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.
 __device__ __forceinline__ uint16_t ldcg16(const uint16_t* p) { return __ldcg(reinterpret_cast<const unsigned short*>(p)); }
 
 constexpr uint64_t WAIT_NS = 2000000000ull;  // every wait gives up after 2 s
-enum MegaError { ERR_PRODUCER = 11, ERR_CONSUMER = 12, ERR_COUNTER = 13, ERR_DRAIN = 14 };
+enum MegaError { ERR_CONSUMER = 12, ERR_COUNTER = 13, ERR_DRAIN = 14 };
 
 // The error flag and the clock are checked every 64 polls only: the flag is one global word that
 // every waiting warp of the grid would otherwise hammer.
-__device__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* error, int code) {
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* error, int code) {
     if (mbar_test(bar, parity)) return true;
     const uint64_t t0 = gtime();
     for (uint32_t i = 1;; i++) {
@@ -87,7 +95,7 @@ __device__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* error, int code) 
 
 // Waits for the completion of copies already issued into this CTA's shared memory before it
 // exits; bounded in time only (a copy from valid global memory always completes).
-__device__ void mbar_drain(uint64_t* bar, uint32_t parity, int* error) {
+__device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity, int* error) {
     const uint64_t t0 = gtime();
     while (!mbar_test(bar, parity)) {
         if (gtime() - t0 > WAIT_NS) {
@@ -97,7 +105,7 @@ __device__ void mbar_drain(uint64_t* bar, uint32_t parity, int* error) {
     }
 }
 
-__device__ bool counter_wait(const unsigned* c, unsigned target, int* error) {
+__device__ __forceinline__ bool counter_wait(const unsigned* c, unsigned target, int* error) {
     const uint64_t t0 = gtime();
     for (uint32_t i = 1;; i++) {
         unsigned v;
@@ -119,6 +127,7 @@ struct TileSpec {
     const uint8_t* data;
     const uint32_t* table;
     uint32_t data_bytes, table_bytes;
+    int row0;  // first weight row (tensor-map tiles)
 };
 
 __device__ __forceinline__ void block_range(int out_rows, int tile_rows, int cta, int G, int& b0, int& b1) {
@@ -133,9 +142,12 @@ __device__ __forceinline__ TileSpec tile_spec(const MegaPhase& ph, int block, in
     const int n = min(ph.tile_rows, ph.out_rows - r0);
     if (sub) r0 += ph.out_rows;  // up rows of the SwiGLU phase
     TileSpec t;
+    t.row0 = r0;
     if (!ph.lin.offsets) {
+        // raw weights come through the phase's swizzled tensor map as a full box of tile_rows
+        // rows (rows past the matrix are zero-filled and still counted)
         t.data = ph.lin.w + size_t(r0) * K * 2;
-        t.data_bytes = uint32_t(n) * K * 2;
+        t.data_bytes = uint32_t(ph.tile_rows) * K * 2;
         t.table = nullptr;
         t.table_bytes = 0;
     } else {
@@ -148,40 +160,44 @@ __device__ __forceinline__ TileSpec tile_spec(const MegaPhase& ph, int block, in
     return t;
 }
 
-// Walks this CTA's tiles of every weight phase in step order; holds a copy of the current phase
-// descriptor so that a tile costs no global read.
+// Walks this CTA's tiles of every weight phase in step order. Holds the current phase
+// descriptor and, loaded one phase early (nothing waits for it until the phase ends), the next
+// weight phase's, so advancing costs no global read on the critical path.
 struct Cursor {
-    MegaPhase ph;
+    MegaPhase ph, nxt;
     int p, b, b1, sub;
 };
 
-__device__ bool cursor_seek(const MegaArgs& a, Cursor& c, int cta, int G) {
-    while (c.p < a.nphases) {
-        const MegaPhase ph = a.phases[c.p];
-        if (ph.kind != MK_ATT) {
-            int b0, b1;
-            block_range(ph.out_rows, ph.tile_rows, cta, G, b0, b1);
-            if (b0 < b1) {
-                c.ph = ph;
-                c.b = b0;
-                c.b1 = b1;
-                c.sub = 0;
-                return true;
-            }
+// Enters weight phase q (descriptor phq) or the first later one with blocks for this CTA.
+__device__ __forceinline__ bool cursor_enter(const MegaArgs& a, Cursor& c, int q, MegaPhase phq, int cta, int G) {
+    while (q < a.nphases) {
+        int b0, b1;
+        block_range(phq.out_rows, phq.tile_rows, cta, G, b0, b1);
+        if (b0 < b1) {
+            c.p = q;
+            c.ph = phq;
+            c.b = b0;
+            c.b1 = b1;
+            c.sub = 0;
+            if (phq.next_weight < a.nphases) c.nxt = a.phases[phq.next_weight];
+            return true;
         }
-        c.p++;
+        q = phq.next_weight;
+        if (q < a.nphases) phq = a.phases[q];
     }
     return false;
 }
-__device__ bool cursor_next(const MegaArgs& a, Cursor& c, int cta, int G) {
+__device__ __forceinline__ bool cursor_seek(const MegaArgs& a, Cursor& c, int cta, int G) {
+    return a.nphases > 0 && cursor_enter(a, c, a.first_weight, a.phases[a.first_weight], cta, G);
+}
+__device__ __forceinline__ bool cursor_next(const MegaArgs& a, Cursor& c, int cta, int G) {
     if (c.ph.kind == MK_GU && c.sub == 0) {
         c.sub = 1;
         return true;
     }
     c.sub = 0;
     if (++c.b < c.b1) return true;
-    c.p++;
-    return cursor_seek(a, c, cta, G);
+    return c.ph.next_weight < a.nphases && cursor_enter(a, c, c.ph.next_weight, c.nxt, cta, G);
 }
 
 // ---- consumer building blocks (256 threads; same arithmetic order as kernels.cu) ----------------
@@ -239,81 +255,154 @@ __device__ __forceinline__ void stage_vec(uint16_t* xs, const uint16_t* src, int
     for (int i = threadIdx.x; i < n; i += 256) xs[xs_index(i)] = ldcg16(src + i);
 }
 
-// Lane partial of one weight row held in a ring slot, over the groups [gb, ge) of 512 weights
-// (lane l: elements g*512 + 16l .. +16), against the activations this lane holds in registers
-// (bf16 pairs xr[g - gb]). GEMV order of kernels.cu: two fma chains (even / odd elements) per 1536-weight
-// segment, segment sums folded in order into t (t = t + (a0 + a1)). With `raw_segment` the single
-// segment's a0 + a1 is returned instead (a warp computing one segment of a split row).
+// Both halves of a bf16 pair times the matching halves of x, accumulated into the even (lo) and
+// odd (hi) chains with sm_100's mixed-precision fma (bf16 x bf16 + f32, one rounding): the same
+// result as fmaf on the widened operands, without unpacking either pair.
+__device__ __forceinline__ void fma_bf16x2(uint32_t w, uint32_t x, float& lo, float& hi) {
+    asm("{\n .reg .b16 wl, wh, xl, xh;\n mov.b32 {wl, wh}, %2;\n mov.b32 {xl, xh}, %3;\n"
+        " fma.rn.f32.bf16 %0, wl, xl, %0;\n fma.rn.f32.bf16 %1, wh, xh, %1;\n}"
+        : "+f"(lo), "+f"(hi)
+        : "r"(w), "r"(x));
+}
+
+// The 16 weights of row r at element e0 of a ring tile, as 8 bf16 pairs (raw or .p12 blocks).
+// Raw tiles arrive 128-byte swizzled (the tensor map's SWIZZLE_128B on a 1024-byte aligned slot):
+// 16-byte chunk c of 128-byte line L sits at chunk c ^ (L & 7), so the two 16-byte reads of the
+// 8 lanes of each quarter-warp hit 8 distinct chunk positions (no bank conflict).
 template <bool PACKED>
-__device__ __forceinline__ float lane_partial(const uint8_t* tile, int r, int K, int gb, int ge, const uint32_t (&xr)[4][8],
-                                              bool raw_segment) {
+__device__ __forceinline__ void tile_w16(const uint8_t* tile, const uint32_t* tab, int r, int K, int e0, uint32_t (&wp)[8]) {
+    if (!PACKED) {
+        const uint32_t line = uint32_t(r) * uint32_t(K >> 6) + uint32_t(e0 >> 6), c = uint32_t(e0 & 63) >> 3;
+        const uint8_t* lb = tile + size_t(line) * 128;
+        const uint4 A = *reinterpret_cast<const uint4*>(lb + ((c ^ (line & 7u)) << 4));
+        const uint4 B = *reinterpret_cast<const uint4*>(lb + (((c + 1u) ^ (line & 7u)) << 4));
+        wp[0] = A.x; wp[1] = A.y; wp[2] = A.z; wp[3] = A.w;
+        wp[4] = B.x; wp[5] = B.y; wp[6] = B.z; wp[7] = B.w;
+    } else {
+        const uint32_t entry = tab[r * (K >> 7) + (e0 >> 7)];
+        const uint8_t* blk = tile + ((entry & ~63u) - (tab[0] & ~63u));
+        const uint32_t i0 = uint32_t(e0 & 127), tag = entry & 63u;
+        if (tag) {
+            decode16(*reinterpret_cast<const uint4*>(blk + i0), *reinterpret_cast<const uint2*>(blk + 128 + (i0 >> 1)),
+                     tag + 107u, wp);
+        } else {
+            const uint4 A = *reinterpret_cast<const uint4*>(blk + 2 * i0);
+            const uint4 B = *reinterpret_cast<const uint4*>(blk + 2 * i0 + 16);
+            wp[0] = A.x; wp[1] = A.y; wp[2] = A.z; wp[3] = A.w;
+            wp[4] = B.x; wp[5] = B.y; wp[6] = B.z; wp[7] = B.w;
+        }
+    }
+}
+
+// Lane partials of two weight rows (row rA of tile A, row rB of tile B; a row is skipped when its
+// flag is false) over the groups [gb, ge) of 512 weights (lane l: elements g*512 + 16l .. +16),
+// against the activations this lane holds in registers (bf16 pairs xr[g - gb]). The two rows
+// are independent chains computed side by side for instruction-level parallelism; each follows
+// the GEMV order of kernels.cu: two fma chains (even / odd elements) per 1536-weight segment,
+// segment sums folded in order (t = t + (a0 + a1)). With `raw_segment` the single segment's
+// a0 + a1 is returned instead (a warp computing one segment of a split row).
+template <bool PACKED>
+__device__ __forceinline__ void lane_partial2(const uint8_t* tA, const uint32_t* tabA, int rA, bool okA, const uint8_t* tB,
+                                              const uint32_t* tabB, int rB, bool okB, int K, int gb, int ge,
+                                              const uint32_t (&xr)[4][8], bool raw_segment, float& outA, float& outB) {
     const int lane = threadIdx.x & 31;
-    const uint8_t* row = tile + size_t(r) * K * 2;
-    const uint32_t* tab = reinterpret_cast<const uint32_t*>(tile + MEGA_SLOT_DATA);
-    const uint32_t base0 = PACKED ? (tab[0] & ~63u) : 0u;
-    const int bpr = K >> 7;
-    float t = 0.f, a0 = 0.f, a1 = 0.f, seg = 0.f;
+    float tA_ = 0.f, a0 = 0.f, a1 = 0.f, sA = 0.f;
+    float tB_ = 0.f, b0 = 0.f, b1 = 0.f, sB = 0.f;
 #pragma unroll
     for (int gi = 0; gi < 4; gi++) {
         const int g = gb + gi;
         if (g < ge) {
             const int e0 = g * 512 + lane * 16;
             if (e0 < K) {
-                uint32_t wp[8];
-                if (!PACKED) {
-                    const uint4 A = *reinterpret_cast<const uint4*>(row + e0 * 2);
-                    const uint4 B = *reinterpret_cast<const uint4*>(row + e0 * 2 + 16);
-                    wp[0] = A.x; wp[1] = A.y; wp[2] = A.z; wp[3] = A.w;
-                    wp[4] = B.x; wp[5] = B.y; wp[6] = B.z; wp[7] = B.w;
-                } else {
-                    const uint32_t entry = tab[r * bpr + (e0 >> 7)];
-                    const uint8_t* blk = tile + ((entry & ~63u) - base0);
-                    const uint32_t i0 = uint32_t(e0 & 127), tag = entry & 63u;
-                    if (tag) {
-                        decode16(*reinterpret_cast<const uint4*>(blk + i0), *reinterpret_cast<const uint2*>(blk + 128 + (i0 >> 1)),
-                                 tag + 107u, wp);
-                    } else {
-                        const uint4 A = *reinterpret_cast<const uint4*>(blk + 2 * i0);
-                        const uint4 B = *reinterpret_cast<const uint4*>(blk + 2 * i0 + 16);
-                        wp[0] = A.x; wp[1] = A.y; wp[2] = A.z; wp[3] = A.w;
-                        wp[4] = B.x; wp[5] = B.y; wp[6] = B.z; wp[7] = B.w;
-                    }
-                }
+                uint32_t wa[8], wb[8];
+                if (okA) tile_w16<PACKED>(tA, tabA, rA, K, e0, wa);
+                if (okB) tile_w16<PACKED>(tB, tabB, rB, K, e0, wb);
+                if (okA) {
 #pragma unroll
-                for (int k = 0; k < 8; k++) {
-                    a0 = fmaf(lo_bf(wp[k]), lo_bf(xr[gi][k]), a0);
-                    a1 = fmaf(hi_bf(wp[k]), hi_bf(xr[gi][k]), a1);
+                    for (int k = 0; k < 8; k++) {
+                        fma_bf16x2(wa[k], xr[gi][k], a0, a1);
+                        if (okB) fma_bf16x2(wb[k], xr[gi][k], b0, b1);
+                    }
+                } else if (okB) {
+#pragma unroll
+                    for (int k = 0; k < 8; k++) fma_bf16x2(wb[k], xr[gi][k], b0, b1);
                 }
             }
             if (gi == 2 || g == ge - 1) {  // end of a 1536-weight segment
-                seg = a0 + a1;
-                t = t + seg;
-                a0 = 0.f;
-                a1 = 0.f;
+                sA = a0 + a1;
+                tA_ = tA_ + sA;
+                sB = b0 + b1;
+                tB_ = tB_ + sB;
+                a0 = a1 = b0 = b1 = 0.f;
             }
         }
     }
-    return raw_segment ? seg : t;
+    outA = raw_segment ? sA : tA_;
+    outB = raw_segment ? sB : tB_;
 }
 
+// Two independent butterfly sums over the warp, interleaved.
+__device__ __forceinline__ void warp_sum2(float& x, float& y) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        x += __shfl_xor_sync(0xffffffffu, x, o);
+        y += __shfl_xor_sync(0xffffffffu, y, o);
+    }
+}
+
+// The CTA's weight ring as seen by one warp. Every warp consumes every tile in step order and
+// keeps an identical lead cursor on the tile MEGA_SLOTS ahead; the warp whose release completes
+// a slot's count (rel) issues that tile into the slot.
 struct ConsumerRing {
-    uint64_t* full;
-    uint64_t* empty;
-    uint8_t* ring;
+    uint64_t* full;    // [MEGA_SLOTS] tile landed (TMA complete_tx)
+    unsigned* rel;     // [MEGA_SLOTS] warps done with the slot's current tile
+    unsigned* issued;  // [MEGA_SLOTS] tiles issued into the slot so far (for the exit drain)
+    uint8_t* ring;     // [MEGA_SLOTS][MEGA_SLOT_DATA], 1024-byte aligned
+    uint8_t* tables;   // [MEGA_SLOTS][MEGA_TABLE_BYTES] .p12 block tables of the tiles
     int slot;
     uint32_t parity;  // bit i: phase parity of slot i's next fill
+    Cursor lead;      // the tile MEGA_SLOTS ahead of this warp's next one
+    bool lead_has;
 };
 
-// Output of row `row` (the full dot product v) of a weight phase.
-__device__ __forceinline__ void emit_row(const MegaArgs& a, int kind, int row, float v, int sub, float& gate,
+// Issues the weight tile at `c` into ring slot `slot` (one thread). The weights are never
+// written, and the slot's previous tile has been read by every warp (each warp's release follows
+// its last read of the slot), so no proxy fence is needed.
+__device__ __forceinline__ void issue_tile(const Cursor& c, uint8_t* ring, uint8_t* tables, uint64_t* full, int slot) {
+    const TileSpec ts = tile_spec(c.ph, c.b, c.sub);
+    mbar_expect_tx(&full[slot], ts.data_bytes + ts.table_bytes);
+    uint8_t* dst = ring + size_t(slot) * MEGA_SLOT_DATA;
+    if (c.ph.tmap) {
+        tma_load_3d(dst, c.ph.tmap, 0, 0, ts.row0, &full[slot]);
+    } else {
+        tma_load(dst, ts.data, ts.data_bytes, &full[slot]);
+        if (ts.table_bytes) tma_load(tables + size_t(slot) * MEGA_TABLE_BYTES, ts.table, ts.table_bytes, &full[slot]);
+    }
+}
+
+// The warp is done reading slot `s`: count the release; the 8th release refills the slot with
+// the lead tile. Every lane advances the lead cursor.
+__device__ __forceinline__ void release_slot(const MegaArgs& a, ConsumerRing& cr, int s) {
+    __syncwarp();
+    if ((threadIdx.x & 31) == 0) {
+        if (atomicAdd(&cr.rel[s], 1u) == 7u) {
+            cr.rel[s] = 0u;
+            if (cr.lead_has) {
+                issue_tile(cr.lead, cr.ring, cr.tables, cr.full, s);
+                cr.issued[s] += 1u;
+            }
+        }
+    }
+    if (cr.lead_has) cr.lead_has = cursor_next(a, cr.lead, blockIdx.x, gridDim.x);
+}
+
+// Output of row `row` (the full dot product v) of a weight phase. SwiGLU rows only park their
+// gate / up sums in shared memory (glu[2 * (row - row0) + sub]); the CTA finishes them together
+// at the end of the phase (swiglu_rows).
+__device__ __forceinline__ void emit_row(const MegaArgs& a, int kind, int row, float v, int sub, float* glu, int row0,
                                          unsigned long long* best) {
     if (kind == MK_GU) {
-        if (sub == 0) {
-            gate = v;
-        } else {
-            const float gq = rbf(gate), uq = rbf(v);
-            a.act[row] = uint16_t(f2bf(rbf(rbf(gq / (1.0f + pexp(-gq))) * uq)));
-        }
+        glu[2 * (row - row0) + sub] = v;
     } else if (kind == MK_HEAD) {
         const uint32_t bits = f2bf(v);
         a.logits[row] = uint16_t(bits);
@@ -325,16 +414,18 @@ __device__ __forceinline__ void emit_row(const MegaArgs& a, int kind, int row, f
     }
 }
 
-// One weight phase: every tile of this CTA's blocks, in the producer's order. Rows of up to 2048
-// weights: warp w computes row w of each tile alone. Longer rows (down_proj) are split into their
-// 1536-weight segments: warp w computes segment w % nseg of row w / nseg, the segment sums meet in
-// shared memory (double-buffered by tile) and warp r folds row r's sums in segment order, the
-// same arithmetic as one warp walking the whole row. After a timed-out wait the warp stops
-// computing but keeps walking the schedule (later waits fail at once, and split tiles still take
-// their barrier), so all consumer warps reach the phase end together.
+// One weight phase: every tile of this CTA's blocks, in the producer's order, two tiles at a
+// time (a SwiGLU block's gate and up tiles, otherwise consecutive blocks) so that every warp
+// carries two independent rows. Rows of up to 2048 weights: warp w computes row w of each tile.
+// Longer rows (down_proj) are split into their 1536-weight segments: warp w computes segment
+// w % nseg of row w / nseg, the segment sums meet in shared memory (double-buffered by pair) and
+// one warp per row folds them in segment order, the same arithmetic as one warp walking the
+// whole row. After a timed-out wait the warp stops computing but keeps walking the schedule
+// (later waits fail at once, and split pairs still take their barrier), so all consumer warps
+// reach the phase end together.
 template <bool PACKED>
-__device__ void gemv_phase(const MegaArgs& a, const MegaPhase& ph, ConsumerRing& cr, const uint16_t* xs, float* part,
-                           unsigned long long* best, unsigned long long* dt) {
+__device__ __forceinline__ void gemv_phase(const MegaArgs& a, const MegaPhase& ph, ConsumerRing& cr, const uint16_t* xs,
+                                           float* part, unsigned long long* best, unsigned long long* dt) {
     int nt = 0;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int K = ph.lin.K, G = (K + 511) >> 9;
@@ -358,39 +449,69 @@ __device__ void gemv_phase(const MegaArgs& a, const MegaPhase& ph, ConsumerRing&
     int b0, b1;
     block_range(ph.out_rows, ph.tile_rows, blockIdx.x, gridDim.x, b0, b1);
     const int nsub = ph.kind == MK_GU ? 2 : 1;
-    int k = 0;
-    for (int b = b0; b < b1; b++) {
-        const int n = min(ph.tile_rows, ph.out_rows - b * ph.tile_rows);
-        float gate = 0.f;
-        for (int sub = 0; sub < nsub; sub++, k++) {
-            const bool ready = mbar_wait(&cr.full[cr.slot], (cr.parity >> cr.slot) & 1u, a.error, ERR_CONSUMER);
-            if (dt && threadIdx.x == 0 && nt < 8) dt[nt++] = gtime();
-            const uint8_t* tile = cr.ring + size_t(cr.slot) * MEGA_SLOT_BYTES;
-            const int r = split ? warp / nseg : warp;
-            float v = 0.f;
-            if (ready && r < n) v = lane_partial<PACKED>(tile, r, K, gb, ge, xr, split);
-            if (ready) {
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&cr.empty[cr.slot]);
-                cr.parity ^= 1u << cr.slot;
-                cr.slot = cr.slot + 1 == MEGA_SLOTS ? 0 : cr.slot + 1;
+    const int T = (b1 - b0) * nsub;  // tiles of this CTA in this phase
+    const int r = split ? warp / nseg : warp;
+    const int row0 = b0 * ph.tile_rows;
+    float* glu = part + 2 * 512;  // [rows of this CTA][gate, up]
+    for (int k = 0, pair = 0; k < T; k += 2, pair++) {
+        const bool two = k + 1 < T;
+        const int bA = b0 + k / nsub, subA = k % nsub;
+        const int bB = b0 + (k + 1) / nsub, subB = (k + 1) % nsub;
+        const int nA = min(ph.tile_rows, ph.out_rows - bA * ph.tile_rows);
+        const int nB = two ? min(ph.tile_rows, ph.out_rows - bB * ph.tile_rows) : 0;
+        const int sA = cr.slot, sB = cr.slot + 1 == MEGA_SLOTS ? 0 : cr.slot + 1;
+        const bool readyA = mbar_wait(&cr.full[sA], (cr.parity >> sA) & 1u, a.error, ERR_CONSUMER);
+        const bool readyB = two && mbar_wait(&cr.full[sB], (cr.parity >> sB) & 1u, a.error, ERR_CONSUMER);
+        const bool stamp = dt && threadIdx.x == 0 && nt < 4;
+        if (stamp) dt[nt * 4] = gtime();
+        const uint8_t* tA = cr.ring + size_t(sA) * MEGA_SLOT_DATA;
+        const uint8_t* tB = cr.ring + size_t(sB) * MEGA_SLOT_DATA;
+        const uint32_t* tabA = reinterpret_cast<const uint32_t*>(cr.tables + size_t(sA) * MEGA_TABLE_BYTES);
+        const uint32_t* tabB = reinterpret_cast<const uint32_t*>(cr.tables + size_t(sB) * MEGA_TABLE_BYTES);
+        float vA = 0.f, vB = 0.f;
+        lane_partial2<PACKED>(tA, tabA, r, readyA && r < nA, tB, tabB, r, readyB && r < nB, K, gb, ge, xr, split, vA, vB);
+        if (stamp) dt[nt * 4 + 1] = gtime();
+        if (readyA) {
+            release_slot(a, cr, sA);
+            cr.parity ^= 1u << sA;
+            cr.slot = sB;
+        }
+        if (readyB) {
+            release_slot(a, cr, sB);
+            cr.parity ^= 1u << sB;
+            cr.slot = sB + 1 == MEGA_SLOTS ? 0 : sB + 1;
+        }
+        if (!split) {
+            warp_sum2(vA, vB);
+            if (stamp) dt[nt * 4 + 2] = gtime();
+            if (lane == 0) {
+                if (readyA && r < nA) emit_row(a, ph.kind, bA * ph.tile_rows + r, vA, subA, glu, row0, best);
+                if (readyB && r < nB) emit_row(a, ph.kind, bB * ph.tile_rows + r, vB, subB, glu, row0, best);
             }
-            if (!split) {
-                if (ready && r < n) {
-                    v = warp_sum(v);
-                    if (lane == 0) emit_row(a, ph.kind, b * ph.tile_rows + r, v, sub, gate, best);
-                }
-                continue;
-            }
-            float* pk = part + (k & 1) * 256;
-            pk[warp * 32 + lane] = v;
-            consumers_sync();
-            if (warp < n) {
-                float t = 0.f;
-                for (int sgi = 0; sgi < nseg; sgi++) t = t + pk[(warp * nseg + sgi) * 32 + lane];
-                t = warp_sum(t);
-                if (lane == 0) emit_row(a, ph.kind, b * ph.tile_rows + warp, t, sub, gate, best);
-            }
+            if (stamp) dt[nt++ * 4 + 3] = gtime();
+            continue;
+        }
+        float* pk = part + (pair & 1) * 512;  // [tile A | tile B][warp][lane]
+        pk[warp * 32 + lane] = vA;
+        pk[256 + warp * 32 + lane] = vB;
+        consumers_sync();
+        // warp w folds the pair's row w: rows 0..nA-1 of tile A, then rows of tile B
+        const bool inA = warp < nA, inB = !inA && warp < nA + nB;
+        if (inA || inB) {
+            const int rr = inA ? warp : warp - nA;
+            const float* src = pk + (inA ? 0 : 256) + rr * nseg * 32 + lane;
+            float t = 0.f;
+            for (int sgi = 0; sgi < nseg; sgi++) t = t + src[sgi * 32];
+            t = warp_sum(t);
+            if (lane == 0) emit_row(a, ph.kind, (inA ? bA : bB) * ph.tile_rows + rr, t, inA ? subA : subB, glu, row0, best);
+        }
+    }
+    if (ph.kind == MK_GU) {  // SwiGLU of this CTA's rows (Kernels.metal:202-210), all threads at once
+        consumers_sync();
+        const int nrows = min(ph.out_rows, b1 * ph.tile_rows) - row0;
+        for (int i = threadIdx.x; i < nrows; i += 256) {
+            const float gq = rbf(glu[2 * i]), uq = rbf(glu[2 * i + 1]);
+            a.act[row0 + i] = uint16_t(f2bf(rbf(rbf(gq / (1.0f + pexp(-gq))) * uq)));
         }
     }
 }
@@ -516,7 +637,7 @@ __device__ __forceinline__ void issue_tile(const MegaArgs& a, void* dst, const u
 // weights are only 2-byte aligned). Issued before the wait for the QKV phase so the copies
 // overlap it; thread 0, the waiting thread, issues nothing. The plain stores are read after the
 // next consumer barrier.
-__device__ void attention_prefetch(const MegaArgs& a, const MegaLayer& Ly, const SplitGeo& g, const AttnSmem& sm,
+__device__ __forceinline__ void attention_prefetch(const MegaArgs& a, const MegaLayer& Ly, const SplitGeo& g, const AttnSmem& sm,
                                    AttnBars& ab) {
     const int t = threadIdx.x;
     if (g.lo >= g.hi) return;
@@ -537,7 +658,7 @@ __device__ void attention_prefetch(const MegaArgs& a, const MegaLayer& Ly, const
 // queries, the append of this step's key/value by the split that holds it, scores, split-local
 // softmax statistics and the unnormalised P.V partial. Expects attention_prefetch's copies issued
 // and a consumer barrier after it.
-__device__ void attention_split(const MegaArgs& a, const MegaLayer& Ly, const SplitGeo& g, int s, const AttnSmem& sm,
+__device__ __forceinline__ void attention_split(const MegaArgs& a, const MegaLayer& Ly, const SplitGeo& g, int s, const AttnSmem& sm,
                                 AttnBars& ab, unsigned long long* dt) {
     const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
     const int H = a.H, KV = a.KV, group = H / KV, cap = Ly.cap, per_max = Ly.per_max;
@@ -557,7 +678,10 @@ __device__ void attention_split(const MegaArgs& a, const MegaLayer& Ly, const Sp
         tma_load(qkvs, a.qkv, bytes, &ab.bar[AB_Q]);
     }
     ab.pending |= 1u << AB_Q;
-    if (dt) dt[0] = gtime();
+    if (dt) {
+        dt[0] = gtime();
+        dt[9] = clock64();
+    }
     ab_wait(a, ab, AB_Q);
     if (dt) dt[1] = gtime();
     ab_wait(a, ab, AB_K);
@@ -621,17 +745,24 @@ __device__ void attention_split(const MegaArgs& a, const MegaLayer& Ly, const Sp
             ab.pending |= 1u << AB_K;
             ab_wait(a, ab, AB_K);
         }
-        for (int i = t; i < tk * kvw; i += 256) {
-            const int j = KV == 1 ? i >> 7 : i / kvw, e = i - j * kvw;
-            const uint16_t* k16 = t0 + j == jnew ? sm.knew : raw16 + j * kvw;
-            uint16_t val;
-            if (full) {
-                val = k16[e];
-            } else {  // window-relative re-rotation of raw local keys (Kernels.metal:277-285)
-                const int d = e & 127, kvoff = e - d, partner = d < 64 ? d + 64 : d - 64;
-                val = uint16_t(f2bf(rope_rotate(bf2f(k16[kvoff + d]), bf2f(k16[kvoff + partner]), d, sm.rope[j * 64 + (d & 63)])));
+        // rotated keys into the padded tile: local keys get the window-relative RoPE
+        // (Kernels.metal:277-285), one thread per (d, d + 64) pair; global keys are copied
+        if (full) {
+            for (int i = t; i < tk * KV * 16; i += 256) {
+                const int j = i / (KV * 16), c = i - j * (KV * 16);
+                const uint16_t* k16 = t0 + j == jnew ? sm.knew : raw16 + j * kvw;
+                reinterpret_cast<uint4*>(sm.kr + j * KS)[c] = reinterpret_cast<const uint4*>(k16)[c];
             }
-            sm.kr[j * KS + e] = val;
+        } else {
+            for (int i = t; i < tk * KV * 64; i += 256) {
+                const int j = KV == 1 ? i >> 6 : i / (KV * 64), e = i - j * (KV * 64);
+                const int d = e & 63, kvoff = (e >> 6) * 128;
+                const uint16_t* k16 = (t0 + j == jnew ? sm.knew : raw16 + j * kvw) + kvoff;
+                const uint32_t cs = sm.rope[j * 64 + d];
+                const float x1 = bf2f(k16[d]), x2 = bf2f(k16[d + 64]);
+                sm.kr[j * KS + kvoff + d] = uint16_t(f2bf(rope_rotate(x1, x2, d, cs)));
+                sm.kr[j * KS + kvoff + d + 64] = uint16_t(f2bf(rope_rotate(x2, x1, d + 64, cs)));
+            }
         }
         consumers_sync();
         if (dt) dt[4] = gtime();
@@ -639,41 +770,74 @@ __device__ void attention_split(const MegaArgs& a, const MegaLayer& Ly, const Sp
             if (t == ISSUER) issue_tile(a, sm.raw, Ly.values, g, 0, min(ATM, n), cap, nullptr, &ab.bar[AB_V]);
             ab.pending |= 1u << AB_V;
         }
-        const int j = t & (ATM - 1);
+        // scores: thread (key j, head quarter hq) computes heads hq, hq + 4, hq + 8, hq + 12 side by
+        // side, each one fma chain over d = 0..127 as the multi-kernel path
+        const int j = t & (ATM - 1), hq = t >> 6;
         if (j < tk) {
-            for (int h = t >> 6; h < H; h += 4) {
-                const float4* q4 = reinterpret_cast<const float4*>(sm.qs + h * QSM);
-                const uint4* k4 = reinterpret_cast<const uint4*>(sm.kr + j * KS + (h / group) * 128);
-                float acc = 0.f;  // one chain over d = 0..127, as the multi-kernel path
-#pragma unroll 4
-                for (int c = 0; c < 16; c++) {
-                    const uint4 kk = k4[c];
-                    const float4 qa = q4[2 * c], qb = q4[2 * c + 1];
-                    acc = fmaf(qa.x, lo_bf(kk.x), acc);
-                    acc = fmaf(qa.y, hi_bf(kk.x), acc);
-                    acc = fmaf(qa.z, lo_bf(kk.y), acc);
-                    acc = fmaf(qa.w, hi_bf(kk.y), acc);
-                    acc = fmaf(qb.x, lo_bf(kk.z), acc);
-                    acc = fmaf(qb.y, hi_bf(kk.z), acc);
-                    acc = fmaf(qb.z, lo_bf(kk.w), acc);
-                    acc = fmaf(qb.w, hi_bf(kk.w), acc);
-                }
-                sm.sc[h * per_max + t0 + j] = acc * PLAMO_ATTN_SCALE;
+            const float4* q4[4];
+            const uint4* k4[4];
+            float acc[4];
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const int h = min(hq + 4 * u, H - 1);
+                q4[u] = reinterpret_cast<const float4*>(sm.qs + h * QSM);
+                k4[u] = reinterpret_cast<const uint4*>(sm.kr + j * KS + (h / group) * 128);
+                acc[u] = 0.f;
             }
+#pragma unroll 2
+            for (int c = 0; c < 16; c++) {
+#pragma unroll
+                for (int u = 0; u < 4; u++) {
+                    const uint4 kk = KV == 1 ? k4[0][c] : k4[u][c];
+                    const float4 qa = q4[u][2 * c], qb = q4[u][2 * c + 1];
+                    acc[u] = fmaf(qa.x, lo_bf(kk.x), acc[u]);
+                    acc[u] = fmaf(qa.y, hi_bf(kk.x), acc[u]);
+                    acc[u] = fmaf(qa.z, lo_bf(kk.y), acc[u]);
+                    acc[u] = fmaf(qa.w, hi_bf(kk.y), acc[u]);
+                    acc[u] = fmaf(qb.x, lo_bf(kk.z), acc[u]);
+                    acc[u] = fmaf(qb.y, hi_bf(kk.z), acc[u]);
+                    acc[u] = fmaf(qb.z, lo_bf(kk.w), acc[u]);
+                    acc[u] = fmaf(qb.w, hi_bf(kk.w), acc[u]);
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < 4; u++)
+                if (hq + 4 * u < H) sm.sc[(hq + 4 * u) * per_max + t0 + j] = acc[u] * PLAMO_ATTN_SCALE;
         }
     }
     consumers_sync();
     if (dt) dt[5] = gtime();
-    // pass 2: split-local softmax statistics
-    for (int h = warp; h < H; h += 8) {
-        float* pr = sm.sc + h * per_max;
-        float m = -INFINITY;
-        for (int i = lane; i < n; i += 32) m = fmaxf(m, pr[i]);
-        m = warp_max(m);
-        float lsum = 0.f;
-        for (int i = lane; i < n; i += 32) { const float e = pexp(pr[i] - m); pr[i] = e; lsum += e; }
-        lsum = warp_sum(lsum);
-        if (lane == 0) ml[h] = make_float2(m, lsum);
+    // pass 2: split-local softmax statistics; warp w handles heads w and w + 8 side by side
+    {
+        const int h0 = warp, h1 = min(warp + 8, H - 1);
+        const bool two = warp + 8 < H;
+        if (h0 < H) {
+            float* p0 = sm.sc + h0 * per_max;
+            float* p1 = sm.sc + h1 * per_max;
+            float m0 = -INFINITY, m1 = -INFINITY;
+            for (int i = lane; i < n; i += 32) {
+                m0 = fmaxf(m0, p0[i]);
+                m1 = fmaxf(m1, p1[i]);
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                m0 = fmaxf(m0, __shfl_xor_sync(0xffffffffu, m0, o));
+                m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, o));
+            }
+            float l0 = 0.f, l1 = 0.f;
+            for (int i = lane; i < n; i += 32) {
+                const float e0 = pexp(p0[i] - m0), e1 = pexp(p1[i] - m1);
+                l0 += e0;
+                l1 += e1;
+                p0[i] = e0;
+                if (two) p1[i] = e1;
+            }
+            warp_sum2(l0, l1);
+            if (lane == 0) {
+                ml[h0] = make_float2(m0, l0);
+                if (two) ml[h1] = make_float2(m1, l1);
+            }
+        }
     }
     consumers_sync();
     if (dt) dt[6] = gtime();
@@ -693,7 +857,11 @@ __device__ void attention_split(const MegaArgs& a, const MegaLayer& Ly, const Sp
         }
         ab_wait(a, ab, AB_V);
         if (dt) dt[7] = gtime();
-        const float* sct = sm.sc + hh * per_max + t0;
+        // probability rows of this thread's heads (clamped to a valid row; results of heads >= H
+        // are never stored)
+        const float* pq[8];
+#pragma unroll
+        for (int q = 0; q < 8; q++) pq[q] = sm.sc + min(hh + 2 * q, H - 1) * per_max + t0;
         if (KV == 1) {
             int i = 0;
             for (; i + 4 <= tk; i += 4) {  // four keys per round: 16-byte probability loads
@@ -702,22 +870,20 @@ __device__ void attention_split(const MegaArgs& a, const MegaLayer& Ly, const Sp
                 for (int u = 0; u < 4; u++) v[u] = bf2f((t0 + i + u == jnew ? sm.vnew : raw16 + (i + u) * 128)[d]);
 #pragma unroll
                 for (int q = 0; q < 8; q++) {
-                    if (hh + 2 * q < H) {
-                        const float4 pr = *reinterpret_cast<const float4*>(sct + 2 * q * per_max + i);
-                        acc[q] = fmaf(pr.x, v[0], acc[q]);
-                        acc[q] = fmaf(pr.y, v[1], acc[q]);
-                        acc[q] = fmaf(pr.z, v[2], acc[q]);
-                        acc[q] = fmaf(pr.w, v[3], acc[q]);
-                    }
+                    const float4 pr = *reinterpret_cast<const float4*>(pq[q] + i);
+                    acc[q] = fmaf(pr.x, v[0], acc[q]);
+                    acc[q] = fmaf(pr.y, v[1], acc[q]);
+                    acc[q] = fmaf(pr.z, v[2], acc[q]);
+                    acc[q] = fmaf(pr.w, v[3], acc[q]);
                 }
             }
             for (; i < tk; i++) {
                 const float v = bf2f((t0 + i == jnew ? sm.vnew : raw16 + i * 128)[d]);
 #pragma unroll
-                for (int q = 0; q < 8; q++)
-                    if (hh + 2 * q < H) acc[q] = fmaf(sct[2 * q * per_max + i], v, acc[q]);
+                for (int q = 0; q < 8; q++) acc[q] = fmaf(pq[q][i], v, acc[q]);
             }
         } else {
+            const float* sct = sm.sc + hh * per_max + t0;
             for (int i = 0; i < tk; i++) {
                 const uint16_t* vr = t0 + i == jnew ? sm.vnew : raw16 + i * kvw;
 #pragma unroll
@@ -731,7 +897,10 @@ __device__ void attention_split(const MegaArgs& a, const MegaLayer& Ly, const Sp
 #pragma unroll
     for (int q = 0; q < 8; q++)
         if (hh + 2 * q < H) po[(hh + 2 * q) * 128 + d] = acc[q];
-    if (dt) dt[8] = gtime();
+    if (dt) {
+        dt[8] = gtime();
+        dt[10] = clock64();
+    }
 }
 
 // Merge of head h over the layer's S split partials (Kernels.metal:530-562), run by CTA h once
@@ -741,7 +910,7 @@ __device__ void attention_split(const MegaArgs& a, const MegaLayer& Ly, const Sp
 // first batch together with the statistics loads. Returns false when the wait for the splits
 // gave up.
 constexpr int MERGE_CHUNK = 64;
-__device__ bool attention_merge_head(const MegaArgs& a, int S, int l, int h, const AttnSmem& sm, AttnBars& ab) {
+__device__ __forceinline__ bool attention_merge_head(const MegaArgs& a, int S, int l, int h, const AttnSmem& sm, AttnBars& ab) {
     const int t = threadIdx.x, H = a.H, d = t & 127;
     __shared__ int merge_stop;
     if (t == 0) merge_stop = counter_wait(&a.sync[a.nphases + l], unsigned(S), a.error) ? 0 : 1;
@@ -807,8 +976,10 @@ size_t mega_xs_bytes(int kmax) { return size_t(((kmax + 511) / 512) * 512) * 2; 
 
 size_t mega_smem_bytes(int H, int KV, int per_max, int kmax) {
     const size_t head = 256;  // mbarriers + reduction scratch
-    const size_t ring = size_t(MEGA_SLOTS) * MEGA_SLOT_BYTES;
-    const size_t gemv = mega_xs_bytes(kmax) + 2 * 256 * 4;  // activations + split-row segment sums
+    // ring data 1024-byte aligned (up to 1 KB of padding) + block tables
+    const size_t ring = 1024 + size_t(MEGA_SLOTS) * (MEGA_SLOT_DATA + MEGA_TABLE_BYTES);
+    // activations + split-row segment sums + SwiGLU gate/up sums of this CTA's rows
+    const size_t gemv = mega_xs_bytes(kmax) + 2 * 512 * 4 + size_t(2) * MEGA_GLU_ROWS * 4;
     return head + ring + std::max(gemv, mega_attention_smem(H, KV, per_max));
 }
 
@@ -816,72 +987,49 @@ size_t mega_smem_bytes(int H, int KV, int per_max, int kmax) {
 template <bool PACKED, int NPT>
 __global__ void __launch_bounds__(MEGA_THREADS, 1) k_decode_mega(MegaArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem);
-    uint64_t* empty = full + MEGA_SLOTS;
-    uint64_t* abar = full + 2 * MEGA_SLOTS;  // [4] attention copy barriers
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem);        // [6] at 0
+    uint64_t* abar = full + MEGA_SLOTS;                         // [4] attention copy barriers at 48
+    unsigned* rel = reinterpret_cast<unsigned*>(smem + 80);     // [6] slot release counts
+    unsigned* issued = reinterpret_cast<unsigned*>(smem + 104); // [6] tiles issued per slot
     float* red = reinterpret_cast<float*>(smem + 128);
-    uint8_t* ring = smem + 256;
-    uint8_t* uni = ring + size_t(MEGA_SLOTS) * MEGA_SLOT_BYTES;
+    // ring slots on a 1024-byte boundary (the 128-byte swizzle pattern repeats every 1024 bytes)
+    uint8_t* ring = smem + 256 + ((1024u - ((smem_u32(smem) + 256u) & 1023u)) & 1023u);
+    uint8_t* tables = ring + size_t(MEGA_SLOTS) * MEGA_SLOT_DATA;
+    uint8_t* uni = tables + size_t(MEGA_SLOTS) * MEGA_TABLE_BYTES;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int G = gridDim.x, cta = blockIdx.x;
+    // ring: every thread walks the tile order; thread 0 issues the first MEGA_SLOTS tiles
+    ConsumerRing cr;
+    cr.full = full;
+    cr.rel = rel;
+    cr.issued = issued;
+    cr.ring = ring;
+    cr.tables = tables;
+    cr.slot = 0;
+    cr.parity = 0;
+    cr.lead_has = cursor_seek(a, cr.lead, cta, G);
     if (threadIdx.x == 0) {
         for (int i = 0; i < MEGA_SLOTS; i++) {
             mbar_init(&full[i], 1);
-            mbar_init(&empty[i], 8);
+            rel[i] = 0u;
+            issued[i] = 0u;
         }
         for (int i = 0; i < 4; i++) mbar_init(&abar[i], 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();
-
-    if (warp == 8) {  // ------------------------------------------------------------ producer
-        if (lane != 0) return;
-        uint32_t parity = 0, used = 0;  // bit i: fills of slot i so far (odd count / any)
-        Cursor cur;
-        cur.p = 0;
-        bool has = cursor_seek(a, cur, cta, G);
-        Cursor pf = cur;
-        bool pf_has = has;
-        uint32_t ahead = 0;  // bytes prefetched into L2 and not yet copied into the ring
-        int nissued = 0;     // (tracing) tiles of the first SwiGLU phase issued
-        int slot = 0;
-        while (has) {
-            while (pf_has && ahead < uint32_t(a.prefetch_bytes)) {
-                const TileSpec ts = tile_spec(pf.ph, pf.b, pf.sub);
-                l2_prefetch(ts.data, ts.data_bytes);
-                pf_has = cursor_next(a, pf, cta, G);
-                ahead += ts.data_bytes;
-            }
-            if (!mbar_wait(&empty[slot], ((parity >> slot) & 1u) ^ 1u, a.error, ERR_PRODUCER)) break;
-            const TileSpec ts = tile_spec(cur.ph, cur.b, cur.sub);
-            if (a.trace && cur.ph.kind == MK_GU && cur.ph.layer == 0 && nissued < 8)
-                a.trace[size_t(G) * (a.nphases + 1) * MEGA_TRACE_STAMPS + size_t(cta) * MEGA_TRACE_DETAIL + 24 + nissued++] = gtime();
-            mbar_expect_tx(&full[slot], ts.data_bytes + ts.table_bytes);
-            uint8_t* dst = ring + size_t(slot) * MEGA_SLOT_BYTES;
-            tma_load(dst, ts.data, ts.data_bytes, &full[slot]);
-            if (ts.table_bytes) tma_load(dst + MEGA_SLOT_DATA, ts.table, ts.table_bytes, &full[slot]);
-            parity ^= 1u << slot;
-            used |= 1u << slot;
-            slot = slot + 1 == MEGA_SLOTS ? 0 : slot + 1;
-            ahead = ahead > ts.data_bytes ? ahead - ts.data_bytes : 0u;
-            has = cursor_next(a, cur, cta, G);
+    for (int i = 0; i < MEGA_SLOTS && cr.lead_has; i++) {
+        if (threadIdx.x == 0) {
+            issue_tile(cr.lead, ring, tables, full, i);
+            issued[i] = 1u;
         }
-        // drain: every copy issued into this CTA's shared memory has landed before the CTA exits
-        for (int i = 0; i < MEGA_SLOTS; i++)
-            if ((used >> i) & 1u) mbar_drain(&full[i], ((parity >> i) & 1u) ^ 1u, a.error);
-        return;
+        cr.lead_has = cursor_next(a, cr.lead, cta, G);
     }
 
     // ----------------------------------------------------------------------------- consumers
     const int t = threadIdx.x;
     unsigned long long* trace = a.trace && t == 0 ? a.trace + size_t(cta) * (a.nphases + 1) * MEGA_TRACE_STAMPS : nullptr;
     if (trace) trace[a.nphases * MEGA_TRACE_STAMPS] = gtime();
-    ConsumerRing cr;
-    cr.full = full;
-    cr.empty = empty;
-    cr.ring = ring;
-    cr.slot = 0;
-    cr.parity = 0;
     uint16_t* xs = reinterpret_cast<uint16_t*>(uni);
     const AttnSmem asm_ = attn_smem(uni, a);
     AttnBars ab{abar, 0u, 0u};
@@ -1015,10 +1163,15 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_decode_mega(MegaArgs a) {
         }
     }
     // no bulk copy may still be writing this CTA's shared memory when its threads exit (only an
-    // aborted step can leave one pending)
-    if (t == 0)
+    // aborted step can leave one pending): wait for the last tile issued into every ring slot and
+    // for the attention copies still outstanding
+    consumers_sync();
+    if (t == 0) {
+        for (int i = 0; i < MEGA_SLOTS; i++)
+            if (issued[i]) mbar_drain(&full[i], (issued[i] - 1u) & 1u, a.error);
         for (int i = 0; i < 4; i++)
             if ((ab.pending >> i) & 1u) mbar_drain(&abar[i], (ab.parity >> i) & 1u, a.error);
+    }
     if (!ok) return;
     // head epilogue: CTA argmax -> global key; the last CTA finishes the step and resets the counters
     if (trace) trace[a.nphases * MEGA_TRACE_STAMPS + 1] = gtime();

@@ -15,6 +15,8 @@ struct MegaPhase {
     const uint32_t* rowoff;  // .p12: byte offset of each row's first block in the data region (M+1)
     int out_rows;            // outputs of the phase (SwiGLU: F)
     int tile_rows;           // weight rows per tile
+    int next_weight;         // index of the next weight (non-attention) phase; nphases after the last
+    const void* tmap;        // raw weights: 3-D tensor map [rows][K/64][64] bf16, 128-byte swizzle (device memory)
 };
 
 struct MegaLayer {
@@ -26,6 +28,7 @@ struct MegaLayer {
 struct MegaArgs {
     const MegaPhase* phases;
     int nphases;
+    int first_weight;  // index of the first weight phase
     const MegaLayer* layers;
     int L;
     const uint16_t* embed;
@@ -36,7 +39,6 @@ struct MegaArgs {
     float post_mlp_offset;  // 1 / 5^1.5 (Runtime.swift:450)
     bool phases_packed;     // weights are .p12 tensors
     int attn_per_max;       // largest split width over the layers (shared-memory layout)
-    int prefetch_bytes;     // L2 prefetch run-ahead of each CTA's weight stream
     int xs_bytes;           // staged activations at the start of the union region; split-row sums follow
     int* ids;          // [1] input token (device-chained: written by the previous step)
     RowDesc* desc;     // [1] position of the token (advanced by the step)
@@ -58,12 +60,13 @@ struct MegaArgs {
 };
 constexpr int MEGA_TRACE_STAMPS = 3;
 constexpr int MEGA_TRACE_DETAIL = 32;  // per CTA, after the phase records: stamps inside the first attention split,
-                                       // then the first SwiGLU phase's tile arrivals and issues
+                                       // then stamps of the first SwiGLU phase's tile pairs
 
-constexpr int MEGA_THREADS = 288;  // 8 consumer warps + 1 producer warp
+constexpr int MEGA_THREADS = 256;  // 8 warps (2 per scheduler: up to 255 registers each)
 constexpr int MEGA_SLOTS = 6;
-constexpr int MEGA_SLOT_DATA = 24576;
-constexpr int MEGA_SLOT_BYTES = MEGA_SLOT_DATA + 512;
+constexpr int MEGA_SLOT_DATA = 24576;    // weight bytes per ring slot (a multiple of 1024)
+constexpr int MEGA_TABLE_BYTES = 512;    // .p12 block-table bytes per ring slot
+constexpr int MEGA_GLU_ROWS = 512;  // SwiGLU rows one CTA may own
 
 size_t mega_attention_smem(int H, int KV, int per_max);
 size_t mega_smem_bytes(int H, int KV, int per_max, int kmax);

@@ -13,6 +13,8 @@
 #include "loader.h"
 #include "mega.h"
 
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <dlfcn.h>
 
 #include <algorithm>
@@ -393,6 +395,21 @@ static int capture_decode_graph(plamo_runtime& rt) {
 }
 
 // Prepares the persistent decode kernel (decode_mega.cu): the phase table, per-row block offsets of
+// cuTensorMapEncodeTiled from the driver, found through the runtime (no link against libcuda).
+static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static std::once_flag once;
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    cudaGetLastError();
+    return fn;
+}
+
 // .p12 tensors, exchange buffers and counters. Leaves rt.mega false when the model shape does not
 // fit its shared-memory plan or cooperative launch is unavailable (the multi-kernel path remains).
 static int setup_mega(plamo_runtime& rt) {
@@ -420,6 +437,10 @@ static int setup_mega(plamo_runtime& rt) {
                        table_ok(c.ffn, tile_rows(c.ffn), 0)))
         return 0;
     if (sms < c.heads) return 0;  // one merging CTA per head
+    {  // SwiGLU rows per CTA fit the gate/up buffer
+        const int tr = mega_tile_rows(c.d), nb = (c.ffn + tr - 1) / tr;
+        if ((nb + sms - 1) / sms * tr > MEGA_GLU_ROWS) return 0;
+    }
     if (configure_mega(smem, rt.packed, mega_npt(c.d)) != cudaSuccess) { cudaGetLastError(); return 0; }
     // per-row first-block byte offsets of a packed matrix (M + 1 entries), from its block table
     auto rowoff = [&](const Linear& lin, const uint32_t*& out) -> int {
@@ -465,6 +486,37 @@ static int setup_mega(plamo_runtime& rt) {
     hp.kind = MK_HEAD; hp.layer = c.layers; hp.lin = rt.head; hp.out_rows = c.vocab; hp.tile_rows = tile_rows(c.d);
     if (rowoff(rt.head, hp.rowoff)) return 1;
     phases.push_back(hp);
+    {  // link every phase to the next weight phase (the weight stream skips attention phases)
+        int nextw = int(phases.size());
+        for (int i = int(phases.size()) - 1; i >= 0; i--) {
+            phases[i].next_weight = nextw;
+            if (phases[i].kind != MK_ATT) nextw = i;
+        }
+        rt.margs.first_weight = nextw;
+    }
+    if (!rt.packed) {  // raw weights stream through swizzled tensor maps: [rows][K/64][64] bf16
+        PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
+        if (!encode) return 0;
+        std::vector<CUtensorMap> maps(phases.size());
+        for (size_t i = 0; i < phases.size(); i++) {
+            const MegaPhase& ph = phases[i];
+            if (ph.kind == MK_ATT) continue;
+            const cuuint64_t dims[3] = {64, cuuint64_t(ph.lin.K / 64), cuuint64_t(ph.lin.M)};
+            const cuuint64_t strides[2] = {128, cuuint64_t(ph.lin.K) * 2};
+            const cuuint32_t box[3] = {64, cuuint32_t(ph.lin.K / 64), cuuint32_t(ph.tile_rows)};
+            const cuuint32_t unit[3] = {1, 1, 1};
+            if (ph.lin.K % 64 || ph.lin.K / 64 > 256 ||
+                encode(&maps[i], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<uint8_t*>(ph.lin.w), dims, strides, box,
+                       unit, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+                return 0;
+        }
+        CUtensorMap* dmaps = nullptr;
+        if (rt.dalloc(dmaps, maps.size())) return 1;
+        CK(cudaMemcpy(dmaps, maps.data(), maps.size() * sizeof(CUtensorMap), cudaMemcpyHostToDevice));
+        for (size_t i = 0; i < phases.size(); i++)
+            if (phases[i].kind != MK_ATT) phases[i].tmap = dmaps + i;
+    }
     MegaArgs& a = rt.margs;
     MegaPhase* dph = nullptr;
     MegaLayer* dly = nullptr;
@@ -484,8 +536,6 @@ static int setup_mega(plamo_runtime& rt) {
     a.phases_packed = rt.packed;
     a.attn_per_max = per_max;
     a.xs_bytes = int(mega_xs_bytes(kmax));
-    const char* pf = getenv("PLAMO_PREFETCH_KB");
-    a.prefetch_bytes = (pf ? std::max(0, atoi(pf)) : 384) * 1024;
     a.ids = rt.work.ids;
     a.desc = rt.work.desc;
     if (rt.dalloc(a.qkv, c.qkv_rows()) || rt.dalloc(a.att, c.q_dim()) ||
