@@ -1,5 +1,7 @@
 // Kernel launch interface shared by the runtime (runtime.cu) and the kernel-level C ABI.
 #pragma once
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cstdint>
 #include <cuda_runtime.h>
 
@@ -82,6 +84,12 @@ cudaError_t launch_embed_norm(const int* ids, int rows, int vocab, const uint16_
                               int nkeys, cudaStream_t s);
 cudaError_t launch_norm(const NormArgs& a, cudaStream_t s);
 cudaError_t launch_gemv(const GemvArgs& a, int mode, cudaStream_t s);
+// cuTensorMapEncodeTiled from the driver, found through the runtime (no link against libcuda).
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();
+// Tiled order-exact GEMM (gemm.cu) for more than 16 rows of raw weights; launch_gemv uses it.
+bool gemm_supported(const GemvArgs& a);
+cudaError_t launch_gemm(const GemvArgs& a, GemvMode mode, cudaStream_t s);
+cudaError_t configure_gemm();
 cudaError_t launch_qkv(const QkvArgs& a, cudaStream_t s);
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s);
 cudaError_t launch_finalize(unsigned long long* keys, const int* key_map, int rows, int* result,

@@ -207,10 +207,14 @@ static int pin_alloc(Owner& o, T*& p, size_t count) {
     return 0;
 }
 
+// Attention runs over at most ATT_ROWS rows per launch, so its split partials are sized for them
+// (a wide prefill would otherwise need rows x splits x heads x 128 floats at once).
+constexpr int ATT_ROWS = 64;
+
 template <typename Owner>
 static int alloc_work(Owner& o, plamo_runtime& rt, Work& w, int rows) {
     const Config& c = rt.c;
-    const size_t R = size_t(rows);
+    const size_t R = size_t(rows), RA = size_t(std::min(rows, ATT_ROWS));
     int max_splits = 1;
     for (const Layer& L : rt.layers) max_splits = std::max(max_splits, L.splits);
     w.rows_cap = rows;
@@ -218,7 +222,7 @@ static int alloc_work(Owner& o, plamo_runtime& rt, Work& w, int rows) {
         dev_alloc(o, rt, w.q, R * c.q_dim()) || dev_alloc(o, rt, w.att, R * c.q_dim()) || dev_alloc(o, rt, w.proj, R * c.d) ||
         dev_alloc(o, rt, w.act, R * c.ffn) || dev_alloc(o, rt, w.geo, R) || dev_alloc(o, rt, w.desc, R) ||
         dev_alloc(o, rt, w.ids, R) || dev_alloc(o, rt, w.out_map, R) ||
-        dev_alloc(o, rt, w.part_o, R * max_splits * c.heads * 128) || dev_alloc(o, rt, w.part_ml, R * max_splits * c.heads) ||
+        dev_alloc(o, rt, w.part_o, RA * max_splits * c.heads * 128) || dev_alloc(o, rt, w.part_ml, RA * max_splits * c.heads) ||
         pin_alloc(o, w.h_desc, R) || pin_alloc(o, w.h_ids, R) || pin_alloc(o, w.h_out_map, R))
         return 1;
     return 0;
@@ -304,14 +308,14 @@ static int prof_end(cudaStream_t s, int cls) {
 
 // ------------------------------------------------------------------------------------------------
 // One decoder pass over `rows` rows whose ids / descriptors / output map are already on the device.
-// out_mode: 0 = no head, 1 = head on the last row only (Runtime.swift:453-458), 2 = head on every
-// row (Batch.swift:163-165). chain: also feed the argmax back as the next step's input id and
-// advance the row descriptors (device-chained decode).
-static int enqueue_forward(plamo_runtime& rt, Work& w, int rows, const CacheView& cv, int out_mode, Outputs& o,
+// The head (final norm, lm_head, argmax) runs on the last `nout` rows, output row k going to slot
+// out_map[k]: 1 for the scalar runtime (Runtime.swift:453-458), every row for a batched step
+// (Batch.swift:163-165), the lanes' last prompt rows for a batched prefill. chain: also feed the
+// argmax back as the next step's input id and advance the row descriptors (device-chained decode).
+static int enqueue_forward(plamo_runtime& rt, Work& w, int rows, const CacheView& cv, int nout, Outputs& o,
                            bool chain) {
     const Config& c = rt.c;
     cudaStream_t s = rt.stream;
-    const int nout = out_mode == 2 ? rows : (out_mode == 1 ? 1 : 0);
     LAUNCH(K_NORM, launch_embed_norm(w.ids, rows, c.vocab, rt.embed, rt.layers[0].pre_mixer, c.d, w.x, w.h, nout ? o.keys : nullptr,
                                      w.out_map, nout, s));
     const float post_mlp_offset = float(1.0 / std::pow(5.0, 1.5));  // Runtime.swift:450
@@ -330,7 +334,13 @@ static int enqueue_forward(plamo_runtime& rt, Work& w, int rows, const CacheView
         a.q = w.q; a.keys = cv.keys[l]; a.values = cv.values[l]; a.desc = w.desc; a.geo = w.geo; a.rope_local = rt.rope_local;
         a.part_o = w.part_o; a.part_ml = w.part_ml; a.out = w.att; a.lane_stride = cv.stride[l]; a.rows = rows;
         a.H = c.heads; a.KV = c.kv_heads; a.cap = L.cap; a.full = L.full; a.splits = L.splits; a.per_max = L.per_max;
-        LAUNCH(K_ATTN, launch_attention(a, s));
+        for (int r0 = 0; r0 < rows; r0 += ATT_ROWS) {
+            AttnArgs b = a;
+            b.rows = std::min(ATT_ROWS, rows - r0);
+            b.q = w.q + size_t(r0) * c.q_dim(); b.out = w.att + size_t(r0) * c.q_dim();
+            b.desc = w.desc + r0; b.geo = w.geo + r0;
+            LAUNCH(K_ATTN, launch_attention(b, s));
+        }
         g = GemvArgs();
         g.lin = L.o; g.x = w.att; g.rows = rows; g.y = w.proj; g.ystride = c.d;
         LAUNCH(K_GEMV, launch_gemv(g, GEMV_PLAIN, s));
@@ -395,21 +405,6 @@ static int capture_decode_graph(plamo_runtime& rt) {
 }
 
 // Prepares the persistent decode kernel (decode_mega.cu): the phase table, per-row block offsets of
-// cuTensorMapEncodeTiled from the driver, found through the runtime (no link against libcuda).
-static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
-    static std::once_flag once;
-    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-    std::call_once(once, [] {
-        void* p = nullptr;
-        cudaDriverEntryPointQueryResult q{};
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-    });
-    cudaGetLastError();
-    return fn;
-}
-
 // .p12 tensors, exchange buffers and counters. Leaves rt.mega false when the model shape does not
 // fit its shared-memory plan or cooperative launch is unavailable (the multi-kernel path remains).
 static int setup_mega(plamo_runtime& rt) {
@@ -596,6 +591,70 @@ static int mega_check(plamo_runtime& rt) {
     cudaMemset(rt.margs.sync, 0, sizeof(unsigned) * size_t(rt.margs.nphases + rt.margs.L + 1));
     cudaMemset(rt.margs.amkey, 0, sizeof(unsigned long long));
     return fail("decode step aborted: a bounded device wait timed out (code " + std::to_string(code) + ")");
+}
+
+// One lane's prompt for prefill_rows.
+struct PrefillLane {
+    const int32_t* ids;
+    int len;   // prompt tokens
+    int pos0;  // position of the first token (lane-relative)
+    int lane;  // lane slab (0 for the scalar runtime)
+    int slot;  // output slot of the lane's last token
+};
+
+// Prefills prompts in as few forward calls as the work buffers allow. Every prompt is cut into
+// the reference's 16-token chunks (Runtime.swift:476-479, Batch.swift:86-101): the row
+// descriptors carry each chunk's start and length, so window bases and attention partitions are
+// those of a chunk-by-chunk prefill. Calls take chunks in chunk-index order across lanes; a call
+// holds several chunks of one lane only when that lane's prompt cannot reuse a local ring slot
+// (pos0 + len <= ring capacity). Then all of the lane's keys in the call are appended before any
+// of its rows attend, and each row masks the keys after its own position, which is exactly the
+// chunked computation. The rows whose logits are wanted (each lane's last prompt token) go last
+// in their call, where the head runs.
+static int prefill_rows(plamo_runtime& rt, Work& w, const CacheView& cv, Outputs& o, const std::vector<PrefillLane>& lanes,
+                        double* seconds) {
+    const int chunk = rt.chunk;
+    int max_chunks = 0;
+    for (const PrefillLane& L : lanes) max_chunks = std::max(max_chunks, (L.len + chunk - 1) / chunk);
+    std::vector<std::pair<int, int>> units;  // (lane index, chunk start), chunk-index major
+    for (int c = 0; c < max_chunks; c++)
+        for (int i = 0; i < int(lanes.size()); i++)
+            if (c * chunk < lanes[i].len) units.push_back({i, c * chunk});
+    std::vector<char> in_call(lanes.size());
+    std::vector<std::pair<int, int>> call;
+    size_t u = 0;
+    while (u < units.size()) {
+        std::fill(in_call.begin(), in_call.end(), 0);
+        call.clear();
+        int rows = 0;
+        while (u < units.size()) {
+            const int i = units[u].first, cn = std::min(chunk, lanes[i].len - units[u].second);
+            if (rows + cn > w.rows_cap) break;
+            if (in_call[i] && lanes[i].pos0 + lanes[i].len > rt.local_cap) break;
+            in_call[i] = 1;
+            call.push_back(units[u++]);
+            rows += cn;
+        }
+        int k = 0, nout = 0;
+        for (int pass = 0; pass < 2; pass++)  // rows without logits first, then the output rows
+            for (const auto& cu : call) {
+                const PrefillLane& L = lanes[cu.first];
+                const int st = cu.second, cn = std::min(chunk, L.len - st);
+                for (int j = 0; j < cn; j++) {
+                    const bool last = st + j == L.len - 1;
+                    if (int(last) != pass) continue;
+                    w.h_ids[k] = L.ids[st + j];
+                    w.h_desc[k] = RowDesc{L.pos0 + st + j, L.lane, L.pos0 + st, cn};
+                    k++;
+                    if (last) w.h_out_map[nout++] = L.slot;
+                }
+            }
+        if (upload_inputs(rt, w, rows)) return 1;
+        CK(cudaEventRecord(rt.e0, rt.stream));
+        if (enqueue_forward(rt, w, rows, cv, nout, o, false)) return 1;
+        if (finish(rt, seconds)) return 1;
+    }
+    return 0;
 }
 
 // Runtime.encode (Runtime.swift:327-467) for the scalar cache.
@@ -865,7 +924,8 @@ static int setup_runtime(plamo_runtime* rt, const ModelFiles* mf, bool upload, s
     if (rt->dalloc(rt->rope_local, lo.size()) || rt->dalloc(rt->rope_global, gl.size())) return 1;
     CK(cudaMemcpy(rt->rope_local, lo.data(), lo.size() * 4, cudaMemcpyHostToDevice));
     CK(cudaMemcpy(rt->rope_global, gl.data(), gl.size() * 4, cudaMemcpyHostToDevice));
-    if (alloc_work(*rt, *rt, rt->work, 16) || alloc_outputs(*rt, *rt, rt->out, 1)) return 1;
+    // prefill calls take up to 512 rows (a 512-token prompt in one call)
+    if (alloc_work(*rt, *rt, rt->work, std::max(16, std::min(rt->context, 512))) || alloc_outputs(*rt, *rt, rt->out, 1)) return 1;
     rt->chain_cap = rt->context;
     if (rt->dalloc(rt->chain_hist, size_t(rt->chain_cap)) || rt->dalloc(rt->chain_count, 1)) return 1;
     CK(cudaMemset(rt->chain_count, 0, sizeof(int)));
@@ -898,13 +958,17 @@ int plamo_forward(plamo_runtime* rt, const int32_t* ids, int n, int output, int3
 
 int plamo_prefill(plamo_runtime* rt, const int32_t* ids, int n, int32_t* next_id) {
     if (!rt || !ids || n < 1 || rt->position + n > rt->context) return fail("Input exceeds context");  // Runtime.swift:474
+    for (int i = 0; i < n; i++)
+        if (ids[i] < 0 || ids[i] >= rt->c.vocab) return fail("Invalid tokens or context exhausted");  // Runtime.swift:328-330
     CK(cudaSetDevice(rt->device));
-    int32_t next = -1;
-    for (int start = 0; start < n; start += rt->chunk) {  // Runtime.swift:476-479
-        const int end = std::min(start + rt->chunk, n);
-        if (forward_impl(*rt, ids + start, end - start, end == n, &next)) return 1;
-    }
-    if (next_id) *next_id = next;
+    // the prompt in 16-token chunks (Runtime.swift:476-479), as few calls as the buffers allow
+    if (prefill_rows(*rt, rt->work, rt->cache, rt->out, {PrefillLane{ids, n, rt->position, 0, 0}}, &rt->gpu_seconds))
+        return 1;
+    CK(cudaMemcpy(rt->out.h_result, rt->out.result, sizeof(int), cudaMemcpyDeviceToHost));
+    rt->position += n;
+    rt->last_rows = 1;
+    rt->last_result = rt->out.h_result[0];
+    if (next_id) *next_id = rt->last_result;
     return 0;
 }
 
@@ -1114,7 +1178,7 @@ int plamo_batch_open(plamo_runtime* rt, int lanes, plamo_batch** out) {
         b->cache.values.push_back(v);
         b->cache.stride.push_back(stride);
     }
-    if (!rc) rc = alloc_work(*b, *rt, b->work, std::max(16, lanes));
+    if (!rc) rc = alloc_work(*b, *rt, b->work, std::max(lanes, std::min(16 * lanes, 1024)));
     if (!rc) rc = alloc_outputs(*b, *rt, b->out, lanes);
     if (rc) { delete b; return rc; }
     {
@@ -1154,24 +1218,12 @@ int plamo_batch_prefill(plamo_batch* b, const int32_t* const* prompts, const int
     CK(cudaSetDevice(rt.device));
     b->ready = false;
     b->gpu_seconds = 0;
-    Work& w = b->work;
-    for (int l = 0; l < n; l++) {
-        // Each prompt is prefilled in 16-token chunks straight into its lane slab (the reference
-        // prefills through the scalar runtime and copies the KV rows, Batch.swift:86-101).
-        for (int start = 0; start < lens[l]; start += rt.chunk) {
-            const int cn = std::min(rt.chunk, lens[l] - start);
-            const bool last = start + cn == lens[l];
-            for (int i = 0; i < cn; i++) {
-                w.h_ids[i] = prompts[l][start + i];
-                w.h_desc[i] = RowDesc{start + i, l, start, cn};
-            }
-            w.h_out_map[0] = l;
-            if (upload_inputs(rt, w, cn)) return 1;
-            CK(cudaEventRecord(rt.e0, rt.stream));
-            if (enqueue_forward(rt, w, cn, b->cache, last ? 1 : 0, b->out, false)) return 1;
-            if (finish(rt, &b->gpu_seconds)) return 1;
-        }
-    }
+    // Every prompt goes in 16-token chunks straight into its lane slab (the reference prefills
+    // through the scalar runtime and copies the KV rows, Batch.swift:86-101); the lanes' chunks
+    // share forward calls.
+    std::vector<PrefillLane> pl;
+    for (int l = 0; l < n; l++) pl.push_back(PrefillLane{prompts[l], lens[l], 0, l, l});
+    if (prefill_rows(rt, b->work, b->cache, b->out, pl, &b->gpu_seconds)) return 1;
     CK(cudaMemcpy(b->out.h_result, b->out.result, sizeof(int) * n, cudaMemcpyDeviceToHost));
     b->positions.assign(lens, lens + n);
     b->ready = true;
@@ -1197,7 +1249,7 @@ int plamo_batch_step(plamo_batch* b, const int32_t* tokens, int n, int32_t* next
     CK(cudaSetDevice(rt.device));
     if (upload_inputs(rt, w, rows)) return 1;
     CK(cudaEventRecord(rt.e0, rt.stream));
-    if (enqueue_forward(rt, w, rows, b->cache, 2, b->out, false)) { b->ready = false; return 1; }
+    if (enqueue_forward(rt, w, rows, b->cache, rows, b->out, false)) { b->ready = false; return 1; }
     CK(cudaMemcpyAsync(b->out.h_result, b->out.result, sizeof(int) * n, cudaMemcpyDeviceToHost, rt.stream));
     if (finish(rt, &b->gpu_seconds)) { b->ready = false; return 1; }
     for (int l = 0; l < n; l++)

@@ -91,10 +91,11 @@ def test_packed_decode_fast_path(torch, rt, pkg):
         assert np.array_equal(host(out, np.uint16), vals), std
 
 
-@pytest.mark.parametrize("rows", [1, 3, 16, 33])
+@pytest.mark.parametrize("rows", [1, 3, 16, 33, 64, 100])
 def test_linear_matches_oracle_and_packed_equals_raw(torch, rt, pkg, oracle, rows):
-    """linear/matrix (Kernels.metal:92-200) vs the CPU restatement: <= 1 bf16 ulp; packed == raw
-    bit for bit (PackedTests.swift:6-45)."""
+    """linear/matrix (Kernels.metal:92-200) vs the CPU restatement, bit for bit; packed == raw
+    bit for bit (PackedTests.swift:6-45). Above 16 rows raw weights go through the tiled GEMM
+    and packed weights through the GEMV in 16-row passes, so this also pins GEMM == GEMV."""
     gen = torch.Generator().manual_seed(rows)
     for M, K in [(35, 128), (2304, 1536), (96, 2048), (64, 6144)]:
         w = (torch.randn(M * K, generator=gen) * 0.02).to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
@@ -130,10 +131,12 @@ def test_linear_reference_pattern(torch, rt, oracle):
         assert np.max(np.abs(got - ref)) <= 1e-4
 
 
-def test_swiglu_and_logits_modes(torch, rt, oracle):
-    """gate_up + swiglu epilogue (Kernels.metal:202-210) and lm_head + argmax (:704-729)."""
+@pytest.mark.parametrize("rows", [3, 40])
+def test_swiglu_and_logits_modes(torch, rt, oracle, rows):
+    """gate_up + swiglu epilogue (Kernels.metal:202-210) and lm_head + argmax (:704-729); 40 rows
+    run the tiled GEMM's epilogues."""
     gen = torch.Generator().manual_seed(11)
-    F, K, rows = 512, 1536, 3
+    F, K = 518, 1536
     w = (torch.randn(2 * F * K, generator=gen) * 0.02).to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
     x16 = torch.randn(rows * K, generator=gen).to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
     x = oracle.bf16_to_f32(x16).reshape(rows, K)
@@ -155,6 +158,7 @@ def test_swiglu_and_logits_modes(torch, rt, oracle):
     rt.k_argmax_keys(keys.data_ptr(), rows, idx.data_ptr())
     torch.cuda.synchronize()
     logits = host(yl, np.uint16).reshape(rows, V)
+    assert np.array_equal(logits, oracle.linear(wl.reshape(V, K), x, logits=True))
     for r in range(rows):
         assert host(idx, np.uint32)[r] == oracle.argmax_bits(logits[r])
 
