@@ -1,23 +1,35 @@
 // Persistent batch-1 decode step for sm_100a: one cooperative launch per token, one CTA per SM.
 //
-// Every CTA owns a contiguous share of the output rows of every projection and streams its weight
-// tiles for the whole step (all 16 layers and the lm_head) through a 6-slot shared-memory ring
-// with TMA bulk copies (cp.async.bulk + mbarrier complete_tx). The ring runs ahead of the data
-// dependencies: the last of the 8 warps to release a slot refills it with the tile six ahead in
-// the step's order, so the next phase's first tiles are already resident while the warps wait at
-// a phase boundary. (No dedicated producer warp: with 8 warps every thread may hold 255
-// registers, with a ninth the register file's per-scheduler split would cap it at 168.) The 8
-// warps run the phases of the step:
+// The step is a list of phases (per layer: QKV, attention, o_proj, gate/up + SwiGLU, down_proj;
+// then the head):
 //   QKV  (prologue: residual + post-MLP norm of the previous layer, pre-mixer norm)  Runtime.swift:377,450
-//   ATT  (QK-norm + RoPE + KV append fused, split-K attention, merge by the last split) Kernels.metal:223-562
+//   ATT  (QK-norm + RoPE + KV append fused, split-K attention, per-head merge)         Kernels.metal:223-562
 //   O    (o_proj)                                                                      Runtime.swift:445
 //   GU   (prologue: residual + post-mixer norm, pre-MLP norm; SwiGLU epilogue)         Runtime.swift:446-448
 //   DOWN (down_proj)                                                                   Runtime.swift:449
 //   HEAD (residual + post-MLP norm, final norm, lm_head, first-index argmax)           Runtime.swift:450-458
-// Phases are joined by device counters in global memory; every wait is bounded in time and
+//
+// Weights. Every CTA owns a contiguous share of the outputs of every projection. Its 8 warps read
+// their weight rows straight from HBM with 16-byte non-allocating loads, up to four (row, 1536-
+// weight segment) tasks per warp at a time (24 loads of 16 bytes in flight per lane). The loads
+// of a warp's next tasks are issued before the current ones are summed, and across phase
+// boundaries: a warp's first tasks of the next projection are in flight while it waits for that
+// projection's input (and, for o_proj, during the whole attention phase).
+//
+// Phase boundaries. Phase outputs are exchanged through tagged words (mega.h): a producer stores
+// each value with the (step, layer) tag, a consumer polls exactly the words it needs. There is
+// no grid-wide barrier, counter or fence between phases. Every poll is bounded in time and
 // raises the error flag (read by the host after the step) instead of hanging.
-// The arithmetic of every output follows the same per-element operation order as kernels.cu (and
-// the CPU restatement), so this path is bit-identical to the multi-kernel path.
+//
+// Attention. A task is (split of the key window, group of 4 query heads); tasks are spread over
+// the CTAs, each stages its key and value tiles with TMA bulk copies issued before its queries
+// are ready. The merge of head h runs on CTA G - 1 - h as soon as the head's split partials land.
+//
+// Arithmetic. Every output follows the same per-element operation order as kernels.cu (and the
+// CPU restatement): 16-weight lane chunks in 1536-weight segments, two fma chains per segment,
+// segment sums folded in order, the 32-lane butterfly; the 256-thread norm tree; one fma chain
+// per score and per P.V output; split order in the merge. So this path is bit-identical to the
+// multi-kernel path.
 #include "common.cuh"
 #include "mega.h"
 
@@ -34,9 +46,6 @@ __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
 }
 __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
     uint32_t ok;
@@ -59,42 +68,93 @@ __device__ __forceinline__ void tma_load(void* dst, const void* src, uint32_t by
                  "l"(src), "r"(bytes), "r"(smem_u32(bar))
                  : "memory");
 }
-// Tiled tensor copy (3-D map, no multicast) global -> this CTA's shared memory, completion on `bar`.
-__device__ __forceinline__ void tma_load_3d(void* dst, const void* tmap, int c0, int c1, int c2, uint64_t* bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(
-            smem_u32(dst)),
-        "l"(tmap), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
-        : "memory");
+// 16-byte asynchronous copy global -> shared (L2 only), completed by cp_async_wait_all
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
 }
-__device__ __forceinline__ void consumers_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
-// orders this thread's earlier generic-proxy accesses (and the data it acquired) before its next
-// bulk copies, which run in the async proxy
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+// orders this thread's earlier generic-proxy accesses before its next bulk copies (async proxy)
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async;" ::: "memory"); }
-__device__ __forceinline__ uint16_t ldcg16(const uint16_t* p) { return __ldcg(reinterpret_cast<const unsigned short*>(p)); }
+
+// Weights: read once per step, never written: non-coherent path, no L1 allocation, and marked
+// first to evict from L2, so the 1.45 GB stream does not flush the small tensors every step
+// re-reads (norm weights, RoPE rows, KV cache, exchange words).
+__device__ __forceinline__ uint64_t evict_first_policy() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+__device__ __forceinline__ uint4 ldw4(const void* p, uint64_t pol) {
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.u32 {%0,%1,%2,%3}, [%4], %5;"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p), "l"(pol));
+    return v;
+}
+__device__ __forceinline__ uint2 ldw2(const void* p, uint64_t pol) {
+    uint2 v;
+    asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.v2.u32 {%0,%1}, [%2], %3;" : "=r"(v.x), "=r"(v.y) : "l"(p), "l"(pol));
+    return v;
+}
+__device__ __forceinline__ uint32_t ldw1(const uint32_t* p, uint64_t pol) {
+    uint32_t v;
+    asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.u32 %0, [%1], %2;" : "=r"(v) : "l"(p), "l"(pol));
+    return v;
+}
+// tagged exchange words: morally strong (relaxed, gpu scope) so a poll always sees the latest store
+__device__ __forceinline__ uint32_t ld_tag(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.relaxed.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ unsigned long long ld_tag64(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_tag(uint32_t* p, uint32_t v) {
+    asm volatile("st.relaxed.gpu.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ void st_tag64(unsigned long long* p, unsigned long long v) {
+    asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t tagged(uint32_t tag, uint32_t bf) { return (tag << 16) | bf; }
+__device__ __forceinline__ unsigned long long tagged64(uint32_t tag, float v) {
+    return (static_cast<unsigned long long>(tag) << 32) | __float_as_uint(v);
+}
 
 constexpr uint64_t WAIT_NS = 2000000000ull;  // every wait gives up after 2 s
-enum MegaError { ERR_CONSUMER = 12, ERR_COUNTER = 13, ERR_DRAIN = 14 };
+enum MegaError { ERR_DATA = 12, ERR_TILE = 13, ERR_DRAIN = 14 };
 
-// The error flag and the clock are checked every 64 polls only: the flag is one global word that
-// every waiting warp of the grid would otherwise hammer.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* error, int code) {
-    if (mbar_test(bar, parity)) return true;
-    const uint64_t t0 = gtime();
-    for (uint32_t i = 1;; i++) {
-        if (mbar_test(bar, parity)) return true;
-        if ((i & 63u) == 0) {
-            if (*reinterpret_cast<volatile int*>(error)) return false;
-            if (gtime() - t0 > WAIT_NS) {
-                atomicCAS(error, 0, code);
-                return false;
-            }
+// Bounded polling. After a miss the clock starts; the error flag (one global word) and the clock
+// are checked every 16 polls, with a short sleep between polls to keep the L2 free for producers.
+struct Spin {
+    uint64_t t0 = 0;
+    uint32_t i = 0;
+};
+__device__ __forceinline__ bool spin_more(Spin& s, int* error, int code) {
+    if (s.i++ == 0) s.t0 = gtime();
+    if ((s.i & 15u) == 0) {
+        if (*reinterpret_cast<volatile int*>(error)) return false;
+        if (gtime() - s.t0 > WAIT_NS) {
+            atomicCAS(error, 0, code);
+            return false;
         }
     }
+    __nanosleep(20);
+    return true;
 }
-
-// Waits for the completion of copies already issued into this CTA's shared memory before it
-// exits; bounded in time only (a copy from valid global memory always completes).
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* error) {
+    if (mbar_test(bar, parity)) return true;
+    Spin s;
+    while (!mbar_test(bar, parity))
+        if (!spin_more(s, error, ERR_TILE)) return false;
+    return true;
+}
+// Waits for copies already issued into this CTA's shared memory before it exits; bounded in
+// time only (a copy from valid global memory always completes).
 __device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity, int* error) {
     const uint64_t t0 = gtime();
     while (!mbar_test(bar, parity)) {
@@ -105,118 +165,50 @@ __device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity, int* 
     }
 }
 
-__device__ __forceinline__ bool counter_wait(const unsigned* c, unsigned target, int* error) {
-    const uint64_t t0 = gtime();
-    for (uint32_t i = 1;; i++) {
-        unsigned v;
-        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(c) : "memory");
-        if (v >= target) return true;
-        if ((i & 15u) == 0) {
-            if (*reinterpret_cast<volatile int*>(error)) return false;
-            if (gtime() - t0 > WAIT_NS) {
-                atomicCAS(error, 0, ERR_COUNTER);
-                return false;
+// Warp 0 polls the n hint words h[i * stride] until all carry `tag` (a few requests per round,
+// spaced out); then the whole CTA passes a barrier. Called by every thread of the CTA.
+__device__ __forceinline__ bool wait_hints(const uint32_t* h, int n, int stride, uint32_t tag, int* error) {
+    bool ok = true;
+    if (threadIdx.x < 32) {
+        Spin s;
+        for (;;) {
+            // every word of the round in flight at once, then the check
+            uint32_t v[8];
+#pragma unroll
+            for (int k = 0; k < 8; k++) {
+                const int i = threadIdx.x + 32 * k;
+                v[k] = i < n ? ld_tag(h + size_t(i) * stride) : tag;
             }
+            bool mine = true;
+            for (int i = threadIdx.x + 256; i < n; i += 32) mine = mine && ld_tag(h + size_t(i) * stride) == tag;
+#pragma unroll
+            for (int k = 0; k < 8; k++) mine = mine && v[k] == tag;
+            if (__all_sync(FULL_MASK, mine)) break;
+            const bool more = __all_sync(FULL_MASK, spin_more(s, error, ERR_DATA));
+            if (!more) {
+                ok = false;
+                break;
+            }
+            __nanosleep(64);
         }
-        __nanosleep(32);
     }
+    return __syncthreads_and(ok);
 }
 
-// ---- tile schedule ---------------------------------------------------------------------------
-struct TileSpec {
-    const uint8_t* data;
-    const uint32_t* table;
-    uint32_t data_bytes, table_bytes;
-    int row0;  // first weight row (tensor-map tiles)
-};
-
-__device__ __forceinline__ void block_range(int out_rows, int tile_rows, int cta, int G, int& b0, int& b1) {
-    const int nb = (out_rows + tile_rows - 1) / tile_rows;
-    b0 = int((long long)nb * cta / G);
-    b1 = int((long long)nb * (cta + 1) / G);
-}
-
-__device__ __forceinline__ TileSpec tile_spec(const MegaPhase& ph, int block, int sub) {
-    const int K = ph.lin.K;
-    int r0 = block * ph.tile_rows;
-    const int n = min(ph.tile_rows, ph.out_rows - r0);
-    if (sub) r0 += ph.out_rows;  // up rows of the SwiGLU phase
-    TileSpec t;
-    t.row0 = r0;
-    if (!ph.lin.offsets) {
-        // raw weights come through the phase's swizzled tensor map as a full box of tile_rows
-        // rows (rows past the matrix are zero-filled and still counted)
-        t.data = ph.lin.w + size_t(r0) * K * 2;
-        t.data_bytes = uint32_t(ph.tile_rows) * K * 2;
-        t.table = nullptr;
-        t.table_bytes = 0;
-    } else {
-        const uint32_t a = __ldg(ph.rowoff + r0), b = __ldg(ph.rowoff + r0 + n);
-        t.data = ph.lin.w + a;
-        t.data_bytes = b - a;
-        t.table = ph.lin.offsets + size_t(r0) * (K / 128);
-        t.table_bytes = (uint32_t(n) * (K / 128) * 4 + 15u) & ~15u;
-    }
-    return t;
-}
-
-// Walks this CTA's tiles of every weight phase in step order. Holds the current phase
-// descriptor and, loaded one phase early (nothing waits for it until the phase ends), the next
-// weight phase's, so advancing costs no global read on the critical path.
-struct Cursor {
-    MegaPhase ph, nxt;
-    int p, b, b1, sub;
-};
-
-// Enters weight phase q (descriptor phq) or the first later one with blocks for this CTA.
-__device__ __forceinline__ bool cursor_enter(const MegaArgs& a, Cursor& c, int q, MegaPhase phq, int cta, int G) {
-    while (q < a.nphases) {
-        int b0, b1;
-        block_range(phq.out_rows, phq.tile_rows, cta, G, b0, b1);
-        if (b0 < b1) {
-            c.p = q;
-            c.ph = phq;
-            c.b = b0;
-            c.b1 = b1;
-            c.sub = 0;
-            if (phq.next_weight < a.nphases) c.nxt = a.phases[phq.next_weight];
-            return true;
-        }
-        q = phq.next_weight;
-        if (q < a.nphases) phq = a.phases[q];
-    }
-    return false;
-}
-__device__ __forceinline__ bool cursor_seek(const MegaArgs& a, Cursor& c, int cta, int G) {
-    return a.nphases > 0 && cursor_enter(a, c, a.first_weight, a.phases[a.first_weight], cta, G);
-}
-__device__ __forceinline__ bool cursor_next(const MegaArgs& a, Cursor& c, int cta, int G) {
-    if (c.ph.kind == MK_GU && c.sub == 0) {
-        c.sub = 1;
-        return true;
-    }
-    c.sub = 0;
-    if (++c.b < c.b1) return true;
-    return c.ph.next_weight < a.nphases && cursor_enter(a, c, c.ph.next_weight, c.nxt, cta, G);
-}
-
-// ---- consumer building blocks (256 threads; same arithmetic order as kernels.cu) ----------------
-constexpr int QSM = 132;  // query row stride (floats) in shared memory
-constexpr int ATM = 64;   // keys per staged attention tile
-
-__device__ __forceinline__ float cblock_sum(float v, float* red) {
+// ---- norms (256 threads; the tree of k_norm) --------------------------------------------------
+// Sum over the 256 threads in k_norm's tree: the butterfly within each warp, then the 8 warp sums
+// as lanes 0..7 of one butterfly (lanes 8..31 zero). After the single barrier every warp folds the
+// 8 sums itself. `red` alternates between two 8-float halves from call to call: a call's writes
+// can only meet the reads of the call before the previous one, which every warp finished before
+// passing the previous call's barrier.
+__device__ __forceinline__ float cblock_sum(float v, float* red, int& parity) {
     v = warp_sum(v);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    consumers_sync();
-    if (lane == 0) red[warp] = v;
-    consumers_sync();
-    if (warp == 0) {
-        float s = lane < 8 ? red[lane] : 0.f;
-        s = warp_sum(s);
-        if (lane == 0) red[8] = s;
-    }
-    consumers_sync();
-    return red[8];
+    float* r = red + 8 * parity;
+    parity ^= 1;
+    if (lane == 0) r[warp] = v;
+    __syncthreads();
+    return warp_sum(lane < 8 ? r[lane] : 0.f);
 }
 
 // Norm factors rbf(w + offset) of the elements t + 256 j this thread owns.
@@ -232,11 +224,12 @@ __device__ __forceinline__ void load_norm(const uint16_t* w, float offset, int n
 // RMSNorm over n elements held NPT per thread (thread t: t + 256 j). The sum of squares is the
 // 256-thread tree of k_norm; elements past n are zero and leave every partial sum unchanged.
 template <int NPT>
-__device__ __forceinline__ void cnorm(const float (&v)[NPT], int n, const float (&wf)[NPT], float* red, float (&z)[NPT]) {
+__device__ __forceinline__ void cnorm(const float (&v)[NPT], int n, const float (&wf)[NPT], float* red, int& parity,
+                                      float (&z)[NPT]) {
     float ss = 0.f;
 #pragma unroll
     for (int j = 0; j < NPT; j++) ss = fmaf(v[j], v[j], ss);
-    const float total = cblock_sum(ss, red);
+    const float total = cblock_sum(ss, red, parity);
     const float scale = 1.0f / sqrtf(total / float(n) + PLAMO_EPS);
 #pragma unroll
     for (int j = 0; j < NPT; j++) {
@@ -245,19 +238,255 @@ __device__ __forceinline__ void cnorm(const float (&v)[NPT], int n, const float 
     }
 }
 
-// bf16 activation element i -> permuted shared layout used by row_dot (conflict-free 16-B reads)
+// bf16 activation element i -> permuted shared layout read by the dot products: lane l's 16
+// elements of group g sit at 16-byte chunks g*64 + l and g*64 + 32 + l (conflict-free reads).
 __device__ __forceinline__ int xs_index(int i) {
     const int c = i >> 3, g = c >> 6, within = c & 63;
     return ((g * 64 + (within & 1) * 32 + (within >> 1)) << 3) + (i & 7);
 }
 
-__device__ __forceinline__ void stage_vec(uint16_t* xs, const uint16_t* src, int n) {
-    for (int i = threadIdx.x; i < n; i += 256) xs[xs_index(i)] = ldcg16(src + i);
+// Gathers n tagged bf16 words: dst[i] (or dst[xs_index(i)] with PERMUTE) = the payload of src[i]
+// once it carries `tag`. All threads: up to 24 loads in flight per thread, then one compact re-poll loop
+// over the words not yet visible. The caller passes a barrier before reading dst.
+template <bool PERMUTE>
+__device__ __forceinline__ bool gather16(uint16_t* dst, const uint32_t* src, int n, uint32_t tag, int* error) {
+    const int t = threadIdx.x;
+    for (int base = 0; base < n; base += 24 * 256) {
+        uint32_t v[24];
+#pragma unroll
+        for (int j = 0; j < 24; j++) {
+            const int i = base + t + j * 256;
+            v[j] = i < n ? ld_tag(src + i) : 0u;
+        }
+        unsigned miss = 0;
+#pragma unroll
+        for (int j = 0; j < 24; j++) {
+            const int i = base + t + j * 256;
+            if (i < n) {
+                if ((v[j] >> 16) == tag) dst[PERMUTE ? xs_index(i) : i] = uint16_t(v[j] & 0xffffu);
+                else miss |= 1u << j;
+            }
+        }
+        Spin s;
+        while (miss) {
+            const int i = base + t + (__ffs(miss) - 1) * 256;
+            const uint32_t w = ld_tag(src + i);
+            if ((w >> 16) == tag) {
+                dst[PERMUTE ? xs_index(i) : i] = uint16_t(w & 0xffffu);
+                miss &= miss - 1;
+            } else if (!spin_more(s, error, ERR_DATA)) {
+                return false;
+            }
+        }
+    }
+    return true;
+}
+
+// The same for tagged f32 words laid out in rows: element i is src[(i >> rshift) * rstride +
+// (i & (2^rshift - 1))]; dst[i] receives its value.
+__device__ __forceinline__ bool gather64(float* dst, const unsigned long long* src, int n, int rshift, size_t rstride,
+                                         uint32_t tag, int* error) {
+    const int t = threadIdx.x;
+    const int rmask = (1 << rshift) - 1;
+    for (int base = 0; base < n; base += 8 * 256) {
+        unsigned long long v[8];
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            const int i = base + t + j * 256;
+            v[j] = i < n ? ld_tag64(src + size_t(i >> rshift) * rstride + (i & rmask)) : 0ull;
+        }
+        unsigned miss = 0;
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            const int i = base + t + j * 256;
+            if (i < n) {
+                if (uint32_t(v[j] >> 32) == tag) dst[i] = __uint_as_float(uint32_t(v[j]));
+                else miss |= 1u << j;
+            }
+        }
+        Spin s;
+        while (miss) {
+            const int i = base + t + (__ffs(miss) - 1) * 256;
+            const unsigned long long w = ld_tag64(src + size_t(i >> rshift) * rstride + (i & rmask));
+            if (uint32_t(w >> 32) == tag) {
+                dst[i] = __uint_as_float(uint32_t(w));
+                miss &= miss - 1;
+            } else if (!spin_more(s, error, ERR_DATA)) {
+                return false;
+            }
+        }
+    }
+    return true;
+}
+
+// ---- weight phases ---------------------------------------------------------------------------
+// A task is (output row, 1536-weight segment of the row): lane l covers weights
+// [g*512 + 16l, +16) of the segment's groups g (at most 3). A warp carries up to RB tasks at a time.
+constexpr int RB = 4;
+constexpr int GB = 3;
+constexpr int MEGA_PF_ROUNDS = 3;  // the rolling L2 prefetch runs this many chunk rounds ahead
+
+struct Batch {
+    uint4 w[RB][GB][2];       // raw: 32 weight bytes; .p12 packed block: sign|mantissa bytes, codes
+    uint32_t ent[RB][GB];     // .p12 block-table entries (offset | tag)
+};
+
+// This CTA's share of one weight phase.
+struct PhaseWork {
+    int kind, K, G, nseg, R;  // row length, 512-weight groups, segments per row, tasks per chunk
+    const uint8_t* w;
+    const uint32_t* off;
+    const uint32_t* rowoff;   // .p12: per-row block offsets (M + 1)
+    int u0, nu;               // this CTA's outputs [u0, u0 + nu)
+    int ntask, nchunk;
+    int up;                   // SwiGLU: row offset of the up half
+    int upc;                  // SwiGLU: outputs per chunk
+};
+
+__device__ __forceinline__ PhaseWork phase_work(const MegaPhase& ph, int cta, int G) {
+    PhaseWork p;
+    p.kind = ph.kind;
+    p.K = ph.lin.K;
+    p.G = (p.K + 511) >> 9;
+    p.nseg = (p.G + 2) / 3;
+    p.w = ph.lin.w;
+    p.off = ph.lin.offsets;
+    p.rowoff = ph.rowoff;
+    const int units = ph.out_rows;
+    p.u0 = int((long long)units * cta / G);
+    p.nu = int((long long)units * (cta + 1) / G) - p.u0;
+    p.up = ph.kind == MK_GU ? ph.out_rows : 0;
+    if (ph.kind == MK_GU) {
+        // chunks hold whole gate/up pairs: (gate m, up m) or (gate m, gate m+1, up m, up m+1)
+        p.ntask = 2 * p.nu;
+        p.upc = p.nu > 8 ? 2 : 1;
+        p.R = 2 * p.upc;
+        p.nchunk = (p.nu + p.upc - 1) / p.upc;
+    } else {
+        p.ntask = p.nu * p.nseg;
+        p.upc = 0;
+        p.R = min(RB, max(1, (p.ntask + 7) / 8));
+        p.nchunk = (p.ntask + p.R - 1) / p.R;
+    }
+    return p;
+}
+
+// L2 prefetch of weight rows: the bulk-copy engine pulls them from HBM into L2, nothing comes
+// back to the SM, so the stream does not sit in front of the latency-critical exchange loads. The
+// demand loads that follow hit L2.
+__device__ __forceinline__ void l2_prefetch_bytes(const uint8_t* p, size_t bytes) {
+    while (bytes >= 16) {
+        const uint32_t n = uint32_t(bytes < 32768 ? bytes & ~size_t(15) : 32768);
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(n) : "memory");
+        p += n;
+        bytes -= n;
+    }
+}
+// Rows [r0, r1) of this CTA's share of phase q (both halves of the SwiGLU phase), at most `cap` bytes per half.
+__device__ __forceinline__ void l2_prefetch_rows(const PhaseWork& q, int r0, int r1, size_t cap) {
+    if (r1 <= r0) return;
+    if (!q.off) {
+        const size_t rb = size_t(q.K) * 2, n = min(size_t(r1 - r0) * rb, cap);
+        l2_prefetch_bytes(q.w + size_t(r0) * rb, n);
+        if (q.up) l2_prefetch_bytes(q.w + size_t(r0 + q.up) * rb, n);
+        return;
+    }
+    // .p12: the rows' blocks (contiguous in the data region) and their block-table entries
+    const int bpr = q.K >> 7;
+    for (int half = 0; half < (q.up ? 2 : 1); half++) {
+        const int a0 = r0 + half * q.up, a1 = r1 + half * q.up;
+        const uint32_t lo = __ldg(q.rowoff + a0), hi = __ldg(q.rowoff + a1);
+        l2_prefetch_bytes(q.w + lo, min(size_t(hi - lo), cap));
+        const uint8_t* t0 = reinterpret_cast<const uint8_t*>(q.off + size_t(a0) * bpr);
+        const uint8_t* ta = reinterpret_cast<const uint8_t*>(reinterpret_cast<uintptr_t>(t0) & ~uintptr_t(15));
+        l2_prefetch_bytes(ta, min(size_t(a1 - a0) * bpr * 4 + size_t(t0 - ta), cap) & ~size_t(15));
+    }
+}
+// Output rows covered by chunk c (the gate half for SwiGLU).
+__device__ __forceinline__ void chunk_rows(const PhaseWork& p, int c, int& r0, int& r1) {
+    if (p.kind == MK_GU) {
+        r0 = p.u0 + c * p.upc;
+        r1 = min(r0 + p.upc, p.u0 + p.nu);
+    } else {
+        const int i0 = c * p.R, i1 = min(i0 + p.R, p.ntask);
+        r0 = p.u0 + i0 / p.nseg;
+        r1 = i1 > i0 ? p.u0 + (i1 - 1) / p.nseg + 1 : r0;
+    }
+}
+
+// Row and segment of task r of chunk c; false when the slot is empty.
+__device__ __forceinline__ bool task_of(const PhaseWork& p, int c, int r, int& row, int& seg) {
+    if (r >= p.R) return false;
+    if (p.kind == MK_GU) {
+        const int u = c * p.upc + (r % p.upc);
+        if (u >= p.nu) return false;
+        row = p.u0 + u + (r / p.upc) * p.up;
+        seg = 0;
+        return true;
+    }
+    const int i = c * p.R + r;
+    if (i >= p.ntask) return false;
+    row = p.u0 + i / p.nseg;
+    seg = i % p.nseg;
+    return true;
+}
+
+// Issues the weight loads of chunk c (this warp). .p12: the block-table entries first, then the
+// blocks they point at.
+template <bool PACKED>
+__device__ __forceinline__ void issue_chunk(const PhaseWork& p, int c, Batch& b, uint64_t pol) {
+    const int lane = threadIdx.x & 31;
+    const uint8_t* rp[RB];
+    bool ok[RB];
+    int sg[RB];
+#pragma unroll
+    for (int r = 0; r < RB; r++) {
+        int row = 0, seg = 0;
+        ok[r] = task_of(p, c, r, row, seg);
+        sg[r] = seg;
+        rp[r] = PACKED ? reinterpret_cast<const uint8_t*>(p.off + size_t(row) * (p.K >> 7))
+                       : p.w + size_t(row) * p.K * 2;
+    }
+#pragma unroll
+    for (int r = 0; r < RB; r++)
+#pragma unroll
+        for (int gi = 0; gi < GB; gi++) {
+            const int e0 = (3 * sg[r] + gi) * 512 + lane * 16;
+            if (ok[r] && e0 < p.K && (3 * sg[r] + gi) < p.G) {
+                if (!PACKED) {
+                    b.w[r][gi][0] = ldw4(rp[r] + e0 * 2, pol);
+                    b.w[r][gi][1] = ldw4(rp[r] + e0 * 2 + 16, pol);
+                } else {
+                    b.ent[r][gi] = ldw1(reinterpret_cast<const uint32_t*>(rp[r]) + (e0 >> 7), pol);
+                }
+            }
+        }
+    if (PACKED) {
+#pragma unroll
+        for (int r = 0; r < RB; r++)
+#pragma unroll
+            for (int gi = 0; gi < GB; gi++) {
+                const int e0 = (3 * sg[r] + gi) * 512 + lane * 16;
+                if (ok[r] && e0 < p.K && (3 * sg[r] + gi) < p.G) {
+                    const uint32_t entry = b.ent[r][gi], i0 = uint32_t(e0 & 127);
+                    const uint8_t* blk = p.w + (entry & ~63u);
+                    if (entry & 63u) {
+                        b.w[r][gi][0] = ldw4(blk + i0, pol);
+                        const uint2 cd = ldw2(blk + 128 + (i0 >> 1), pol);
+                        b.w[r][gi][1] = make_uint4(cd.x, cd.y, 0u, 0u);
+                    } else {
+                        b.w[r][gi][0] = ldw4(blk + 2 * i0, pol);
+                        b.w[r][gi][1] = ldw4(blk + 2 * i0 + 16, pol);
+                    }
+                }
+            }
+    }
 }
 
 // Both halves of a bf16 pair times the matching halves of x, accumulated into the even (lo) and
 // odd (hi) chains with sm_100's mixed-precision fma (bf16 x bf16 + f32, one rounding): the same
-// result as fmaf on the widened operands, without unpacking either pair.
+// result as fmaf on the widened operands (the product of two bf16 values is exact in f32), in
+// one instruction per weight.
 __device__ __forceinline__ void fma_bf16x2(uint32_t w, uint32_t x, float& lo, float& hi) {
     asm("{\n .reg .b16 wl, wh, xl, xh;\n mov.b32 {wl, wh}, %2;\n mov.b32 {xl, xh}, %3;\n"
         " fma.rn.f32.bf16 %0, wl, xl, %0;\n fma.rn.f32.bf16 %1, wh, xh, %1;\n}"
@@ -265,854 +494,556 @@ __device__ __forceinline__ void fma_bf16x2(uint32_t w, uint32_t x, float& lo, fl
         : "r"(w), "r"(x));
 }
 
-// The 16 weights of row r at element e0 of a ring tile, as 8 bf16 pairs (raw or .p12 blocks).
-// Raw tiles arrive 128-byte swizzled (the tensor map's SWIZZLE_128B on a 1024-byte aligned slot):
-// 16-byte chunk c of 128-byte line L sits at chunk c ^ (L & 7), so the two 16-byte reads of the
-// 8 lanes of each quarter-warp hit 8 distinct chunk positions (no bank conflict).
+// The 16 weights of (task r, group gi) as bf16 pairs.
 template <bool PACKED>
-__device__ __forceinline__ void tile_w16(const uint8_t* tile, const uint32_t* tab, int r, int K, int e0, uint32_t (&wp)[8]) {
-    if (!PACKED) {
-        const uint32_t line = uint32_t(r) * uint32_t(K >> 6) + uint32_t(e0 >> 6), c = uint32_t(e0 & 63) >> 3;
-        const uint8_t* lb = tile + size_t(line) * 128;
-        const uint4 A = *reinterpret_cast<const uint4*>(lb + ((c ^ (line & 7u)) << 4));
-        const uint4 B = *reinterpret_cast<const uint4*>(lb + (((c + 1u) ^ (line & 7u)) << 4));
+__device__ __forceinline__ void weights16(const Batch& b, int r, int gi, uint32_t (&wp)[8]) {
+    const uint4 A = b.w[r][gi][0], B = b.w[r][gi][1];
+    if (PACKED && (b.ent[r][gi] & 63u)) {
+        decode16(A, make_uint2(B.x, B.y), (b.ent[r][gi] & 63u) + 107u, wp);
+    } else {
         wp[0] = A.x; wp[1] = A.y; wp[2] = A.z; wp[3] = A.w;
         wp[4] = B.x; wp[5] = B.y; wp[6] = B.z; wp[7] = B.w;
-    } else {
-        const uint32_t entry = tab[r * (K >> 7) + (e0 >> 7)];
-        const uint8_t* blk = tile + ((entry & ~63u) - (tab[0] & ~63u));
-        const uint32_t i0 = uint32_t(e0 & 127), tag = entry & 63u;
-        if (tag) {
-            decode16(*reinterpret_cast<const uint4*>(blk + i0), *reinterpret_cast<const uint2*>(blk + 128 + (i0 >> 1)),
-                     tag + 107u, wp);
-        } else {
-            const uint4 A = *reinterpret_cast<const uint4*>(blk + 2 * i0);
-            const uint4 B = *reinterpret_cast<const uint4*>(blk + 2 * i0 + 16);
-            wp[0] = A.x; wp[1] = A.y; wp[2] = A.z; wp[3] = A.w;
-            wp[4] = B.x; wp[5] = B.y; wp[6] = B.z; wp[7] = B.w;
-        }
     }
 }
 
-// Lane partials of two weight rows (row rA of tile A, row rB of tile B; a row is skipped when its
-// flag is false) over the groups [gb, ge) of 512 weights (lane l: elements g*512 + 16l .. +16),
-// against the activations this lane holds in registers (bf16 pairs xr[g - gb]). The two rows
-// are independent chains computed side by side for instruction-level parallelism; each follows
-// the GEMV order of kernels.cu: two fma chains (even / odd elements) per 1536-weight segment,
-// segment sums folded in order (t = t + (a0 + a1)). With `raw_segment` the single segment's
-// a0 + a1 is returned instead (a warp computing one segment of a split row).
+// Lane partials of the chunk's tasks: per task the segment's two fma chains (even / odd
+// elements, groups in order), returned as a0 + a1.
 template <bool PACKED>
-__device__ __forceinline__ void lane_partial2(const uint8_t* tA, const uint32_t* tabA, int rA, bool okA, const uint8_t* tB,
-                                              const uint32_t* tabB, int rB, bool okB, int K, int gb, int ge,
-                                              const uint32_t (&xr)[4][8], bool raw_segment, float& outA, float& outB) {
+__device__ __forceinline__ void chunk_partials(const PhaseWork& p, int c, const Batch& b, const uint4* xs4, float (&res)[RB]) {
     const int lane = threadIdx.x & 31;
-    float tA_ = 0.f, a0 = 0.f, a1 = 0.f, sA = 0.f;
-    float tB_ = 0.f, b0 = 0.f, b1 = 0.f, sB = 0.f;
+    float a0[RB], a1[RB];
+    bool ok[RB];
+    int sg[RB];
 #pragma unroll
-    for (int gi = 0; gi < 4; gi++) {
-        const int g = gb + gi;
-        if (g < ge) {
-            const int e0 = g * 512 + lane * 16;
-            if (e0 < K) {
-                uint32_t wa[8], wb[8];
-                if (okA) tile_w16<PACKED>(tA, tabA, rA, K, e0, wa);
-                if (okB) tile_w16<PACKED>(tB, tabB, rB, K, e0, wb);
-                if (okA) {
+    for (int r = 0; r < RB; r++) {
+        int row = 0, seg = 0;
+        ok[r] = task_of(p, c, r, row, seg);
+        sg[r] = seg;
+        a0[r] = 0.f;
+        a1[r] = 0.f;
+    }
 #pragma unroll
-                    for (int k = 0; k < 8; k++) {
-                        fma_bf16x2(wa[k], xr[gi][k], a0, a1);
-                        if (okB) fma_bf16x2(wb[k], xr[gi][k], b0, b1);
-                    }
-                } else if (okB) {
+    for (int gi = 0; gi < GB; gi++) {
 #pragma unroll
-                    for (int k = 0; k < 8; k++) fma_bf16x2(wb[k], xr[gi][k], b0, b1);
-                }
-            }
-            if (gi == 2 || g == ge - 1) {  // end of a 1536-weight segment
-                sA = a0 + a1;
-                tA_ = tA_ + sA;
-                sB = b0 + b1;
-                tB_ = tB_ + sB;
-                a0 = a1 = b0 = b1 = 0.f;
+        for (int r = 0; r < RB; r++) {
+            const int g = 3 * sg[r] + gi, e0 = g * 512 + lane * 16;
+            if (ok[r] && g < p.G && e0 < p.K) {
+                uint32_t xp[8];
+                const uint4 xa = xs4[g * 64 + lane], xb = xs4[g * 64 + 32 + lane];
+                xp[0] = xa.x; xp[1] = xa.y; xp[2] = xa.z; xp[3] = xa.w;
+                xp[4] = xb.x; xp[5] = xb.y; xp[6] = xb.z; xp[7] = xb.w;
+                uint32_t wp[8];
+                weights16<PACKED>(b, r, gi, wp);
+#pragma unroll
+                for (int k = 0; k < 8; k++) fma_bf16x2(wp[k], xp[k], a0[r], a1[r]);
             }
         }
     }
-    outA = raw_segment ? sA : tA_;
-    outB = raw_segment ? sB : tB_;
-}
-
-// Two independent butterfly sums over the warp, interleaved.
-__device__ __forceinline__ void warp_sum2(float& x, float& y) {
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        x += __shfl_xor_sync(0xffffffffu, x, o);
-        y += __shfl_xor_sync(0xffffffffu, y, o);
-    }
-}
-
-// The CTA's weight ring as seen by one warp. Every warp consumes every tile in step order and
-// keeps an identical lead cursor on the tile MEGA_SLOTS ahead; the warp whose release completes
-// a slot's count (rel) issues that tile into the slot.
-struct ConsumerRing {
-    uint64_t* full;    // [MEGA_SLOTS] tile landed (TMA complete_tx)
-    unsigned* rel;     // [MEGA_SLOTS] warps done with the slot's current tile
-    unsigned* issued;  // [MEGA_SLOTS] tiles issued into the slot so far (for the exit drain)
-    uint8_t* ring;     // [MEGA_SLOTS][MEGA_SLOT_DATA], 1024-byte aligned
-    uint8_t* tables;   // [MEGA_SLOTS][MEGA_TABLE_BYTES] .p12 block tables of the tiles
-    int slot;
-    uint32_t parity;  // bit i: phase parity of slot i's next fill
-    Cursor lead;      // the tile MEGA_SLOTS ahead of this warp's next one
-    bool lead_has;
-};
-
-// Issues the weight tile at `c` into ring slot `slot` (one thread). The weights are never
-// written, and the slot's previous tile has been read by every warp (each warp's release follows
-// its last read of the slot), so no proxy fence is needed.
-__device__ __forceinline__ void issue_tile(const Cursor& c, uint8_t* ring, uint8_t* tables, uint64_t* full, int slot) {
-    const TileSpec ts = tile_spec(c.ph, c.b, c.sub);
-    mbar_expect_tx(&full[slot], ts.data_bytes + ts.table_bytes);
-    uint8_t* dst = ring + size_t(slot) * MEGA_SLOT_DATA;
-    if (c.ph.tmap) {
-        tma_load_3d(dst, c.ph.tmap, 0, 0, ts.row0, &full[slot]);
-    } else {
-        tma_load(dst, ts.data, ts.data_bytes, &full[slot]);
-        if (ts.table_bytes) tma_load(tables + size_t(slot) * MEGA_TABLE_BYTES, ts.table, ts.table_bytes, &full[slot]);
-    }
-}
-
-// The warp is done reading slot `s`: count the release; the 8th release refills the slot with
-// the lead tile. Every lane advances the lead cursor.
-__device__ __forceinline__ void release_slot(const MegaArgs& a, ConsumerRing& cr, int s) {
-    __syncwarp();
-    if ((threadIdx.x & 31) == 0) {
-        if (atomicAdd(&cr.rel[s], 1u) == 7u) {
-            cr.rel[s] = 0u;
-            if (cr.lead_has) {
-                issue_tile(cr.lead, cr.ring, cr.tables, cr.full, s);
-                cr.issued[s] += 1u;
-            }
-        }
-    }
-    if (cr.lead_has) cr.lead_has = cursor_next(a, cr.lead, blockIdx.x, gridDim.x);
-}
-
-// Output of row `row` (the full dot product v) of a weight phase. SwiGLU rows only park their
-// gate / up sums in shared memory (glu[2 * (row - row0) + sub]); the CTA finishes them together
-// at the end of the phase (swiglu_rows).
-__device__ __forceinline__ void emit_row(const MegaArgs& a, int kind, int row, float v, int sub, float* glu, int row0,
-                                         unsigned long long* best) {
-    if (kind == MK_GU) {
-        glu[2 * (row - row0) + sub] = v;
-    } else if (kind == MK_HEAD) {
-        const uint32_t bits = f2bf(v);
-        a.logits[row] = uint16_t(bits);
-        const unsigned long long key = argmax_key(bf2f(bits), uint32_t(row));
-        *best = key > *best ? key : *best;
-    } else {
-        uint16_t* out = kind == MK_QKV ? a.qkv : (kind == MK_O ? a.po : a.pd);
-        out[row] = uint16_t(f2bf(v));
-    }
-}
-
-// One weight phase: every tile of this CTA's blocks, in the producer's order, two tiles at a
-// time (a SwiGLU block's gate and up tiles, otherwise consecutive blocks) so that every warp
-// carries two independent rows. Rows of up to 2048 weights: warp w computes row w of each tile.
-// Longer rows (down_proj) are split into their 1536-weight segments: warp w computes segment
-// w % nseg of row w / nseg, the segment sums meet in shared memory (double-buffered by pair) and
-// one warp per row folds them in segment order, the same arithmetic as one warp walking the
-// whole row. After a timed-out wait the warp stops computing but keeps walking the schedule
-// (later waits fail at once, and split pairs still take their barrier), so all consumer warps
-// reach the phase end together.
-template <bool PACKED>
-__device__ __forceinline__ void gemv_phase(const MegaArgs& a, const MegaPhase& ph, ConsumerRing& cr, const uint16_t* xs,
-                                           float* part, unsigned long long* best, unsigned long long* dt) {
-    int nt = 0;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int K = ph.lin.K, G = (K + 511) >> 9;
-    const bool split = G > 4;
-    const int nseg = split ? (G + 2) / 3 : 1;
-    const int gb = split ? 3 * (warp % nseg) : 0, ge = split ? min(G, gb + 3) : G;
-    // this warp's activations in registers for the whole phase
-    uint32_t xr[4][8];
-    const uint4* xs4 = reinterpret_cast<const uint4*>(xs);
-#pragma unroll
-    for (int gi = 0; gi < 4; gi++) {
-        const int g = gb + gi;
-        uint4 xa = make_uint4(0, 0, 0, 0), xb = xa;
-        if (g < ge) {
-            xa = xs4[g * 64 + lane];
-            xb = xs4[g * 64 + 32 + lane];
-        }
-        xr[gi][0] = xa.x; xr[gi][1] = xa.y; xr[gi][2] = xa.z; xr[gi][3] = xa.w;
-        xr[gi][4] = xb.x; xr[gi][5] = xb.y; xr[gi][6] = xb.z; xr[gi][7] = xb.w;
-    }
-    int b0, b1;
-    block_range(ph.out_rows, ph.tile_rows, blockIdx.x, gridDim.x, b0, b1);
-    const int nsub = ph.kind == MK_GU ? 2 : 1;
-    const int T = (b1 - b0) * nsub;  // tiles of this CTA in this phase
-    const int r = split ? warp / nseg : warp;
-    const int row0 = b0 * ph.tile_rows;
-    float* glu = part + 2 * 512;  // [rows of this CTA][gate, up]
-    for (int k = 0, pair = 0; k < T; k += 2, pair++) {
-        const bool two = k + 1 < T;
-        const int bA = b0 + k / nsub, subA = k % nsub;
-        const int bB = b0 + (k + 1) / nsub, subB = (k + 1) % nsub;
-        const int nA = min(ph.tile_rows, ph.out_rows - bA * ph.tile_rows);
-        const int nB = two ? min(ph.tile_rows, ph.out_rows - bB * ph.tile_rows) : 0;
-        const int sA = cr.slot, sB = cr.slot + 1 == MEGA_SLOTS ? 0 : cr.slot + 1;
-        const bool readyA = mbar_wait(&cr.full[sA], (cr.parity >> sA) & 1u, a.error, ERR_CONSUMER);
-        const bool readyB = two && mbar_wait(&cr.full[sB], (cr.parity >> sB) & 1u, a.error, ERR_CONSUMER);
-        const bool stamp = dt && threadIdx.x == 0 && nt < 4;
-        if (stamp) dt[nt * 4] = gtime();
-        const uint8_t* tA = cr.ring + size_t(sA) * MEGA_SLOT_DATA;
-        const uint8_t* tB = cr.ring + size_t(sB) * MEGA_SLOT_DATA;
-        const uint32_t* tabA = reinterpret_cast<const uint32_t*>(cr.tables + size_t(sA) * MEGA_TABLE_BYTES);
-        const uint32_t* tabB = reinterpret_cast<const uint32_t*>(cr.tables + size_t(sB) * MEGA_TABLE_BYTES);
-        float vA = 0.f, vB = 0.f;
-        lane_partial2<PACKED>(tA, tabA, r, readyA && r < nA, tB, tabB, r, readyB && r < nB, K, gb, ge, xr, split, vA, vB);
-        if (stamp) dt[nt * 4 + 1] = gtime();
-        if (readyA) {
-            release_slot(a, cr, sA);
-            cr.parity ^= 1u << sA;
-            cr.slot = sB;
-        }
-        if (readyB) {
-            release_slot(a, cr, sB);
-            cr.parity ^= 1u << sB;
-            cr.slot = sB + 1 == MEGA_SLOTS ? 0 : sB + 1;
-        }
-        if (!split) {
-            warp_sum2(vA, vB);
-            if (stamp) dt[nt * 4 + 2] = gtime();
-            if (lane == 0) {
-                if (readyA && r < nA) emit_row(a, ph.kind, bA * ph.tile_rows + r, vA, subA, glu, row0, best);
-                if (readyB && r < nB) emit_row(a, ph.kind, bB * ph.tile_rows + r, vB, subB, glu, row0, best);
-            }
-            if (stamp) dt[nt++ * 4 + 3] = gtime();
-            continue;
-        }
-        float* pk = part + (pair & 1) * 512;  // [tile A | tile B][warp][lane]
-        pk[warp * 32 + lane] = vA;
-        pk[256 + warp * 32 + lane] = vB;
-        consumers_sync();
-        // warp w folds the pair's row w: rows 0..nA-1 of tile A, then rows of tile B
-        const bool inA = warp < nA, inB = !inA && warp < nA + nB;
-        if (inA || inB) {
-            const int rr = inA ? warp : warp - nA;
-            const float* src = pk + (inA ? 0 : 256) + rr * nseg * 32 + lane;
-            float t = 0.f;
-            for (int sgi = 0; sgi < nseg; sgi++) t = t + src[sgi * 32];
-            t = warp_sum(t);
-            if (lane == 0) emit_row(a, ph.kind, (inA ? bA : bB) * ph.tile_rows + rr, t, inA ? subA : subB, glu, row0, best);
-        }
-    }
-    if (ph.kind == MK_GU) {  // SwiGLU of this CTA's rows (Kernels.metal:202-210), all threads at once
-        consumers_sync();
-        const int nrows = min(ph.out_rows, b1 * ph.tile_rows) - row0;
-        for (int i = threadIdx.x; i < nrows; i += 256) {
-            const float gq = rbf(glu[2 * i]), uq = rbf(glu[2 * i + 1]);
-            a.act[row0 + i] = uint16_t(f2bf(rbf(rbf(gq / (1.0f + pexp(-gq))) * uq)));
-        }
-    }
-}
-
-// Weight rows per tile (host and device agree): whole rows up to 2048 weights, one row per warp;
-// longer rows take nseg warps each.
-int mega_tile_rows(int K) {
-    const int G = (K + 511) / 512, byslot = MEGA_SLOT_DATA / (K * 2);
-    if (G > 4) return std::min(byslot, 8 / ((G + 2) / 3));
-    return std::max(1, std::min(8, byslot));
+    for (int r = 0; r < RB; r++) res[r] = a0[r] + a1[r];
 }
 
 // ---- attention ---------------------------------------------------------------------------------
-// Shared-memory regions of the attention phase (inside the union region, all 16-byte aligned):
-//   qs   [H][QSM] f32      normed + rotated queries
-//   raw  [ATM][KV*128] bf16 key tile as stored in the cache, later the value tile
-//   rope [ATM][64] u32     RoPE rows of the tile's window coordinates (local layers)
-//   kr   [ATM][KV*128+8]   rotated keys, rows padded to a 16-byte multiple that keeps 16-byte
-//                          loads of 8 consecutive rows on distinct banks (first: q/k/v rows)
-//   sc   [H][per_max] f32  scores, then exp(score - m)
-//   aux  q/k norm weights, the two RoPE rows of this step, this step's key and value
-// The merge of one head reuses raw + rope for up to 64 split partials and kr for the statistics.
+// Shared-memory regions of an attention task (inside the work region, 16-byte aligned):
+//   qs   [HG][QSM] f32         normed + rotated queries of the task's heads
+//   kraw [ATM][128] bf16       key tile as stored in the cache (TMA)
+//   vraw [ATM][128] bf16       value tile (TMA)
+//   rope [ATM][64] u32         RoPE rows of the key tile's window coordinates (local layers, TMA)
+//   kr   [ATM][136] bf16       rotated keys, rows padded so 16-byte loads of 8 rows hit distinct banks
+//   sc   [HG][per_max] f32     scores, then exp(score - m)
+//   aux  knew, vnew [128] bf16 this step's key (cache format) and value; qkvs [768] bf16 the
+//        task's query rows, then this step's key and value rows as produced
+// The merge of a head reuses kraw + vraw for 32 split partials and kr for the split statistics.
+constexpr int QSM = 132;
+constexpr int KRS = 136;
+constexpr int MERGE_CHUNK = 32;
 struct AttnSizes {
-    size_t qs, raw, rope, kr, sc, aux, total;
+    size_t qs, kraw, vraw, rope, kr, sc, aux, total;
 };
-__host__ __device__ inline AttnSizes attn_sizes(int H, int KV, int per_max) {
+__host__ __device__ inline AttnSizes attn_sizes(int per_max) {
     AttnSizes z;
-    z.qs = size_t(H) * QSM * 4;
-    z.raw = size_t(ATM) * KV * 256;
-    z.rope = size_t(ATM) * 256;
-    z.kr = size_t(ATM) * (KV * 128 + 8) * 2;
-    z.sc = size_t(H) * per_max * 4;
-    z.aux = 1024 + size_t(KV) * 512;
-    z.total = z.qs + z.raw + z.rope + z.kr + z.sc + z.aux;
+    z.qs = size_t(MEGA_HG) * QSM * 4;
+    z.kraw = size_t(MEGA_ATM) * 256;
+    z.vraw = size_t(MEGA_ATM) * 256;
+    z.rope = size_t(MEGA_ATM) * 256;
+    z.kr = size_t(MEGA_ATM) * KRS * 2;
+    z.sc = ((size_t(MEGA_HG) * per_max * 4) + 15) & ~size_t(15);
+    z.aux = 2048;
+    z.total = z.qs + z.kraw + z.vraw + z.rope + z.kr + z.sc + z.aux;
     return z;
 }
 
 struct AttnSmem {
     float* qs;
-    uint4* raw;
+    uint16_t *kraw, *vraw;
     uint32_t* rope;
     uint16_t* kr;
     float* sc;
-    uint16_t *qn, *kn;        // q_norm / k_norm weights [128]
-    uint32_t *ropeq, *ropek;  // RoPE rows of the query coordinate and of the key position [64]
-    uint16_t *knew, *vnew;    // this step's key (cache format) and value [KV*128]
+    uint16_t *knew, *vnew, *qkvs;
 };
 
-__device__ __forceinline__ AttnSmem attn_smem(uint8_t* uni, const MegaArgs& a) {
-    const AttnSizes z = attn_sizes(a.H, a.KV, a.attn_per_max);
+__device__ __forceinline__ AttnSmem attn_smem(uint8_t* base, int per_max) {
+    const AttnSizes z = attn_sizes(per_max);
     AttnSmem m;
-    uint8_t* q = uni;
+    uint8_t* q = base;
     m.qs = reinterpret_cast<float*>(q); q += z.qs;
-    m.raw = reinterpret_cast<uint4*>(q); q += z.raw;
+    m.kraw = reinterpret_cast<uint16_t*>(q); q += z.kraw;
+    m.vraw = reinterpret_cast<uint16_t*>(q); q += z.vraw;
     m.rope = reinterpret_cast<uint32_t*>(q); q += z.rope;
     m.kr = reinterpret_cast<uint16_t*>(q); q += z.kr;
     m.sc = reinterpret_cast<float*>(q); q += z.sc;
-    m.qn = reinterpret_cast<uint16_t*>(q);
-    m.kn = m.qn + 128;
-    m.ropeq = reinterpret_cast<uint32_t*>(q + 512);
-    m.ropek = m.ropeq + 64;
-    m.knew = reinterpret_cast<uint16_t*>(q + 1024);
-    m.vnew = m.knew + a.KV * 128;
+    m.knew = reinterpret_cast<uint16_t*>(q);
+    m.vnew = m.knew + 128;
+    m.qkvs = m.knew + 256;
     return m;
 }
 
-// Attention copies are TMA bulk copies, one mbarrier per purpose: key tile + its RoPE rows, this
-// step's q/k/v rows, value tile, merge partials. Thread ISSUER issues every copy; all consumer
-// threads wait on the barrier, so they all track the same phase parities and pending copies.
-enum { AB_K = 0, AB_Q = 1, AB_V = 2, AB_M = 3 };
-constexpr int ISSUER = 32;  // warp 1, lane 0 (thread 0 is the counter-polling thread)
+// The attention copies complete on two mbarriers (key tile + RoPE rows, value tile). Thread
+// ISSUER issues every copy; all threads wait on the barrier, so they all track the same parities.
+enum { AB_K = 0, AB_V = 1 };
+constexpr int ISSUER = 224;  // warp 7: warp 0 polls the hints meanwhile
 struct AttnBars {
-    uint64_t* bar;     // [4] in the shared-memory header
+    uint64_t* bar;     // [2]
     uint32_t parity;   // bit i: parity of barrier i's next completion
     uint32_t pending;  // bit i: copies issued on barrier i and not yet waited for
 };
-__device__ __forceinline__ void ab_wait(const MegaArgs& a, AttnBars& b, int i) {
-    if (mbar_wait(&b.bar[i], (b.parity >> i) & 1u, a.error, ERR_CONSUMER)) b.pending &= ~(1u << i);
+__device__ __forceinline__ bool ab_wait(AttnBars& b, int i, int* error) {
+    const bool ok = mbar_wait(&b.bar[i], (b.parity >> i) & 1u, error);
+    if (ok) b.pending &= ~(1u << i);
     b.parity ^= 1u << i;
+    return ok;
 }
 
 // Window geometry of split s for the step's single row (Runtime.swift:389-395, Kernels.metal:440-470).
 struct SplitGeo {
-    int first, count, begin, end, qcoord, pos, lo, hi;
+    int first, count, qcoord, pos, lo, hi;
 };
 __device__ __forceinline__ SplitGeo split_geo(const MegaArgs& a, const MegaLayer& Ly, const RowDesc& dsc, int s) {
     SplitGeo g;
     g.pos = dsc.pos;
+    int end, begin;
     if (Ly.full) {
-        g.first = 0; g.count = dsc.cstart + dsc.crows; g.end = dsc.pos + 1; g.begin = 0; g.qcoord = dsc.pos;
+        g.first = 0; g.count = dsc.cstart + dsc.crows; end = dsc.pos + 1; begin = 0; g.qcoord = dsc.pos;
     } else {
         g.first = max(0, dsc.cstart - (a.W - 1));
         g.count = dsc.cstart + dsc.crows - g.first;
-        g.end = dsc.pos - g.first + 1;
-        g.begin = max(0, g.end - a.W);
+        end = dsc.pos - g.first + 1;
+        begin = max(0, end - a.W);
         g.qcoord = dsc.pos - g.first;
     }
     int per = (g.count + Ly.splits - 1) / Ly.splits;
     per = (per + 31) & ~31;
     const int k0 = s * per, k1 = min(k0 + per, g.count);
-    g.lo = max(k0, g.begin);
-    g.hi = min(k1, g.end);
+    g.lo = max(k0, begin);
+    g.hi = min(k1, end);
     return g;
 }
+// Splits holding keys form a prefix of the split list (decode rows see their whole window).
+__device__ __forceinline__ int active_splits(const MegaArgs& a, const MegaLayer& Ly, const RowDesc& dsc) {
+    int n = 0;
+    for (int s = 0; s < Ly.splits; s++) {
+        const SplitGeo g = split_geo(a, Ly, dsc, s);
+        if (g.lo < g.hi) n = s + 1;
+    }
+    return n;
+}
 
-// Issuer only: rows [t0, t0 + tk) of the split's cache window (a ring buffer: at most two
+// ISSUER only: rows [t0, t0 + tk) of the split's cache window (a ring buffer: at most two
 // contiguous row ranges) and, for local layers, the RoPE rows of their window coordinates.
-__device__ __forceinline__ void issue_tile(const MegaArgs& a, void* dst, const uint16_t* cache, const SplitGeo& g, int t0,
+__device__ __forceinline__ void issue_rows(const MegaArgs& a, void* dst, const uint16_t* cache, const SplitGeo& g, int t0,
                                            int tk, int cap, uint32_t* rope_dst, uint64_t* bar) {
-    const uint32_t row = uint32_t(a.KV) * 256;
     const uint32_t rb = rope_dst ? uint32_t(tk) * 256u : 0u;
     fence_proxy_async();
-    mbar_expect_tx(bar, uint32_t(tk) * row + rb);
+    mbar_expect_tx(bar, uint32_t(tk) * 256u + rb);
     const int start = (g.first + g.lo + t0) % cap, n1 = min(tk, cap - start);
     const uint8_t* base = reinterpret_cast<const uint8_t*>(cache);
-    tma_load(dst, base + size_t(start) * row, uint32_t(n1) * row, bar);
-    if (tk > n1) tma_load(static_cast<uint8_t*>(dst) + size_t(n1) * row, base, uint32_t(tk - n1) * row, bar);
+    tma_load(dst, base + size_t(start) * 256, uint32_t(n1) * 256u, bar);
+    if (tk > n1) tma_load(static_cast<uint8_t*>(dst) + size_t(n1) * 256, base, uint32_t(tk - n1) * 256u, bar);
     if (rope_dst) tma_load(rope_dst, a.rope_local + size_t(g.lo + t0) * 64, rb, bar);
 }
 
-// Everything a split reads that this step does not write: its first key tile with the tile's
-// RoPE rows (bulk copies), the norm weights and this step's RoPE rows (plain loads; the norm
-// weights are only 2-byte aligned). Issued before the wait for the QKV phase so the copies
-// overlap it; thread 0, the waiting thread, issues nothing. The plain stores are read after the
-// next consumer barrier.
-__device__ __forceinline__ void attention_prefetch(const MegaArgs& a, const MegaLayer& Ly, const SplitGeo& g, const AttnSmem& sm,
-                                   AttnBars& ab) {
-    const int t = threadIdx.x;
-    if (g.lo >= g.hi) return;
-    if (t == ISSUER)
-        issue_tile(a, sm.raw, Ly.keys, g, 0, min(ATM, g.hi - g.lo), Ly.cap, Ly.full ? nullptr : sm.rope, &ab.bar[AB_K]);
-    ab.pending |= 1u << AB_K;
-    if (t >= 64 && t < 192) {
-        sm.qn[t - 64] = Ly.q_norm[t - 64];
-        sm.kn[t - 64] = Ly.k_norm[t - 64];
-    } else if (t >= 192) {
-        const uint32_t* qtab = Ly.full ? a.rope_global : a.rope_local;
-        sm.ropeq[t - 192] = qtab[size_t(g.qcoord) * 64 + (t - 192)];
-        sm.ropek[t - 192] = a.rope_global[size_t(g.pos) * 64 + (t - 192)];
-    }
-}
-
-// Split-K attention task `s` (same arithmetic as k_qkv + k_attn_partial): QK-norm and RoPE of the
-// queries, the append of this step's key/value by the split that holds it, scores, split-local
-// softmax statistics and the unnormalised P.V partial. Expects attention_prefetch's copies issued
-// and a consumer barrier after it.
-__device__ __forceinline__ void attention_split(const MegaArgs& a, const MegaLayer& Ly, const SplitGeo& g, int s, const AttnSmem& sm,
-                                AttnBars& ab, unsigned long long* dt) {
+// One attention task: split s of the layer's key window for query heads [4 hg, 4 hg + 4).
+// Same arithmetic as k_qkv + k_attn_partial. Writes the tagged split partials of its heads.
+// Returns false when a wait gave up.
+__device__ __forceinline__ bool attention_task(const MegaArgs& a, const MegaLayer& Ly, const SplitGeo& g, int s, int hg,
+                                            int task, uint32_t tag, const AttnSmem& sm, AttnBars& ab, unsigned long long* dt) {
     const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
-    const int H = a.H, KV = a.KV, group = H / KV, cap = Ly.cap, per_max = Ly.per_max;
+    const int H = a.H, cap = Ly.cap, per_max = Ly.per_max;
     const bool full = Ly.full != 0;
-    float2* ml = a.part_ml + size_t(s) * H;
-    float* po = a.part_o + size_t(s) * H * 128;
-    if (g.lo >= g.hi) {
-        for (int h = t; h < H; h += 256) ml[h] = make_float2(-INFINITY, 0.f);
-        return;
-    }
-    // this step's q/k/v rows, staged in the rotated-key region (free until the first rotation)
-    uint16_t* qkvs = sm.kr;
+    const int n = g.hi - g.lo, ntiles = (n + MEGA_ATM - 1) / MEGA_ATM;
+    const int newest = g.count - 1;
+    const bool owner = g.lo <= newest && newest < g.hi;
+    const int jnew = owner ? newest - g.lo : -1;  // split-relative row of this step's key
+    if (dt && t == 0) dt[0] = gtime();
+    // key and value tiles (cache rows written by earlier steps) before the queries are ready
     if (t == ISSUER) {
-        const uint32_t bytes = uint32_t(H + 2 * KV) * 256;
-        fence_proxy_async();
-        mbar_expect_tx(&ab.bar[AB_Q], bytes);
-        tma_load(qkvs, a.qkv, bytes, &ab.bar[AB_Q]);
+        issue_rows(a, sm.kraw, Ly.keys, g, 0, min(MEGA_ATM, n), cap, full ? nullptr : sm.rope, &ab.bar[AB_K]);
+        issue_rows(a, sm.vraw, Ly.values, g, 0, min(MEGA_ATM, n), cap, nullptr, &ab.bar[AB_V]);
     }
-    ab.pending |= 1u << AB_Q;
-    if (dt) {
-        dt[0] = gtime();
-        dt[9] = clock64();
+    ab.pending |= (1u << AB_K) | (1u << AB_V);
+    // norm weights and RoPE rows of the warp's head (step-independent): in flight during the wait
+    const int h0 = MEGA_HG * hg, nq = min(MEGA_HG, H - h0);
+    const bool qwarp = warp < nq, kwarp = warp == MEGA_HG && owner;
+    const uint16_t* nwp = qwarp ? Ly.q_norm : Ly.k_norm;
+    const uint32_t* rrow = qwarp ? (full ? a.rope_global : a.rope_local) + size_t(g.qcoord) * 64
+                                 : (full ? a.rope_global + size_t(g.pos) * 64 : nullptr);
+    uint16_t nwv[4];
+    uint32_t csv[4];
+    if (qwarp || kwarp) {
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            nwv[j] = nwp[lane + 32 * j];
+            csv[j] = rrow ? rrow[(lane + 32 * j) & 63] : 0u;
+        }
     }
-    ab_wait(a, ab, AB_Q);
-    if (dt) dt[1] = gtime();
-    ab_wait(a, ab, AB_K);
-    if (dt) dt[2] = gtime();
-    // queries: per-head RMSNorm (w + 1) and RoPE (Kernels.metal:223-252)
-    for (int h = warp; h < H; h += 8) {
-        const uint16_t* src = qkvs + h * 128;
+    // every CTA's q/k/v rows are in (their hints); the group's query rows and, for the split that
+    // holds this step's key, the key and value rows are read once into shared memory
+    bool ok = wait_hints(a.hints, gridDim.x, 1, tag, a.error);
+    if (!ok) return false;
+    ok = gather16<false>(sm.qkvs, a.qkv + h0 * 128, nq * 128, tag, a.error);
+    if (owner && ok) ok = gather16<false>(sm.qkvs + MEGA_HG * 128, a.qkv + H * 128, 256, tag, a.error);
+    if (!__syncthreads_and(ok)) return false;
+    // per-head RMSNorm with w + 1 and RoPE (Kernels.metal:223-252): warp u < 4 for query head
+    // h0 + u; warp 4 for this step's key (rotated at its absolute position on global layers,
+    // stored unrotated on local ones), whose value is copied
+    if (qwarp || kwarp) {
+        const uint16_t* src = sm.qkvs + (qwarp ? warp : MEGA_HG) * 128;
         float v[4], z[4], ss = 0.f;
 #pragma unroll
-        for (int j = 0; j < 4; j++) { v[j] = bf2f(src[lane + 32 * j]); ss = fmaf(v[j], v[j], ss); }
+        for (int j = 0; j < 4; j++) {
+            v[j] = bf2f(src[lane + 32 * j]);
+            ss = fmaf(v[j], v[j], ss);
+        }
         ss = warp_sum(ss);
         const float scale = 1.0f / sqrtf(ss / 128.0f + PLAMO_EPS);
 #pragma unroll
-        for (int j = 0; j < 4; j++) z[j] = rbf(rbf(v[j] * scale) * rbf(bf2f(sm.qn[lane + 32 * j]) + 1.0f));
+        for (int j = 0; j < 4; j++) z[j] = rbf(rbf(v[j] * scale) * rbf(bf2f(nwv[j]) + 1.0f));
+        const size_t slot = size_t(g.pos % cap) * 128;
 #pragma unroll
         for (int j = 0; j < 4; j++) {
             const int d = lane + 32 * j;
-            sm.qs[h * QSM + d] = rope_rotate(z[j], z[(j + 2) & 3], d, sm.ropeq[d & 63]);
-        }
-    }
-    // the split that holds this step's key appends it to the cache (local layers store it
-    // unrotated, global layers rotated) and keeps a copy for its own tiles
-    const int newest = g.count - 1;
-    const bool owner = g.lo <= newest && newest < g.hi;
-    if (owner) {
-        for (int kvh = warp; kvh < KV; kvh += 8) {
-            const uint16_t* src = qkvs + (H + kvh) * 128;
-            float v[4], z[4], ss = 0.f;
-#pragma unroll
-            for (int j = 0; j < 4; j++) { v[j] = bf2f(src[lane + 32 * j]); ss = fmaf(v[j], v[j], ss); }
-            ss = warp_sum(ss);
-            const float scale = 1.0f / sqrtf(ss / 128.0f + PLAMO_EPS);
-#pragma unroll
-            for (int j = 0; j < 4; j++) z[j] = rbf(rbf(v[j] * scale) * rbf(bf2f(sm.kn[lane + 32 * j]) + 1.0f));
-            const size_t slot = (size_t(g.pos % cap) * KV + kvh) * 128;
-#pragma unroll
-            for (int j = 0; j < 4; j++) {
-                const int d = lane + 32 * j;
-                const float k = full ? rope_rotate(z[j], z[(j + 2) & 3], d, sm.ropek[d & 63]) : z[j];
-                const uint16_t kb = uint16_t(f2bf(k)), vb = src[KV * 128 + d];
-                Ly.keys[slot + d] = kb;
-                Ly.values[slot + d] = vb;
-                sm.knew[kvh * 128 + d] = kb;
-                sm.vnew[kvh * 128 + d] = vb;
-            }
-        }
-    }
-    consumers_sync();
-    if (dt) dt[3] = gtime();
-    const int KS = KV * 128 + 8, kvw = KV * 128;
-    const uint16_t* raw16 = reinterpret_cast<const uint16_t*>(sm.raw);
-    const int n = g.hi - g.lo;
-    const int jnew = owner ? newest - g.lo : -1;  // split-relative row of this step's key
-    const int ntiles = (n + ATM - 1) / ATM;
-    // pass 1: scores
-    for (int tile = 0; tile < ntiles; tile++) {
-        const int t0 = tile * ATM, tk = min(ATM, n - t0);
-        if (tile > 0) {
-            consumers_sync();
-            if (t == ISSUER) issue_tile(a, sm.raw, Ly.keys, g, t0, tk, cap, full ? nullptr : sm.rope, &ab.bar[AB_K]);
-            ab.pending |= 1u << AB_K;
-            ab_wait(a, ab, AB_K);
-        }
-        // rotated keys into the padded tile: local keys get the window-relative RoPE
-        // (Kernels.metal:277-285), one thread per (d, d + 64) pair; global keys are copied
-        if (full) {
-            for (int i = t; i < tk * KV * 16; i += 256) {
-                const int j = i / (KV * 16), c = i - j * (KV * 16);
-                const uint16_t* k16 = t0 + j == jnew ? sm.knew : raw16 + j * kvw;
-                reinterpret_cast<uint4*>(sm.kr + j * KS)[c] = reinterpret_cast<const uint4*>(k16)[c];
-            }
-        } else {
-            for (int i = t; i < tk * KV * 64; i += 256) {
-                const int j = KV == 1 ? i >> 6 : i / (KV * 64), e = i - j * (KV * 64);
-                const int d = e & 63, kvoff = (e >> 6) * 128;
-                const uint16_t* k16 = (t0 + j == jnew ? sm.knew : raw16 + j * kvw) + kvoff;
-                const uint32_t cs = sm.rope[j * 64 + d];
-                const float x1 = bf2f(k16[d]), x2 = bf2f(k16[d + 64]);
-                sm.kr[j * KS + kvoff + d] = uint16_t(f2bf(rope_rotate(x1, x2, d, cs)));
-                sm.kr[j * KS + kvoff + d + 64] = uint16_t(f2bf(rope_rotate(x2, x1, d + 64, cs)));
-            }
-        }
-        consumers_sync();
-        if (dt) dt[4] = gtime();
-        if (tile == ntiles - 1) {  // the raw tile is free: start the first value tile
-            if (t == ISSUER) issue_tile(a, sm.raw, Ly.values, g, 0, min(ATM, n), cap, nullptr, &ab.bar[AB_V]);
-            ab.pending |= 1u << AB_V;
-        }
-        // scores: thread (key j, head quarter hq) computes heads hq, hq + 4, hq + 8, hq + 12 side by
-        // side, each one fma chain over d = 0..127 as the multi-kernel path
-        const int j = t & (ATM - 1), hq = t >> 6;
-        if (j < tk) {
-            const float4* q4[4];
-            const uint4* k4[4];
-            float acc[4];
-#pragma unroll
-            for (int u = 0; u < 4; u++) {
-                const int h = min(hq + 4 * u, H - 1);
-                q4[u] = reinterpret_cast<const float4*>(sm.qs + h * QSM);
-                k4[u] = reinterpret_cast<const uint4*>(sm.kr + j * KS + (h / group) * 128);
-                acc[u] = 0.f;
-            }
-#pragma unroll 2
-            for (int c = 0; c < 16; c++) {
-#pragma unroll
-                for (int u = 0; u < 4; u++) {
-                    const uint4 kk = KV == 1 ? k4[0][c] : k4[u][c];
-                    const float4 qa = q4[u][2 * c], qb = q4[u][2 * c + 1];
-                    acc[u] = fmaf(qa.x, lo_bf(kk.x), acc[u]);
-                    acc[u] = fmaf(qa.y, hi_bf(kk.x), acc[u]);
-                    acc[u] = fmaf(qa.z, lo_bf(kk.y), acc[u]);
-                    acc[u] = fmaf(qa.w, hi_bf(kk.y), acc[u]);
-                    acc[u] = fmaf(qb.x, lo_bf(kk.z), acc[u]);
-                    acc[u] = fmaf(qb.y, hi_bf(kk.z), acc[u]);
-                    acc[u] = fmaf(qb.z, lo_bf(kk.w), acc[u]);
-                    acc[u] = fmaf(qb.w, hi_bf(kk.w), acc[u]);
+            const float r = rrow ? rope_rotate(z[j], z[(j + 2) & 3], d, csv[j]) : z[j];
+            if (qwarp) {
+                sm.qs[warp * QSM + d] = r;
+            } else {
+                const uint16_t kb = uint16_t(f2bf(r)), vb = sm.qkvs[(MEGA_HG + 1) * 128 + d];
+                sm.knew[d] = kb;
+                sm.vnew[d] = vb;
+                if (hg == 0) {  // one task of the owning split appends to the cache
+                    Ly.keys[slot + d] = kb;
+                    Ly.values[slot + d] = vb;
                 }
             }
-#pragma unroll
-            for (int u = 0; u < 4; u++)
-                if (hq + 4 * u < H) sm.sc[(hq + 4 * u) * per_max + t0 + j] = acc[u] * PLAMO_ATTN_SCALE;
         }
     }
-    consumers_sync();
-    if (dt) dt[5] = gtime();
-    // pass 2: split-local softmax statistics; warp w handles heads w and w + 8 side by side
-    {
-        const int h0 = warp, h1 = min(warp + 8, H - 1);
-        const bool two = warp + 8 < H;
-        if (h0 < H) {
-            float* p0 = sm.sc + h0 * per_max;
-            float* p1 = sm.sc + h1 * per_max;
-            float m0 = -INFINITY, m1 = -INFINITY;
-            for (int i = lane; i < n; i += 32) {
-                m0 = fmaxf(m0, p0[i]);
-                m1 = fmaxf(m1, p1[i]);
+    __syncthreads();
+    if (dt && t == 0) dt[1] = gtime();
+    const uint16_t* vnew = sm.vnew;
+    // pass 1: scores. Thread (key j, head u) runs one fma chain over d = 0..127 (k_attn_partial order).
+    for (int tile = 0; tile < ntiles; tile++) {
+        const int t0 = tile * MEGA_ATM, tk = min(MEGA_ATM, n - t0);
+        if (tile > 0) {
+            __syncthreads();
+            if (t == ISSUER) issue_rows(a, sm.kraw, Ly.keys, g, t0, tk, cap, full ? nullptr : sm.rope, &ab.bar[AB_K]);
+            ab.pending |= 1u << AB_K;
+        }
+        if (!ab_wait(ab, AB_K, a.error)) ok = false;
+        if (!__syncthreads_and(ok)) return false;
+        // keys into the padded tile: local keys get the window-relative RoPE (Kernels.metal:277-285),
+        // one thread per (d, d + 64) pair; global keys are copied
+        if (full) {
+            for (int i = t; i < tk * 16; i += 256) {
+                const int j = i >> 4, c = i & 15;
+                const uint16_t* k16 = t0 + j == jnew ? sm.knew : sm.kraw + j * 128;
+                reinterpret_cast<uint4*>(sm.kr + j * KRS)[c] = reinterpret_cast<const uint4*>(k16)[c];
             }
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-                m0 = fmaxf(m0, __shfl_xor_sync(0xffffffffu, m0, o));
-                m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, o));
-            }
-            float l0 = 0.f, l1 = 0.f;
-            for (int i = lane; i < n; i += 32) {
-                const float e0 = pexp(p0[i] - m0), e1 = pexp(p1[i] - m1);
-                l0 += e0;
-                l1 += e1;
-                p0[i] = e0;
-                if (two) p1[i] = e1;
-            }
-            warp_sum2(l0, l1);
-            if (lane == 0) {
-                ml[h0] = make_float2(m0, l0);
-                if (two) ml[h1] = make_float2(m1, l1);
+        } else {
+            for (int i = t; i < tk * 64; i += 256) {
+                const int j = i >> 6, dd = i & 63;
+                const uint16_t* k16 = t0 + j == jnew ? sm.knew : sm.kraw + j * 128;
+                const uint32_t cs = sm.rope[j * 64 + dd];
+                const float x1 = bf2f(k16[dd]), x2 = bf2f(k16[dd + 64]);
+                sm.kr[j * KRS + dd] = uint16_t(f2bf(rope_rotate(x1, x2, dd, cs)));
+                sm.kr[j * KRS + dd + 64] = uint16_t(f2bf(rope_rotate(x2, x1, dd + 64, cs)));
             }
         }
+        __syncthreads();
+        const int j = t & (MEGA_ATM - 1), u = t >> 6;
+        if (j < tk && MEGA_HG * hg + u < H) {
+            const float4* q4 = reinterpret_cast<const float4*>(sm.qs + u * QSM);
+            const uint4* k4 = reinterpret_cast<const uint4*>(sm.kr + j * KRS);
+            float acc = 0.f;
+#pragma unroll 4
+            for (int c = 0; c < 16; c++) {
+                const uint4 kk = k4[c];
+                const float4 qa = q4[2 * c], qb = q4[2 * c + 1];
+                acc = fmaf(qa.x, lo_bf(kk.x), acc);
+                acc = fmaf(qa.y, hi_bf(kk.x), acc);
+                acc = fmaf(qa.z, lo_bf(kk.y), acc);
+                acc = fmaf(qa.w, hi_bf(kk.y), acc);
+                acc = fmaf(qb.x, lo_bf(kk.z), acc);
+                acc = fmaf(qb.y, hi_bf(kk.z), acc);
+                acc = fmaf(qb.z, lo_bf(kk.w), acc);
+                acc = fmaf(qb.w, hi_bf(kk.w), acc);
+            }
+            sm.sc[u * per_max + t0 + j] = acc * PLAMO_ATTN_SCALE;
+        }
     }
-    consumers_sync();
-    if (dt) dt[6] = gtime();
-    // pass 3: unnormalised P.V
-    // thread (d, hh) accumulates heads hh, hh + 2, ... (at most 8: H <= 16 on this path), each
+    __syncthreads();
+    if (dt && t == 0) dt[2] = gtime();
+    // pass 2: split-local softmax statistics, warp u for head u (lane-strided sums, butterfly)
+    if (warp < MEGA_HG && MEGA_HG * hg + warp < H) {
+        const int h = MEGA_HG * hg + warp;
+        float* p0 = sm.sc + warp * per_max;
+        float m0 = -INFINITY;
+        for (int i = lane; i < n; i += 32) m0 = fmaxf(m0, p0[i]);
+        m0 = warp_max(m0);
+        float l0 = 0.f;
+        for (int i = lane; i < n; i += 32) {
+            const float e0 = pexp(p0[i] - m0);
+            l0 += e0;
+            p0[i] = e0;
+        }
+        l0 = warp_sum(l0);
+        if (lane == 0) {
+            st_tag64(a.part_ml + (size_t(s) * H + h) * 2, tagged64(tag, m0));
+            st_tag64(a.part_ml + (size_t(s) * H + h) * 2 + 1, tagged64(tag, l0));
+        }
+    }
+    __syncthreads();
+    if (dt && t == 0) dt[3] = gtime();
+    // pass 3: unnormalised P.V; thread (d, hh) accumulates heads hh and hh + 2 of the group, each
     // one chain over the split's keys in order
     const int d = t & 127, hh = t >> 7;
-    float acc[8];
-#pragma unroll
-    for (int q = 0; q < 8; q++) acc[q] = 0.f;
+    float acc0 = 0.f, acc1 = 0.f;
+    const float* p0 = sm.sc + hh * per_max;
+    const float* p1 = sm.sc + (hh + 2) * per_max;
     for (int tile = 0; tile < ntiles; tile++) {
-        const int t0 = tile * ATM, tk = min(ATM, n - t0);
+        const int t0 = tile * MEGA_ATM, tk = min(MEGA_ATM, n - t0);
         if (tile > 0) {
-            consumers_sync();
-            if (t == ISSUER) issue_tile(a, sm.raw, Ly.values, g, t0, tk, cap, nullptr, &ab.bar[AB_V]);
+            __syncthreads();
+            if (t == ISSUER) issue_rows(a, sm.vraw, Ly.values, g, t0, tk, cap, nullptr, &ab.bar[AB_V]);
             ab.pending |= 1u << AB_V;
         }
-        ab_wait(a, ab, AB_V);
-        if (dt) dt[7] = gtime();
-        // probability rows of this thread's heads (clamped to a valid row; results of heads >= H
-        // are never stored)
-        const float* pq[8];
+        if (!ab_wait(ab, AB_V, a.error)) ok = false;
+        if (!__syncthreads_and(ok)) return false;
+        int i = 0;
+        for (; i + 4 <= tk; i += 4) {
+            float v[4];
 #pragma unroll
-        for (int q = 0; q < 8; q++) pq[q] = sm.sc + min(hh + 2 * q, H - 1) * per_max + t0;
-        if (KV == 1) {
-            int i = 0;
-            for (; i + 4 <= tk; i += 4) {  // four keys per round: 16-byte probability loads
-                float v[4];
-#pragma unroll
-                for (int u = 0; u < 4; u++) v[u] = bf2f((t0 + i + u == jnew ? sm.vnew : raw16 + (i + u) * 128)[d]);
-#pragma unroll
-                for (int q = 0; q < 8; q++) {
-                    const float4 pr = *reinterpret_cast<const float4*>(pq[q] + i);
-                    acc[q] = fmaf(pr.x, v[0], acc[q]);
-                    acc[q] = fmaf(pr.y, v[1], acc[q]);
-                    acc[q] = fmaf(pr.z, v[2], acc[q]);
-                    acc[q] = fmaf(pr.w, v[3], acc[q]);
-                }
-            }
-            for (; i < tk; i++) {
-                const float v = bf2f((t0 + i == jnew ? sm.vnew : raw16 + i * 128)[d]);
-#pragma unroll
-                for (int q = 0; q < 8; q++) acc[q] = fmaf(pq[q][i], v, acc[q]);
-            }
-        } else {
-            const float* sct = sm.sc + hh * per_max + t0;
-            for (int i = 0; i < tk; i++) {
-                const uint16_t* vr = t0 + i == jnew ? sm.vnew : raw16 + i * kvw;
-#pragma unroll
-                for (int q = 0; q < 8; q++) {
-                    const int h = hh + 2 * q;
-                    if (h < H) acc[q] = fmaf(sct[2 * q * per_max + i], bf2f(vr[(h / group) * 128 + d]), acc[q]);
-                }
-            }
+            for (int u = 0; u < 4; u++) v[u] = bf2f((t0 + i + u == jnew ? vnew : sm.vraw + (i + u) * 128)[d]);
+            const float4 pa = *reinterpret_cast<const float4*>(p0 + t0 + i);
+            const float4 pb = *reinterpret_cast<const float4*>(p1 + t0 + i);
+            acc0 = fmaf(pa.x, v[0], acc0);
+            acc0 = fmaf(pa.y, v[1], acc0);
+            acc0 = fmaf(pa.z, v[2], acc0);
+            acc0 = fmaf(pa.w, v[3], acc0);
+            acc1 = fmaf(pb.x, v[0], acc1);
+            acc1 = fmaf(pb.y, v[1], acc1);
+            acc1 = fmaf(pb.z, v[2], acc1);
+            acc1 = fmaf(pb.w, v[3], acc1);
+        }
+        for (; i < tk; i++) {
+            const float v = bf2f((t0 + i == jnew ? vnew : sm.vraw + i * 128)[d]);
+            acc0 = fmaf(p0[t0 + i], v, acc0);
+            acc1 = fmaf(p1[t0 + i], v, acc1);
         }
     }
-#pragma unroll
-    for (int q = 0; q < 8; q++)
-        if (hh + 2 * q < H) po[(hh + 2 * q) * 128 + d] = acc[q];
-    if (dt) {
-        dt[8] = gtime();
-        dt[10] = clock64();
-    }
+    const int ha = h0 + hh, hb = ha + 2;
+    if (ha < H) st_tag64(a.part_o + (size_t(s) * H + ha) * 128 + d, tagged64(tag, acc0));
+    if (hb < H) st_tag64(a.part_o + (size_t(s) * H + hb) * 128 + d, tagged64(tag, acc1));
+    __syncthreads();  // the tiles and score rows are free for the next task
+    if (t == 0) st_tag(a.hints + 4 * gridDim.x + H + task, tag);
+    if (dt && t == 0) dt[4] = gtime();
+    return true;
 }
 
-// Merge of head h over the layer's S split partials (Kernels.metal:530-562), run by CTA h once
-// every split has been counted: M = max of the split maxima, w_q = exp(m_q - M), L = sum of
-// w_q * l_q and o = sum of part_o_q * w_q, both in split order; splits without keys are skipped.
-// The partial rows of the head (512 bytes per split) are bulk-copied 64 splits at a time, the
-// first batch together with the statistics loads. Returns false when the wait for the splits
-// gave up.
-constexpr int MERGE_CHUNK = 64;
-__device__ __forceinline__ bool attention_merge_head(const MegaArgs& a, int S, int l, int h, const AttnSmem& sm, AttnBars& ab) {
+// Merge of head h over the layer's first `S` splits (Kernels.metal:530-562): M = max of the split
+// maxima, w_q = exp(m_q - M), L = sum of w_q * l_q and o = sum of part_o_q * w_q, both in split
+// order; splits without keys are skipped. Polls the tagged partials as they land.
+__device__ __forceinline__ bool attention_merge(const MegaArgs& a, int S, int h, uint32_t tag, const AttnSmem& sm, uint32_t out_tag) {
     const int t = threadIdx.x, H = a.H, d = t & 127;
-    __shared__ int merge_stop;
-    if (t == 0) merge_stop = counter_wait(&a.sync[a.nphases + l], unsigned(S), a.error) ? 0 : 1;
-    consumers_sync();
-    if (merge_stop) return false;
-    float* pbuf = reinterpret_cast<float*>(sm.raw);  // [MERGE_CHUNK][128] (raw + rope regions)
-    float* mx = reinterpret_cast<float*>(sm.kr);
-    float* my = mx + S;
-    float* mw = my + S;
-    auto stage = [&](int q0) {
-        if (t == ISSUER) {
-            const int nq = min(MERGE_CHUNK, S - q0);
-            fence_proxy_async();
-            mbar_expect_tx(&ab.bar[AB_M], uint32_t(nq) * 512u);
-            for (int q = 0; q < nq; q++)
-                tma_load(pbuf + q * 128, a.part_o + (size_t(q0 + q) * H + h) * 128, 512u, &ab.bar[AB_M]);
-        }
-        ab.pending |= 1u << AB_M;
-    };
-    stage(0);
-    for (int q = t; q < S; q += 256) {
-        const float2 st = __ldcg(&a.part_ml[size_t(q) * H + h]);
-        mx[q] = st.x;
-        my[q] = st.y;
-    }
-    consumers_sync();
+    const int ngroups = (H + MEGA_HG - 1) / MEGA_HG;
+    // the head's tasks (s, h / 4) for s < S
+    if (!wait_hints(a.hints + 4 * gridDim.x + H + h / MEGA_HG, S, ngroups, tag, a.error)) return false;
+    float* pbuf = reinterpret_cast<float*>(sm.kraw);  // [MERGE_CHUNK][128] over kraw + vraw
+    float* mxy = reinterpret_cast<float*>(sm.kr);      // [S][2] split (max, sum)
+    float* mw = mxy + 2 * S;
+    // the statistics and the first MERGE_CHUNK partial rows, read once each
+    bool ok = gather64(mxy, a.part_ml + size_t(h) * 2, 2 * S, 1, size_t(H) * 2, tag, a.error);
+    if (ok) ok = gather64(pbuf, a.part_o + size_t(h) * 128, min(MERGE_CHUNK, S) * 128, 7, size_t(H) * 128, tag, a.error);
+    if (!__syncthreads_and(ok)) return false;
+    // M: a max, exact in any order (every warp computes it); w_q and the split-order chain for L
+    // run in every warp with the split statistics in registers, broadcast lane by lane
+    const int lane = t & 31;
     float M = -INFINITY;
-    for (int q = 0; q < S; q++) M = fmaxf(M, mx[q]);
-    for (int q = t; q < S; q += 256) mw[q] = my[q] > 0.f ? pexp(mx[q] - M) : -1.f;
-    consumers_sync();
+    for (int q = lane; q < S; q += 32) M = fmaxf(M, mxy[2 * q]);
+    M = warp_max(M);
     float L = 0.f, o = 0.f;
-    for (int q = 0; q < S; q++) {
-        const float w = mw[q];
-        if (w >= 0.f) L = fmaf(w, my[q], L);
-    }
-    for (int q0 = 0; q0 < S; q0 += MERGE_CHUNK) {
-        if (q0 > 0) {
-            consumers_sync();
-            stage(q0);
+    for (int q0 = 0; q0 < S; q0 += 32) {
+        const int q = q0 + lane;
+        const float l = q < S ? mxy[2 * q + 1] : 0.f;
+        const float w = q < S && l > 0.f ? pexp(mxy[2 * q] - M) : -1.f;
+        if (t < 32 && q < S) mw[q] = w;
+        const int nq = min(32, S - q0);
+        for (int j = 0; j < nq; j++) {
+            const float wj = __shfl_sync(FULL_MASK, w, j), lj = __shfl_sync(FULL_MASK, l, j);
+            if (wj >= 0.f) L = fmaf(wj, lj, L);
         }
-        ab_wait(a, ab, AB_M);
+    }
+    __syncthreads();
+    for (int q0 = 0; q0 < S; q0 += MERGE_CHUNK) {
+        const int nq = min(MERGE_CHUNK, S - q0);
+        if (q0 > 0) {
+            __syncthreads();
+            ok = gather64(pbuf, a.part_o + (size_t(q0) * H + h) * 128, nq * 128, 7, size_t(H) * 128, tag, a.error);
+            if (!__syncthreads_and(ok)) return false;
+        }
         if (t < 128) {
-            const int nq = min(MERGE_CHUNK, S - q0);
+#pragma unroll 8
             for (int q = 0; q < nq; q++) {
                 const float w = mw[q0 + q];
                 if (w >= 0.f) o = fmaf(pbuf[q * 128 + d], w, o);
             }
         }
     }
-    if (t < 128) a.att[h * 128 + d] = uint16_t(f2bf(o / L));
+    if (t < 128) st_tag(a.att + h * 128 + d, tagged(out_tag, f2bf(o / L)));
+    __syncthreads();  // the merge buffers are free, the head's rows are stored: raise its hint
+    if (t == 0) st_tag(a.hints + 4 * gridDim.x + h, out_tag);
     return true;
 }
 
-size_t mega_attention_smem(int H, int KV, int per_max) { return attn_sizes(H, KV, per_max).total; }
-
-// The merge keeps 3 x S statistics in the rotated-key region.
-bool mega_merge_fits(int H, int KV, int splits) {
-    (void)H;
-    return size_t(3) * splits * 4 <= attn_sizes(1, KV, 32).kr;
-}
-
 size_t mega_xs_bytes(int kmax) { return size_t(((kmax + 511) / 512) * 512) * 2; }
-
-size_t mega_smem_bytes(int H, int KV, int per_max, int kmax) {
-    const size_t head = 256;  // mbarriers + reduction scratch
-    // ring data 1024-byte aligned (up to 1 KB of padding) + block tables
-    const size_t ring = 1024 + size_t(MEGA_SLOTS) * (MEGA_SLOT_DATA + MEGA_TABLE_BYTES);
-    // activations + split-row segment sums + SwiGLU gate/up sums of this CTA's rows
-    const size_t gemv = mega_xs_bytes(kmax) + 2 * 512 * 4 + size_t(2) * MEGA_GLU_ROWS * 4;
-    return head + ring + std::max(gemv, mega_attention_smem(H, KV, per_max));
+__host__ __device__ inline size_t mega_table_bytes(int nphases, int L) {
+    return (size_t(nphases) * sizeof(MegaPhase) + size_t(L) * sizeof(MegaLayer) + 127) & ~size_t(127);
 }
 
-// NPT: hidden elements per consumer thread (d <= 256 * NPT).
+// dynamic shared memory: [mbarriers, reduction scratch 256][2 x activations][split-row partials]
+// [phase and layer tables][attention]
+size_t mega_smem_bytes(int per_max, int splits_max, int kmax, int nphases, int L) {
+    const size_t head = 256;
+    const size_t fold = size_t(MEGA_FOLD_TASKS) * 32 * 4;
+    size_t att = attn_sizes(per_max).total;
+    // merge statistics (3 x splits floats) live in the rotated-key region
+    if (size_t(3) * splits_max * 4 > attn_sizes(per_max).kr) att = 0;
+    const size_t nbuf = size_t(4) * ((kmax + 7) / 8 * 8);  // two norm rows (d <= kmax)
+    return att ? head + 2 * mega_xs_bytes(kmax) + fold + mega_table_bytes(nphases, L) + nbuf + att : 0;
+}
+
+// NPT: hidden elements per thread (d <= 256 * NPT).
 template <bool PACKED, int NPT>
 __global__ void __launch_bounds__(MEGA_THREADS, 1) k_decode_mega(MegaArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem);        // [6] at 0
-    uint64_t* abar = full + MEGA_SLOTS;                         // [4] attention copy barriers at 48
-    unsigned* rel = reinterpret_cast<unsigned*>(smem + 80);     // [6] slot release counts
-    unsigned* issued = reinterpret_cast<unsigned*>(smem + 104); // [6] tiles issued per slot
-    float* red = reinterpret_cast<float*>(smem + 128);
-    // ring slots on a 1024-byte boundary (the 128-byte swizzle pattern repeats every 1024 bytes)
-    uint8_t* ring = smem + 256 + ((1024u - ((smem_u32(smem) + 256u) & 1023u)) & 1023u);
-    uint8_t* tables = ring + size_t(MEGA_SLOTS) * MEGA_SLOT_DATA;
-    uint8_t* uni = tables + size_t(MEGA_SLOTS) * MEGA_TABLE_BYTES;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    uint64_t* abar = reinterpret_cast<uint64_t*>(smem);  // [2] attention copy barriers
+    float* red = reinterpret_cast<float*>(smem + 64);    // [2][8] norm reduction scratch
+    int rpar = 0;
+    __shared__ int s_flag;
+    // two activation buffers, alternating between consecutive weight phases: a phase's staging
+    // never overwrites the vector that slower warps of the previous phase are still reading
+    uint16_t* const xs_buf = reinterpret_cast<uint16_t*>(smem + 256);
+    float* part = reinterpret_cast<float*>(smem + 256 + 2 * a.xs_bytes);  // [MEGA_FOLD_TASKS][32]
+    // the phase and layer tables, copied once per step (their global copies are not re-read)
+    MegaPhase* const phases = reinterpret_cast<MegaPhase*>(smem + 256 + 2 * a.xs_bytes + MEGA_FOLD_TASKS * 32 * 4);
+    MegaLayer* const layers = reinterpret_cast<MegaLayer*>(phases + a.nphases);
+    // the two norm-weight rows of the next norm prologue, copied in while the phase before runs
+    uint16_t* const nbuf = reinterpret_cast<uint16_t*>(smem + 256 + 2 * a.xs_bytes + MEGA_FOLD_TASKS * 32 * 4 + mega_table_bytes(a.nphases, a.L));
+    uint8_t* attn_base = reinterpret_cast<uint8_t*>(nbuf) + size_t(4) * a.dpad;
+    int wphase = 0;
+    const AttnSmem asm_ = attn_smem(attn_base, a.attn_per_max);
+    const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
     const int G = gridDim.x, cta = blockIdx.x;
-    // ring: every thread walks the tile order; thread 0 issues the first MEGA_SLOTS tiles
-    ConsumerRing cr;
-    cr.full = full;
-    cr.rel = rel;
-    cr.issued = issued;
-    cr.ring = ring;
-    cr.tables = tables;
-    cr.slot = 0;
-    cr.parity = 0;
-    cr.lead_has = cursor_seek(a, cr.lead, cta, G);
-    if (threadIdx.x == 0) {
-        for (int i = 0; i < MEGA_SLOTS; i++) {
-            mbar_init(&full[i], 1);
-            rel[i] = 0u;
-            issued[i] = 0u;
-        }
-        for (int i = 0; i < 4; i++) mbar_init(&abar[i], 1);
+    if (t == 0) {
+        for (int i = 0; i < 2; i++) mbar_init(&abar[i], 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    __syncthreads();
-    for (int i = 0; i < MEGA_SLOTS && cr.lead_has; i++) {
-        if (threadIdx.x == 0) {
-            issue_tile(cr.lead, ring, tables, full, i);
-            issued[i] = 1u;
-        }
-        cr.lead_has = cursor_next(a, cr.lead, cta, G);
+    {
+        const int nw4 = int(sizeof(MegaPhase) / 4) * a.nphases, lw4 = int(sizeof(MegaLayer) / 4) * a.L;
+        for (int i = t; i < nw4; i += MEGA_THREADS) reinterpret_cast<uint32_t*>(phases)[i] = reinterpret_cast<const uint32_t*>(a.phases)[i];
+        for (int i = t; i < lw4; i += MEGA_THREADS) reinterpret_cast<uint32_t*>(layers)[i] = reinterpret_cast<const uint32_t*>(a.layers)[i];
     }
-
-    // ----------------------------------------------------------------------------- consumers
-    const int t = threadIdx.x;
+    __syncthreads();
+    const uint64_t pol = evict_first_policy();
+    // rows of the norm table: layer l: 4l pre-mixer, 4l+1 post-mixer, 4l+2 pre-MLP, 4l+3 post-MLP; 4L final
+    auto prefetch_norms = [&](int r1, int r2) {
+        const int per = a.dpad / 8;
+        for (int i = threadIdx.x; i < 2 * per; i += MEGA_THREADS) {
+            const int which = i >= per, c = i - which * per, row = which ? r2 : r1;
+            if (row >= 0) cp_async16(nbuf + which * a.dpad + c * 8, a.norms + size_t(row) * a.dpad + c * 8);
+        }
+        cp_async_commit();
+    };
+    prefetch_norms(-1, 0);
+    AttnBars ab{abar, 0u, 0u};
     unsigned long long* trace = a.trace && t == 0 ? a.trace + size_t(cta) * (a.nphases + 1) * MEGA_TRACE_STAMPS : nullptr;
     if (trace) trace[a.nphases * MEGA_TRACE_STAMPS] = gtime();
-    uint16_t* xs = reinterpret_cast<uint16_t*>(uni);
-    const AttnSmem asm_ = attn_smem(uni, a);
-    AttnBars ab{abar, 0u, 0u};
+    const uint32_t step = *reinterpret_cast<volatile unsigned*>(a.step);
+    auto tag_of = [&](int layer) -> uint32_t {
+        return uint32_t((static_cast<unsigned long long>(step) * unsigned(a.L + 1) + unsigned(layer)) % 65535ull) + 1u;
+    };
     const RowDesc dsc0 = a.desc[0];
-    unsigned long long best = 0ull;
     const int d = a.d;
-    float xres[NPT];    // residual stream (bf16 values), computed identically by every CTA
-    float w1[NPT], w2[NPT];  // norm factors of the current prologue
-    // Stop decisions are taken by thread 0 and read by all consumers from shared memory after a
-    // barrier, so every consumer warp leaves at the same phase (a split decision would leave the
-    // others waiting at the next named barrier). Two alternating flags: the flag of phase p is
-    // rewritten at phase p + 2, after every consumer passed the barrier of phase p + 1.
-    __shared__ int stop_flag[2];
+    float xres[NPT];  // residual stream (bf16 values), computed identically by every CTA
+#pragma unroll
+    for (int j = 0; j < NPT; j++) xres[j] = 0.f;
+    unsigned long long best = 0ull;
     bool ok = true;
-    for (int p = 0; p < a.nphases; p++) {
-        const MegaPhase ph = a.phases[p];
+
+    // the first weight phase's first chunk of this warp
+    Batch b;
+    PhaseWork pw = phase_work(phases[a.first_weight], cta, G);
+    if (PACKED && warp < pw.nchunk) issue_chunk<PACKED>(pw, warp, b, pol);
+    if (warp == 7 && lane == 0) l2_prefetch_rows(pw, pw.u0, pw.u0 + pw.nu, size_t(256) << 10);
+
+    for (int p = 0; p < a.nphases && ok; p++) {
+        const MegaPhase ph = phases[p];
         const int l = ph.layer;
         if (trace) trace[p * MEGA_TRACE_STAMPS] = gtime();
-        // -- work that does not depend on the previous phase, overlapping the wait
-        MegaLayer Ly;
-        SplitGeo g0;
         if (ph.kind == MK_ATT) {
-            Ly = a.layers[l];
-            if (cta < Ly.splits) {
-                g0 = split_geo(a, Ly, dsc0, cta);
-                attention_prefetch(a, Ly, g0, asm_, ab);
+            const MegaLayer Ly = layers[l];
+            const uint32_t tag = tag_of(l);
+            const int S = active_splits(a, Ly, dsc0);
+            const int ngroups = (a.H + MEGA_HG - 1) / MEGA_HG, ntask = S * ngroups;
+            if (trace) trace[p * MEGA_TRACE_STAMPS + 1] = gtime();
+            for (int task = cta; task < ntask && ok; task += G) {
+                const int s = task / ngroups, hg = task - s * ngroups;
+                const SplitGeo g = split_geo(a, Ly, dsc0, s);
+                unsigned long long* dt = a.trace && l == 0 && task == cta
+                                             ? a.trace + size_t(G) * (a.nphases + 1) * MEGA_TRACE_STAMPS + size_t(cta) * MEGA_TRACE_DETAIL
+                                             : nullptr;
+                ok = attention_task(a, Ly, g, s, hg, task, tag, asm_, ab, dt);
             }
-        } else if (ph.kind == MK_QKV || ph.kind == MK_GU || ph.kind == MK_HEAD) {
-            if (!(ph.kind == MK_QKV && l == 0)) {
-                // post-mixer norm (offset 0.2) before the MLP, post-MLP norm (1/5^1.5) before the
-                // next layer / the head (Runtime.swift:446-450)
-                const bool mlp_in = ph.kind == MK_GU;
-                const MegaLayer& Lp = a.layers[mlp_in ? l : (ph.kind == MK_HEAD ? a.L - 1 : l - 1)];
-                load_norm<NPT>(mlp_in ? Lp.post_mixer : Lp.post_mlp, mlp_in ? 0.2f : a.post_mlp_offset, d, w1);
-            }
-            const uint16_t* nw = ph.kind == MK_HEAD ? a.final_norm
-                                 : (ph.kind == MK_GU ? a.layers[l].pre_mlp : a.layers[l].pre_mixer);
-            load_norm<NPT>(nw, 1.0f, d, w2);
-        }
-        // -- wait for the previous phase (attention completes with one count per merged head)
-        if (p > 0) {
-            const unsigned target = a.phases[p - 1].kind == MK_ATT ? unsigned(a.H) : unsigned(G);
-            if (t == 0)
-                stop_flag[p & 1] = counter_wait(&a.sync[p - 1], target, a.error) ? *reinterpret_cast<volatile int*>(a.error) : 1;
-            consumers_sync();
-            if (stop_flag[p & 1]) { ok = false; break; }
-        }
-        if (trace) trace[p * MEGA_TRACE_STAMPS + 1] = gtime();
-        if (ph.kind == MK_ATT) {
-            int nspl = 0;
-            for (int s = cta; s < Ly.splits; s += G) {
-                if (s != cta) {  // further splits of this CTA (more splits than CTAs)
-                    consumers_sync();
-                    const SplitGeo g = split_geo(a, Ly, dsc0, s);
-                    attention_prefetch(a, Ly, g, asm_, ab);
-                    consumers_sync();
-                    attention_split(a, Ly, g, s, asm_, ab, nullptr);
-                } else {
-                    // detail timeline of the first attention phase (tracing only)
-                    unsigned long long* dt = trace && l == 0 ? a.trace + size_t(G) * (a.nphases + 1) * MEGA_TRACE_STAMPS + size_t(cta) * MEGA_TRACE_DETAIL : nullptr;
-                    attention_split(a, Ly, g0, s, asm_, ab, dt);
-                }
-                nspl++;
-            }
-            consumers_sync();
-            if (t == 0 && nspl) {
-                __threadfence();
-                atomicAdd(&a.sync[a.nphases + l], unsigned(nspl));
-            }
-            bool merged = false;
-            if (cta < a.H) merged = attention_merge_head(a, Ly.splits, l, cta, asm_, ab);
-            consumers_sync();
-            if (t == 0 && merged) {
-                __threadfence();
-                atomicAdd(&a.sync[p], 1u);
-            }
+            if (ok && cta >= G - a.H) ok = attention_merge(a, S, G - 1 - cta, tag, asm_, tag);
             if (trace) trace[p * MEGA_TRACE_STAMPS + 2] = gtime();
             continue;
         }
-        // prologue: the phase's input vector, staged in the permuted layout
+        // ---- weight phase p: pw describes it, b holds this warp's first chunk in flight
+        const int nw = ph.next_weight;
+        const PhaseWork pn = nw < a.nphases ? phase_work(phases[nw], cta, G) : PhaseWork{};
+        if (warp == 7 && lane == 0 && nw < a.nphases) {
+            // the next two weight phases' rows of this CTA into L2 (the first 256 KB of each)
+            l2_prefetch_rows(pn, pn.u0, pn.u0 + pn.nu, size_t(256) << 10);
+            const int nw2 = phases[nw].next_weight;
+            if (nw2 < a.nphases) {
+                const PhaseWork p2 = phase_work(phases[nw2], cta, G);
+                l2_prefetch_rows(p2, p2.u0, p2.u0 + p2.nu, size_t(256) << 10);
+            }
+        }
+        const uint32_t tag = tag_of(ph.kind == MK_HEAD ? a.L : l);
+        uint16_t* const xs = xs_buf + (wphase++ & 1) * (a.xs_bytes / 2);
+        const uint4* const xs4 = reinterpret_cast<const uint4*>(xs);
+        // prologue: the phase's input vector, staged in the permuted layout. Every prologue passes
+        // a CTA barrier, so no warp is still in phase p - 1 when phase p + 1 restages its buffer.
         if (ph.kind == MK_QKV || ph.kind == MK_GU || ph.kind == MK_HEAD) {
-            float z[NPT];
-            if (ph.kind == MK_QKV && l == 0) {
+            float w1[NPT], w2[NPT], z[NPT];
+            const bool first = ph.kind == MK_QKV && l == 0;
+            // norm weights: the post-mixer norm (offset 0.2) before the MLP, the post-MLP norm
+            // (1/5^1.5) before the next layer / the head (Runtime.swift:446-450), then the pre-norm
+            // (offset 1); read from nbuf after the barrier that follows every thread's copy wait
+            const float off1 = ph.kind == MK_GU ? 0.2f : a.post_mlp_offset;
+            cp_async_wait_all();
+            if (first) {
+                __syncthreads();
+                load_norm<NPT>(nbuf + a.dpad, 1.0f, d, w2);
                 const int id0 = a.ids[0];
                 const size_t row = size_t(id0 >= 0 && id0 < a.V ? id0 : 0) * d;
 #pragma unroll
@@ -1121,74 +1052,159 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_decode_mega(MegaArgs a) {
                     xres[j] = i < d ? bf2f(a.embed[row + i]) : 0.f;
                 }
             } else {
-                // residual stream + norm of the previous projection
-                const uint16_t* pin = ph.kind == MK_GU ? a.po : a.pd;
+                // residual stream + norm of the previous projection (o_proj before the MLP,
+                // down_proj before the next layer and the head), as its tagged words land
+                const uint32_t* pin = ph.kind == MK_GU ? a.po : a.pd;
+                const uint32_t itag = tag_of(ph.kind == MK_HEAD ? a.L - 1 : (ph.kind == MK_GU ? l : l - 1));
+                if (!wait_hints(a.hints + (ph.kind == MK_GU ? 1 : 3) * G, G, 1, itag, a.error)) { ok = false; break; }
+                load_norm<NPT>(nbuf, off1, d, w1);
+                load_norm<NPT>(nbuf + a.dpad, 1.0f, d, w2);
+                // the vector lands in this phase's activation buffer, which the norm overwrites only
+                // after its barriers
+                ok = gather16<false>(xs, pin, d, itag, a.error);
+                if (!__syncthreads_and(ok)) break;
                 float pv[NPT];
 #pragma unroll
                 for (int j = 0; j < NPT; j++) {
                     const int i = t + j * 256;
-                    pv[j] = i < d ? bf2f(ldcg16(pin + i)) : 0.f;
+                    pv[j] = i < d ? bf2f(xs[i]) : 0.f;
                 }
-                cnorm<NPT>(pv, d, w1, red, z);
+                if (trace) trace[p * MEGA_TRACE_STAMPS + 1] = gtime();
+                cnorm<NPT>(pv, d, w1, red, rpar, z);
 #pragma unroll
                 for (int j = 0; j < NPT; j++) {
                     const int i = t + j * 256;
                     xres[j] = i < d ? rbf(xres[j] + z[j]) : 0.f;
                 }
             }
-            cnorm<NPT>(xres, d, w2, red, z);
+            cnorm<NPT>(xres, d, w2, red, rpar, z);
+            // every thread has read nbuf (before the norm's barrier): fetch the next prologue's rows
+            if (ph.kind == MK_QKV) prefetch_norms(4 * l + 1, 4 * l + 2);
+            else if (ph.kind == MK_GU) prefetch_norms(4 * l + 3, l + 1 < a.L ? 4 * (l + 1) : 4 * a.L);
 #pragma unroll
             for (int j = 0; j < NPT; j++) {
                 const int i = t + j * 256;
                 if (i < d) {
-                    const uint16_t b = uint16_t(f2bf(z[j]));
-                    xs[xs_index(i)] = b;
-                    if (ph.kind == MK_HEAD && cta == 0) a.hidden[i] = b;
+                    const uint16_t bv = uint16_t(f2bf(z[j]));
+                    xs[xs_index(i)] = bv;
+                    if (ph.kind == MK_HEAD && cta == 0) a.hidden[i] = bv;
                 }
             }
         } else {
-            stage_vec(xs, ph.kind == MK_O ? a.att : a.act, ph.lin.K);
+            // o_proj reads the merged attention rows, down_proj the SwiGLU activations
+            if (pw.nchunk > 0) {
+                ok = ph.kind == MK_O ? wait_hints(a.hints + 4 * G, a.H, 1, tag, a.error)
+                                     : wait_hints(a.hints + 2 * G, G, 1, tag, a.error);
+                if (ok) ok = gather16<true>(xs, ph.kind == MK_O ? a.att : a.act, ph.lin.K, tag, a.error);
+            }
+            if (!__syncthreads_and(ok)) break;
+            if (trace) trace[p * MEGA_TRACE_STAMPS + 1] = gtime();
         }
-        consumers_sync();
-        unsigned long long* gdt = trace && ph.kind == MK_GU && l == 0
-                                      ? a.trace + size_t(G) * (a.nphases + 1) * MEGA_TRACE_STAMPS + size_t(cta) * MEGA_TRACE_DETAIL + 16
-                                      : nullptr;
-        if (gdt) gdt[-1] = gtime();
-        gemv_phase<PACKED>(a, ph, cr, xs, reinterpret_cast<float*>(uni + a.xs_bytes), &best, gdt);
-        consumers_sync();
-        if (trace) trace[p * MEGA_TRACE_STAMPS + 2] = gtime();
-        if (ph.kind != MK_HEAD && t == 0) {
-            __threadfence();
-            atomicAdd(&a.sync[p], 1u);
+        __syncthreads();
+        // raw weights: the first chunk's rows were prefetched into L2 one or two phases ago; its
+        // loads are issued only now, so no burst of loads sits in front of this phase's exchange
+        if (!PACKED && warp < pw.nchunk) issue_chunk<PACKED>(pw, warp, b, pol);
+        // ---- the warp's chunks; each chunk's successor (in this phase or the next weight phase)
+        // is issued before the chunk's sums are reduced and stored
+        for (int c = warp;; c += 8) {
+            const bool have = c < pw.nchunk;
+            float res[RB];
+            if (have) chunk_partials<PACKED>(pw, c, b, xs4, res);
+            if (lane == 0 && c + 8 * MEGA_PF_ROUNDS < pw.nchunk) {  // rolling L2 prefetch of a later chunk of the warp
+                int r0, r1;
+                chunk_rows(pw, c + 8 * MEGA_PF_ROUNDS, r0, r1);
+                l2_prefetch_rows(pw, r0, r1, ~size_t(0));
+            }
+            
+            {  // the successor: chunk c + 8 of this phase, else this warp's first chunk of the next weight phase
+                const bool inph = c + 8 < pw.nchunk;
+                const PhaseWork nx = inph ? pw : pn;
+                const int nc = inph ? c + 8 : warp;
+                if ((inph || (PACKED && nw < a.nphases)) && nc < nx.nchunk) issue_chunk<PACKED>(nx, nc, b, pol);
+            }
+            if (!have) break;
+            if (ph.kind == MK_O || ph.kind == MK_DOWN) {
+                // split-row phases: segment partials meet in shared memory, folded below
+#pragma unroll
+                for (int r = 0; r < RB; r++)
+                    if (r < pw.R && c * pw.R + r < pw.ntask) part[(c * pw.R + r) * 32 + lane] = res[r];
+                if (c + 8 >= pw.nchunk) break;
+                continue;
+            }
+            // whole-row phases: t = 0 + (a0 + a1) (one segment), then the butterfly; lane 8 r
+            // holds task r's sum
+            float v[RB];
+#pragma unroll
+            for (int r = 0; r < RB; r++) v[r] = 0.f + res[r];
+            const float sum = warp_reduce_transposed<RB>(v, lane);
+            const int r = lane >> 3;
+            int row = 0, seg = 0;
+            const bool mine = (lane & 7) == 0 && task_of(pw, c, r, row, seg);
+            if (ph.kind == MK_GU) {
+                // gate sums in lanes 0 .. 8 upc - 8, the matching up sums 8 upc lanes higher
+                const float u = __shfl_down_sync(FULL_MASK, sum, 8 * pw.upc);
+                if (mine && r < pw.upc) {
+                    const float gq = rbf(sum), uq = rbf(u);
+                    st_tag(a.act + row, tagged(tag, f2bf(rbf(rbf(gq / (1.0f + pexp(-gq))) * uq))));
+                }
+            } else if (mine) {
+                const uint32_t bits = f2bf(sum);
+                if (ph.kind == MK_QKV) {
+                    st_tag(a.qkv + row, tagged(tag, bits));
+                } else {
+                    a.logits[row] = uint16_t(bits);
+                    const unsigned long long key = argmax_key(bf2f(bits), uint32_t(row));
+                    best = key > best ? key : best;
+                }
+            }
+            if (c + 8 >= pw.nchunk) break;
         }
+        if (ph.kind == MK_O || ph.kind == MK_DOWN) {
+            // fold each row's segment partials in segment order, then the butterfly (one warp per row)
+            __syncthreads();
+            uint32_t* out = ph.kind == MK_O ? a.po : a.pd;
+            for (int rl = warp; rl < pw.nu; rl += 8) {
+                float s = 0.f;
+                for (int sg = 0; sg < pw.nseg; sg++) s = s + part[(rl * pw.nseg + sg) * 32 + lane];
+                s = warp_sum(s);
+                if (lane == 0) st_tag(out + pw.u0 + rl, tagged(tag, f2bf(s)));
+            }
+        }
+        if (ph.kind != MK_HEAD) {  // this CTA's outputs of the phase are stored: raise its hint
+            __syncthreads();
+            if (t == 0) st_tag(a.hints + (ph.kind == MK_QKV ? 0 : ph.kind == MK_O ? 1 : ph.kind == MK_GU ? 2 : 3) * G + cta, tag);
+        }
+        if (a.trace && lane == 0)  // a phase ends for the CTA when its last warp is done
+            atomicMax(a.trace + (size_t(cta) * (a.nphases + 1) + p) * MEGA_TRACE_STAMPS + 2, gtime());
+        pw = pn;
     }
     // no bulk copy may still be writing this CTA's shared memory when its threads exit (only an
-    // aborted step can leave one pending): wait for the last tile issued into every ring slot and
-    // for the attention copies still outstanding
-    consumers_sync();
-    if (t == 0) {
-        for (int i = 0; i < MEGA_SLOTS; i++)
-            if (issued[i]) mbar_drain(&full[i], (issued[i] - 1u) & 1u, a.error);
-        for (int i = 0; i < 4; i++)
+    // aborted step can leave one pending)
+    __syncthreads();
+    if (t == 0)
+        for (int i = 0; i < 2; i++)
             if ((ab.pending >> i) & 1u) mbar_drain(&abar[i], (ab.parity >> i) & 1u, a.error);
-    }
-    if (!ok) return;
-    // head epilogue: CTA argmax -> global key; the last CTA finishes the step and resets the counters
+    if (!__syncthreads_and(ok)) return;
+    // head epilogue: CTA argmax -> global key; the last CTA finishes the step
     if (trace) trace[a.nphases * MEGA_TRACE_STAMPS + 1] = gtime();
     __shared__ unsigned long long keys8[8];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {  // the emitting lanes of a warp are 0, 8, 16 and 24
+        const unsigned long long other = __shfl_xor_sync(FULL_MASK, best, o);
+        best = other > best ? other : best;
+    }
     if (lane == 0) keys8[warp] = best;
-    consumers_sync();
-    __shared__ unsigned last;
+    __syncthreads();
     if (t == 0) {
-        unsigned long long b = 0ull;
-        for (int w = 0; w < 8; w++) b = keys8[w] > b ? keys8[w] : b;
-        if (b) atomicMax(a.amkey, b);
+        unsigned long long bk = 0ull;
+        for (int w = 0; w < 8; w++) bk = keys8[w] > bk ? keys8[w] : bk;
+        if (bk) atomicMax(a.amkey, bk);
         __threadfence();
-        last = atomicAdd(&a.sync[a.nphases + a.L], 1u) == unsigned(G - 1);
+        s_flag = atomicAdd(a.ticket, 1u) == unsigned(G - 1);
         if (trace) trace[a.nphases * MEGA_TRACE_STAMPS + 2] = gtime();
     }
-    consumers_sync();
-    if (!last || t != 0) return;
+    __syncthreads();
+    if (!s_flag || t != 0) return;
     __threadfence();
     const unsigned long long key = atomicAdd(a.amkey, 0ull);
     const int id = int(argmax_index(key));
@@ -1202,22 +1218,21 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_decode_mega(MegaArgs a) {
         *a.hist_count = c + 1;
     }
     *a.amkey = 0ull;
-    for (int i = 0; i <= a.nphases + a.L; i++) a.sync[i] = 0u;
+    *a.ticket = 0u;
+    *a.step = step + 1u;
     __threadfence();
 }
 
 static const void* mega_kernel(bool packed, int npt) {
     if (packed) {
         if (npt <= 2) return reinterpret_cast<const void*>(k_decode_mega<true, 2>);
-        if (npt <= 6) return reinterpret_cast<const void*>(k_decode_mega<true, 6>);
-        return reinterpret_cast<const void*>(k_decode_mega<true, 16>);
+        return reinterpret_cast<const void*>(k_decode_mega<true, 6>);
     }
     if (npt <= 2) return reinterpret_cast<const void*>(k_decode_mega<false, 2>);
-    if (npt <= 6) return reinterpret_cast<const void*>(k_decode_mega<false, 6>);
-    return reinterpret_cast<const void*>(k_decode_mega<false, 16>);
+    return reinterpret_cast<const void*>(k_decode_mega<false, 6>);
 }
 
-int mega_npt(int d) { return d <= 512 ? 2 : (d <= 1536 ? 6 : 16); }
+int mega_npt(int d) { return d <= 512 ? 2 : 6; }
 
 cudaError_t configure_mega(size_t smem, bool packed, int npt) {
     return cudaFuncSetAttribute(mega_kernel(packed, npt), cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));

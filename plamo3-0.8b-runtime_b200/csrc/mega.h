@@ -6,17 +6,14 @@ namespace plamo {
 
 enum MegaKind { MK_QKV = 0, MK_ATT = 1, MK_O = 2, MK_GU = 3, MK_DOWN = 4, MK_HEAD = 5 };
 
-// One phase of the decode step. Weight phases stream `lin` in tiles of `tile_rows` whole rows
-// (one contiguous byte range per tile; the SwiGLU phase streams a gate tile and an up tile per
-// block of outputs).
+// One phase of the decode step. Weight phases compute `out_rows` outputs of `lin` (the SwiGLU
+// phase: F outputs, each from gate row m and up row F + m).
 struct MegaPhase {
     int kind, layer;
     Linear lin;
-    const uint32_t* rowoff;  // .p12: byte offset of each row's first block in the data region (M+1)
-    int out_rows;            // outputs of the phase (SwiGLU: F)
-    int tile_rows;           // weight rows per tile
-    int next_weight;         // index of the next weight (non-attention) phase; nphases after the last
-    const void* tmap;        // raw weights: 3-D tensor map [rows][K/64][64] bf16, 128-byte swizzle (device memory)
+    const uint32_t* rowoff;  // .p12: byte offset of each row's first block in the data region (M + 1)
+    int out_rows;
+    int next_weight;  // index of the next weight (non-attention) phase; nphases after the last
 };
 
 struct MegaLayer {
@@ -25,6 +22,10 @@ struct MegaLayer {
     int cap, splits, per_max, full;
 };
 
+// Exchange vectors between phases carry their own readiness: every 32-bit word is
+// (tag << 16) | bf16 value, every 64-bit word (tag << 32) | f32 bits, where the tag names the
+// (step, layer) that wrote it. A consumer polls the words it needs until they carry the current
+// tag, so a phase boundary costs one store-to-load trip through L2 and no counters or fences.
 struct MegaArgs {
     const MegaPhase* phases;
     int nphases;
@@ -33,18 +34,27 @@ struct MegaArgs {
     int L;
     const uint16_t* embed;
     const uint16_t* final_norm;
+    const uint16_t* norms;  // [4L + 1][dpad] copy of every norm vector, 16-byte aligned rows
+    int dpad;               // hidden size rounded up to 8
     const uint32_t* rope_local;
     const uint32_t* rope_global;
-    int d, H, KV, F, V, W;
+    int d, H, F, V, W;
     float post_mlp_offset;  // 1 / 5^1.5 (Runtime.swift:450)
     bool phases_packed;     // weights are .p12 tensors
     int attn_per_max;       // largest split width over the layers (shared-memory layout)
-    int xs_bytes;           // staged activations at the start of the union region; split-row sums follow
+    int splits_max;         // largest split count over the layers
+    int xs_bytes;           // staged activations at the start of the work region
     int* ids;          // [1] input token (device-chained: written by the previous step)
     RowDesc* desc;     // [1] position of the token (advanced by the step)
-    uint16_t *qkv, *att, *po, *pd, *act;  // phase outputs: q/k/v rows, attention, o_proj, down_proj, SwiGLU
-    float* part_o;
-    float2* part_ml;
+    uint32_t *qkv, *att, *po, *pd, *act;  // tagged phase outputs: q/k/v rows, attention, o_proj, down_proj, SwiGLU
+    // Readiness hints, one word per producer (CTA, attention task or merged head) holding the tag
+    // of its last finished phase: [0, G) q/k/v, [G, 2G) o_proj, [2G, 3G) SwiGLU, [3G, 4G) down_proj,
+    // [4G, 4G + H) merged heads, then one per attention task. A consumer waits for its producers'
+    // hints with one warp, then reads the tagged words once (re-polling the rare word whose store
+    // is not yet visible), instead of every thread polling the data.
+    uint32_t* hints;
+    unsigned long long* part_o;   // [splits][H][128] tagged split partials P.V
+    unsigned long long* part_ml;  // [splits][H][2] tagged split (max, sum)
     uint16_t* logits;
     uint16_t* hidden;
     unsigned long long* amkey;
@@ -52,27 +62,24 @@ struct MegaArgs {
     int* hist;
     int* hist_count;
     int hist_cap;
-    unsigned* sync;    // [nphases] phase counters, [L] split tickets, [1] final ticket (all reset by the step)
+    unsigned* step;    // [1] steps run so far (source of the tags; never reset)
+    unsigned* ticket;  // [1] CTAs done with the step (reset by the last one)
     int* error;        // set to a non-zero code when a bounded wait times out
     // Optional timeline (null when off): per CTA, per phase, %globaltimer ns at [wait begin, work
-    // begin, work end], then one record [step begin, head epilogue begin, step end].
+    // begin, work end], then one record [step begin, head epilogue begin, step end], then
+    // after all CTAs' records, MEGA_TRACE_DETAIL stamps per CTA of its first attention task of layer 0.
     unsigned long long* trace;
 };
 constexpr int MEGA_TRACE_STAMPS = 3;
-constexpr int MEGA_TRACE_DETAIL = 32;  // per CTA, after the phase records: stamps inside the first attention split,
-                                       // then stamps of the first SwiGLU phase's tile pairs
+constexpr int MEGA_TRACE_DETAIL = 32;
 
-constexpr int MEGA_THREADS = 256;  // 8 warps (2 per scheduler: up to 255 registers each)
-constexpr int MEGA_SLOTS = 6;
-constexpr int MEGA_SLOT_DATA = 24576;    // weight bytes per ring slot (a multiple of 1024)
-constexpr int MEGA_TABLE_BYTES = 512;    // .p12 block-table bytes per ring slot
-constexpr int MEGA_GLU_ROWS = 512;  // SwiGLU rows one CTA may own
+constexpr int MEGA_THREADS = 256;    // 8 warps
+constexpr int MEGA_HG = 4;           // query heads per attention task
+constexpr int MEGA_ATM = 64;         // keys per staged attention tile
+constexpr int MEGA_FOLD_TASKS = 64;  // (row, segment) partials one CTA may hold in a split-row phase
 
-size_t mega_attention_smem(int H, int KV, int per_max);
-size_t mega_smem_bytes(int H, int KV, int per_max, int kmax);
-bool mega_merge_fits(int H, int KV, int splits);
+size_t mega_smem_bytes(int per_max, int splits_max, int kmax, int nphases, int L);
 size_t mega_xs_bytes(int kmax);
-int mega_tile_rows(int K);
 int mega_npt(int d);
 cudaError_t configure_mega(size_t smem, bool packed, int npt);
 int mega_occupancy(size_t smem, bool packed, int npt);

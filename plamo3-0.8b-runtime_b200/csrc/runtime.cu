@@ -404,9 +404,10 @@ static int capture_decode_graph(plamo_runtime& rt) {
     return 0;
 }
 
-// Prepares the persistent decode kernel (decode_mega.cu): the phase table, per-row block offsets of
-// .p12 tensors, exchange buffers and counters. Leaves rt.mega false when the model shape does not
-// fit its shared-memory plan or cooperative launch is unavailable (the multi-kernel path remains).
+// Prepares the persistent decode kernel (decode_mega.cu): the phase table, the tagged exchange
+// buffers and the step counter. Leaves rt.mega false when the model shape is outside the kernel's
+// plan (hidden size <= 1536, one KV head, <= 16 query heads) or cooperative launch is unavailable
+// (the multi-kernel path remains).
 static int setup_mega(plamo_runtime& rt) {
     const char* env = getenv("PLAMO_PERSISTENT");
     if (env && env[0] == '0') return 0;
@@ -415,27 +416,19 @@ static int setup_mega(plamo_runtime& rt) {
     CK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
     CK(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev));
     CK(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
-    if (!coop || c.d > 4096 || c.heads > 16 || c.kv_heads > 8) return 0;
+    if (!coop || c.d > 1536 || c.heads > 16 || c.kv_heads != 1 || c.head_dim != 128) return 0;
+    if (sms < c.heads + 1) return 0;  // one merging CTA per head
     int per_max = 0, splits_max = 0;
     for (const Layer& L : rt.layers) { per_max = std::max(per_max, L.per_max); splits_max = std::max(splits_max, L.splits); }
     const int kmax = std::max(std::max(c.d, c.q_dim()), c.ffn);
-    const size_t smem = mega_smem_bytes(c.heads, c.kv_heads, per_max, kmax);
-    if (smem + 2048 > size_t(optin) || !mega_merge_fits(c.heads, c.kv_heads, splits_max)) return 0;
-    auto tile_rows = [](int K) { return mega_tile_rows(K); };
-    for (int K : {c.d, c.q_dim(), c.ffn})  // a tile holds at least one row; split rows take <= 8 warps
-        if (K * 2 > MEGA_SLOT_DATA || (K + 511) / 512 > 24 || mega_tile_rows(K) < 1) return 0;
-    // block-table copies must be 16-byte aligned and sized: rows x (K/128) x 4 bytes
-    auto table_ok = [&](int K, int tr, int up_rows) {
-        return (size_t(tr) * (K / 128) * 4) % 16 == 0 && (size_t(up_rows) * (K / 128) * 4) % 16 == 0;
+    const int nphases = 5 * c.layers + 1;
+    const size_t smem = mega_smem_bytes(per_max, splits_max, kmax, nphases, c.layers);
+    if (!smem || smem + 2048 > size_t(optin)) return 0;
+    // split-row phases (o_proj, down_proj): a CTA's (row, segment) partials fit the fold buffer
+    auto fold_ok = [&](int rows, int K) {
+        return size_t((rows + sms - 1) / sms) * size_t(((K + 511) / 512 + 2) / 3) <= size_t(MEGA_FOLD_TASKS);
     };
-    if (rt.packed && !(table_ok(c.d, tile_rows(c.d), c.ffn) && table_ok(c.q_dim(), tile_rows(c.q_dim()), 0) &&
-                       table_ok(c.ffn, tile_rows(c.ffn), 0)))
-        return 0;
-    if (sms < c.heads) return 0;  // one merging CTA per head
-    {  // SwiGLU rows per CTA fit the gate/up buffer
-        const int tr = mega_tile_rows(c.d), nb = (c.ffn + tr - 1) / tr;
-        if ((nb + sms - 1) / sms * tr > MEGA_GLU_ROWS) return 0;
-    }
+    if (!fold_ok(c.d, c.q_dim()) || !fold_ok(c.d, c.ffn)) return 0;
     if (configure_mega(smem, rt.packed, mega_npt(c.d)) != cudaSuccess) { cudaGetLastError(); return 0; }
     // per-row first-block byte offsets of a packed matrix (M + 1 entries), from its block table
     auto rowoff = [&](const Linear& lin, const uint32_t*& out) -> int {
@@ -448,69 +441,39 @@ static int setup_mega(plamo_runtime& rt) {
         for (size_t m = 0; m < size_t(lin.M); m++) ro[m] = tab[m * bpr] & ~63u;
         const uint32_t last = tab[blocks - 1];
         ro[lin.M] = (last & ~63u) + ((last & 63u) ? 192u : 256u);
-        uint32_t* d = nullptr;
-        if (rt.dalloc(d, ro.size())) return 1;
-        CK(cudaMemcpy(d, ro.data(), ro.size() * 4, cudaMemcpyHostToDevice));
-        out = d;
+        uint32_t* dptr = nullptr;
+        if (rt.dalloc(dptr, ro.size())) return 1;
+        CK(cudaMemcpy(dptr, ro.data(), ro.size() * 4, cudaMemcpyHostToDevice));
+        out = dptr;
         return 0;
     };
     std::vector<MegaPhase> phases;
     std::vector<MegaLayer> layers;
+    auto weight_phase = [&](int kind, int l, const Linear& lin, int rows) -> int {
+        MegaPhase ph{kind, l, lin, nullptr, rows, 0};
+        if (rowoff(lin, ph.rowoff)) return 1;
+        phases.push_back(ph);
+        return 0;
+    };
     for (int l = 0; l < c.layers; l++) {
         const Layer& L = rt.layers[l];
         MegaLayer ml{L.pre_mixer, L.post_mixer, L.pre_mlp, L.post_mlp, L.q_norm, L.k_norm,
                      L.keys, L.values, L.cap, L.splits, L.per_max, L.full ? 1 : 0};
         layers.push_back(ml);
-        MegaPhase p{};
-        p.layer = l;
-        p.kind = MK_QKV; p.lin = L.qkv; p.out_rows = c.qkv_rows(); p.tile_rows = tile_rows(c.d);
-        if (rowoff(L.qkv, p.rowoff)) return 1;
-        phases.push_back(p);
-        p = MegaPhase{}; p.layer = l; p.kind = MK_ATT; phases.push_back(p);
-        p = MegaPhase{}; p.layer = l; p.kind = MK_O; p.lin = L.o; p.out_rows = c.d; p.tile_rows = tile_rows(c.q_dim());
-        if (rowoff(L.o, p.rowoff)) return 1;
-        phases.push_back(p);
-        p = MegaPhase{}; p.layer = l; p.kind = MK_GU; p.lin = L.gate_up; p.out_rows = c.ffn; p.tile_rows = tile_rows(c.d);
-        if (rowoff(L.gate_up, p.rowoff)) return 1;
-        phases.push_back(p);
-        p = MegaPhase{}; p.layer = l; p.kind = MK_DOWN; p.lin = L.down; p.out_rows = c.d; p.tile_rows = tile_rows(c.ffn);
-        if (rowoff(L.down, p.rowoff)) return 1;
-        phases.push_back(p);
+        if (weight_phase(MK_QKV, l, L.qkv, c.qkv_rows())) return 1;
+        phases.push_back(MegaPhase{MK_ATT, l, Linear{}, nullptr, 0, 0});
+        if (weight_phase(MK_O, l, L.o, c.d) || weight_phase(MK_GU, l, L.gate_up, c.ffn) ||
+            weight_phase(MK_DOWN, l, L.down, c.d))
+            return 1;
     }
-    MegaPhase hp{};
-    hp.kind = MK_HEAD; hp.layer = c.layers; hp.lin = rt.head; hp.out_rows = c.vocab; hp.tile_rows = tile_rows(c.d);
-    if (rowoff(rt.head, hp.rowoff)) return 1;
-    phases.push_back(hp);
-    {  // link every phase to the next weight phase (the weight stream skips attention phases)
+    if (weight_phase(MK_HEAD, c.layers, rt.head, c.vocab)) return 1;
+    {  // link every phase to the next weight phase (attention phases have no weights)
         int nextw = int(phases.size());
         for (int i = int(phases.size()) - 1; i >= 0; i--) {
             phases[i].next_weight = nextw;
             if (phases[i].kind != MK_ATT) nextw = i;
         }
         rt.margs.first_weight = nextw;
-    }
-    if (!rt.packed) {  // raw weights stream through swizzled tensor maps: [rows][K/64][64] bf16
-        PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
-        if (!encode) return 0;
-        std::vector<CUtensorMap> maps(phases.size());
-        for (size_t i = 0; i < phases.size(); i++) {
-            const MegaPhase& ph = phases[i];
-            if (ph.kind == MK_ATT) continue;
-            const cuuint64_t dims[3] = {64, cuuint64_t(ph.lin.K / 64), cuuint64_t(ph.lin.M)};
-            const cuuint64_t strides[2] = {128, cuuint64_t(ph.lin.K) * 2};
-            const cuuint32_t box[3] = {64, cuuint32_t(ph.lin.K / 64), cuuint32_t(ph.tile_rows)};
-            const cuuint32_t unit[3] = {1, 1, 1};
-            if (ph.lin.K % 64 || ph.lin.K / 64 > 256 ||
-                encode(&maps[i], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<uint8_t*>(ph.lin.w), dims, strides, box,
-                       unit, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-                return 0;
-        }
-        CUtensorMap* dmaps = nullptr;
-        if (rt.dalloc(dmaps, maps.size())) return 1;
-        CK(cudaMemcpy(dmaps, maps.data(), maps.size() * sizeof(CUtensorMap), cudaMemcpyHostToDevice));
-        for (size_t i = 0; i < phases.size(); i++)
-            if (phases[i].kind != MK_ATT) phases[i].tmap = dmaps + i;
     }
     MegaArgs& a = rt.margs;
     MegaPhase* dph = nullptr;
@@ -526,17 +489,33 @@ static int setup_mega(plamo_runtime& rt) {
     a.final_norm = rt.final_norm;
     a.rope_local = rt.rope_local;
     a.rope_global = rt.rope_global;
-    a.d = c.d; a.H = c.heads; a.KV = c.kv_heads; a.F = c.ffn; a.V = c.vocab; a.W = c.window;
+    a.d = c.d; a.H = c.heads; a.F = c.ffn; a.V = c.vocab; a.W = c.window;
+    {  // the norm table: [4l + k] = pre-mixer, post-mixer, pre-MLP, post-MLP of layer l; [4L] final
+        a.dpad = (c.d + 7) / 8 * 8;
+        uint16_t* tab = nullptr;
+        if (rt.dalloc(tab, size_t(4 * c.layers + 1) * a.dpad)) return 1;
+        for (int l = 0; l < c.layers; l++) {
+            const Layer& L = rt.layers[l];
+            const uint16_t* src[4] = {L.pre_mixer, L.post_mixer, L.pre_mlp, L.post_mlp};
+            for (int k = 0; k < 4; k++)
+                CK(cudaMemcpy(tab + size_t(4 * l + k) * a.dpad, src[k], size_t(c.d) * 2, cudaMemcpyDeviceToDevice));
+        }
+        CK(cudaMemcpy(tab + size_t(4 * c.layers) * a.dpad, rt.final_norm, size_t(c.d) * 2, cudaMemcpyDeviceToDevice));
+        a.norms = tab;
+    }
     a.post_mlp_offset = float(1.0 / std::pow(5.0, 1.5));
     a.phases_packed = rt.packed;
     a.attn_per_max = per_max;
+    a.splits_max = splits_max;
     a.xs_bytes = int(mega_xs_bytes(kmax));
     a.ids = rt.work.ids;
     a.desc = rt.work.desc;
+    // tagged buffers start at zero: tag 0 is never current
     if (rt.dalloc(a.qkv, c.qkv_rows()) || rt.dalloc(a.att, c.q_dim()) ||
         rt.dalloc(a.po, c.d) || rt.dalloc(a.pd, c.d) || rt.dalloc(a.act, c.ffn) ||
-        rt.dalloc(a.part_o, size_t(splits_max) * c.heads * 128) || rt.dalloc(a.part_ml, size_t(splits_max) * c.heads) ||
-        rt.dalloc(a.sync, size_t(a.nphases + a.L + 1)) || rt.dalloc(a.error, 1) || rt.halloc(rt.h_error, 1))
+        rt.dalloc(a.part_o, size_t(splits_max) * c.heads * 128) || rt.dalloc(a.part_ml, size_t(splits_max) * c.heads * 2) ||
+        rt.dalloc(a.hints, size_t(4) * sms + c.heads + size_t(splits_max) * ((c.heads + MEGA_HG - 1) / MEGA_HG)) ||
+        rt.dalloc(a.step, 1) || rt.dalloc(a.ticket, 1) || rt.dalloc(a.error, 1) || rt.halloc(rt.h_error, 1))
         return 1;
     a.logits = rt.out.logits;
     a.hidden = rt.out.hidden;
@@ -588,8 +567,13 @@ static int mega_check(plamo_runtime& rt) {
     const int code = *rt.h_error;
     *rt.h_error = 0;
     cudaMemset(rt.margs.error, 0, sizeof(int));
-    cudaMemset(rt.margs.sync, 0, sizeof(unsigned) * size_t(rt.margs.nphases + rt.margs.L + 1));
+    cudaMemset(rt.margs.ticket, 0, sizeof(unsigned));
     cudaMemset(rt.margs.amkey, 0, sizeof(unsigned long long));
+    // the aborted step left some exchange words unwritten: move every tag past it
+    unsigned step = 0;
+    cudaMemcpy(&step, rt.margs.step, sizeof(unsigned), cudaMemcpyDeviceToHost);
+    step += 1u;
+    cudaMemcpy(rt.margs.step, &step, sizeof(unsigned), cudaMemcpyHostToDevice);
     return fail("decode step aborted: a bounded device wait timed out (code " + std::to_string(code) + ")");
 }
 
