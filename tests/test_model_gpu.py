@@ -144,6 +144,27 @@ def test_persistent_equals_multikernel(cuda, pkg, tiny_dir, monkeypatch, packed)
     assert set(prof) == {"persistent"} and prof["persistent"]["launches"] == 4
 
 
+def test_persistent_long_context_multi_tile(cuda, pkg, tiny_dir, monkeypatch):
+    """Global-layer splits wider than one 64-key tile (a 2100-token history over 32 splits gives
+    96-key splits): the persistent kernel stages several key and value tiles per split and must
+    still equal the multi-kernel path bit for bit."""
+    mega = pkg.Runtime(tiny_dir, context=2304)
+    monkeypatch.setenv("PLAMO_PERSISTENT", "0")
+    multi = pkg.Runtime(tiny_dir, context=2304)
+    monkeypatch.delenv("PLAMO_PERSISTENT")
+    assert mega.persistent and not multi.persistent
+    prompt = pkg.synthetic.seeded_tokens(2100, mega.vocab, seed=5)
+    a, b = mega.prefill(prompt), multi.prefill(prompt)
+    for step in range(12):
+        assert a == b, step
+        assert np.array_equal(mega.logits().view(np.uint32), multi.logits().view(np.uint32)), step
+        a, b = mega.forward([a]), multi.forward([b])
+    for layer in range(mega.layers):
+        mk, mv = mega.debug_kv(layer)
+        gk, gv = multi.debug_kv(layer)
+        assert np.array_equal(mk, gk) and np.array_equal(mv, gv), layer
+
+
 def test_reset_and_errors(cuda, pkg, tiny_dir):
     """PlamoTests.swift:204-209 (reset gives bit-identical logits) and the API edge validation
     (Runtime.swift:328-330, :474)."""
