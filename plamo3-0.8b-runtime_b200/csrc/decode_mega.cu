@@ -73,6 +73,10 @@ __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async4(void* dst, const void* src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_but_newest() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 // orders this thread's earlier generic-proxy accesses before its next bulk copies (async proxy)
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async;" ::: "memory"); }
@@ -434,7 +438,7 @@ __device__ __forceinline__ bool task_of(const PhaseWork& p, int c, int r, int& r
 // Issues the weight loads of chunk c (this warp). .p12: the block-table entries first, then the
 // blocks they point at.
 template <bool PACKED>
-__device__ __forceinline__ void issue_chunk(const PhaseWork& p, int c, Batch& b, uint64_t pol) {
+__device__ __forceinline__ void issue_chunk(const PhaseWork& p, int c, Batch& b, uint64_t pol, const uint32_t* tbl) {
     const int lane = threadIdx.x & 31;
     const uint8_t* rp[RB];
     bool ok[RB];
@@ -444,8 +448,12 @@ __device__ __forceinline__ void issue_chunk(const PhaseWork& p, int c, Batch& b,
         int row = 0, seg = 0;
         ok[r] = task_of(p, c, r, row, seg);
         sg[r] = seg;
-        rp[r] = PACKED ? reinterpret_cast<const uint8_t*>(p.off + size_t(row) * (p.K >> 7))
-                       : p.w + size_t(row) * p.K * 2;
+        if (PACKED) {  // the row's block-table entries in this CTA's shared copy (gate rows, then up rows)
+            const int half = p.up && row >= p.up;
+            rp[r] = reinterpret_cast<const uint8_t*>(tbl + size_t(row - half * p.up - p.u0 + half * p.nu) * (p.K >> 7));
+        } else {
+            rp[r] = p.w + size_t(row) * p.K * 2;
+        }
     }
 #pragma unroll
     for (int r = 0; r < RB; r++)
@@ -457,7 +465,7 @@ __device__ __forceinline__ void issue_chunk(const PhaseWork& p, int c, Batch& b,
                     b.w[r][gi][0] = ldw4(rp[r] + e0 * 2, pol);
                     b.w[r][gi][1] = ldw4(rp[r] + e0 * 2 + 16, pol);
                 } else {
-                    b.ent[r][gi] = ldw1(reinterpret_cast<const uint32_t*>(rp[r]) + (e0 >> 7), pol);
+                    b.ent[r][gi] = reinterpret_cast<const uint32_t*>(rp[r])[e0 >> 7];
                 }
             }
         }
@@ -920,14 +928,14 @@ __host__ __device__ inline size_t mega_table_bytes(int nphases, int L) {
 
 // dynamic shared memory: [mbarriers, reduction scratch 256][2 x activations][split-row partials]
 // [phase and layer tables][attention]
-size_t mega_smem_bytes(int per_max, int splits_max, int kmax, int nphases, int L) {
+size_t mega_smem_bytes(int per_max, int splits_max, int kmax, int nphases, int L, int tbl_bytes) {
     const size_t head = 256;
     const size_t fold = size_t(MEGA_FOLD_TASKS) * 32 * 4;
     size_t att = attn_sizes(per_max).total;
     // merge statistics (3 x splits floats) live in the rotated-key region
     if (size_t(3) * splits_max * 4 > attn_sizes(per_max).kr) att = 0;
     const size_t nbuf = size_t(4) * ((kmax + 7) / 8 * 8);  // two norm rows (d <= kmax)
-    return att ? head + 2 * mega_xs_bytes(kmax) + fold + mega_table_bytes(nphases, L) + nbuf + att : 0;
+    return att ? head + 2 * mega_xs_bytes(kmax) + fold + mega_table_bytes(nphases, L) + nbuf + size_t(tbl_bytes) + att : 0;
 }
 
 // NPT: hidden elements per thread (d <= 256 * NPT).
@@ -947,7 +955,9 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_decode_mega(MegaArgs a) {
     MegaLayer* const layers = reinterpret_cast<MegaLayer*>(phases + a.nphases);
     // the two norm-weight rows of the next norm prologue, copied in while the phase before runs
     uint16_t* const nbuf = reinterpret_cast<uint16_t*>(smem + 256 + 2 * a.xs_bytes + MEGA_FOLD_TASKS * 32 * 4 + mega_table_bytes(a.nphases, a.L));
-    uint8_t* attn_base = reinterpret_cast<uint8_t*>(nbuf) + size_t(4) * a.dpad;
+    // .p12: this CTA's block-table entries of the current weight phase, copied at the phase start
+    uint32_t* const tbl = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(nbuf) + size_t(4) * a.dpad);
+    uint8_t* attn_base = reinterpret_cast<uint8_t*>(tbl) + a.tbl_bytes;
     int wphase = 0;
     const AttnSmem asm_ = attn_smem(attn_base, a.attn_per_max);
     const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
@@ -991,7 +1001,6 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_decode_mega(MegaArgs a) {
     // the first weight phase's first chunk of this warp
     Batch b;
     PhaseWork pw = phase_work(phases[a.first_weight], cta, G);
-    if (PACKED && warp < pw.nchunk) issue_chunk<PACKED>(pw, warp, b, pol);
     if (warp == 7 && lane == 0) l2_prefetch_rows(pw, pw.u0, pw.u0 + pw.nu, size_t(256) << 10);
 
     for (int p = 0; p < a.nphases && ok; p++) {
@@ -1029,6 +1038,14 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_decode_mega(MegaArgs a) {
             }
         }
         const uint32_t tag = tag_of(ph.kind == MK_HEAD ? a.L : l);
+        if (PACKED) {  // this CTA's block-table rows of the phase into shared memory (gate rows, then up rows)
+            const int bpr = pw.K >> 7, n32 = pw.nu * bpr;
+            for (int half = 0; half < (pw.up ? 2 : 1); half++) {
+                const uint32_t* src = pw.off + size_t(pw.u0 + half * pw.up) * bpr;
+                for (int i = t; i < n32; i += MEGA_THREADS) cp_async4(tbl + half * n32 + i, src + i);
+            }
+            cp_async_commit();
+        }
         uint16_t* const xs = xs_buf + (wphase++ & 1) * (a.xs_bytes / 2);
         const uint4* const xs4 = reinterpret_cast<const uint4*>(xs);
         // prologue: the phase's input vector, staged in the permuted layout. Every prologue passes
@@ -1040,7 +1057,8 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_decode_mega(MegaArgs a) {
             // (1/5^1.5) before the next layer / the head (Runtime.swift:446-450), then the pre-norm
             // (offset 1); read from nbuf after the barrier that follows every thread's copy wait
             const float off1 = ph.kind == MK_GU ? 0.2f : a.post_mlp_offset;
-            cp_async_wait_all();
+            if (PACKED) cp_async_wait_but_newest();  // the norm rows; the table copy may still run
+            else cp_async_wait_all();
             if (first) {
                 __syncthreads();
                 load_norm<NPT>(nbuf + a.dpad, 1.0f, d, w2);
@@ -1103,7 +1121,11 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_decode_mega(MegaArgs a) {
         __syncthreads();
         // raw weights: the first chunk's rows were prefetched into L2 one or two phases ago; its
         // loads are issued only now, so no burst of loads sits in front of this phase's exchange
-        if (!PACKED && warp < pw.nchunk) issue_chunk<PACKED>(pw, warp, b, pol);
+        if (PACKED) {
+            cp_async_wait_all();
+            __syncthreads();
+        }
+        if (warp < pw.nchunk) issue_chunk<PACKED>(pw, warp, b, pol, tbl);
         // ---- the warp's chunks; each chunk's successor (in this phase or the next weight phase)
         // is issued before the chunk's sums are reduced and stored
         for (int c = warp;; c += 8) {
@@ -1120,7 +1142,7 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_decode_mega(MegaArgs a) {
                 const bool inph = c + 8 < pw.nchunk;
                 const PhaseWork nx = inph ? pw : pn;
                 const int nc = inph ? c + 8 : warp;
-                if ((inph || (PACKED && nw < a.nphases)) && nc < nx.nchunk) issue_chunk<PACKED>(nx, nc, b, pol);
+                if (inph && nc < nx.nchunk) issue_chunk<PACKED>(nx, nc, b, pol, tbl);
             }
             if (!have) break;
             if (ph.kind == MK_O || ph.kind == MK_DOWN) {

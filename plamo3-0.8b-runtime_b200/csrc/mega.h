@@ -44,6 +44,7 @@ struct MegaArgs {
     int attn_per_max;       // largest split width over the layers (shared-memory layout)
     int splits_max;         // largest split count over the layers
     int xs_bytes;           // staged activations at the start of the work region
+    int tbl_bytes;          // .p12: shared copy of one phase's block-table rows of a CTA
     int* ids;          // [1] input token (device-chained: written by the previous step)
     RowDesc* desc;     // [1] position of the token (advanced by the step)
     uint32_t *qkv, *att, *po, *pd, *act;  // tagged phase outputs: q/k/v rows, attention, o_proj, down_proj, SwiGLU
@@ -78,7 +79,7 @@ constexpr int MEGA_HG = 4;           // query heads per attention task
 constexpr int MEGA_ATM = 64;         // keys per staged attention tile
 constexpr int MEGA_FOLD_TASKS = 64;  // (row, segment) partials one CTA may hold in a split-row phase
 
-size_t mega_smem_bytes(int per_max, int splits_max, int kmax, int nphases, int L);
+size_t mega_smem_bytes(int per_max, int splits_max, int kmax, int nphases, int L, int tbl_bytes);
 size_t mega_xs_bytes(int kmax);
 int mega_npt(int d);
 cudaError_t configure_mega(size_t smem, bool packed, int npt);

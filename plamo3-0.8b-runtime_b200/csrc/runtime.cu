@@ -422,7 +422,14 @@ static int setup_mega(plamo_runtime& rt) {
     for (const Layer& L : rt.layers) { per_max = std::max(per_max, L.per_max); splits_max = std::max(splits_max, L.splits); }
     const int kmax = std::max(std::max(c.d, c.q_dim()), c.ffn);
     const int nphases = 5 * c.layers + 1;
-    const size_t smem = mega_smem_bytes(per_max, splits_max, kmax, nphases, c.layers);
+    int tbl_bytes = 0;  // .p12: the largest per-CTA share of one phase's block table
+    if (rt.packed) {
+        auto share = [&](int rows, int K, int halves) { return ((rows + sms - 1) / sms) * (K / 128) * 4 * halves; };
+        tbl_bytes = std::max({share(c.qkv_rows(), c.d, 1), share(c.d, c.q_dim(), 1), share(c.ffn, c.d, 2),
+                              share(c.d, c.ffn, 1), share(c.vocab, c.d, 1)});
+        tbl_bytes = (tbl_bytes + 15) & ~15;
+    }
+    const size_t smem = mega_smem_bytes(per_max, splits_max, kmax, nphases, c.layers, tbl_bytes);
     if (!smem || smem + 2048 > size_t(optin)) return 0;
     // split-row phases (o_proj, down_proj): a CTA's (row, segment) partials fit the fold buffer
     auto fold_ok = [&](int rows, int K) {
@@ -508,6 +515,7 @@ static int setup_mega(plamo_runtime& rt) {
     a.attn_per_max = per_max;
     a.splits_max = splits_max;
     a.xs_bytes = int(mega_xs_bytes(kmax));
+    a.tbl_bytes = tbl_bytes;
     a.ids = rt.work.ids;
     a.desc = rt.work.desc;
     // tagged buffers start at zero: tag 0 is never current
