@@ -323,6 +323,57 @@ __device__ __forceinline__ bool gather64(float* dst, const unsigned long long* s
     return true;
 }
 
+// Two tagged-f32 gathers with every load of both in flight before the first check: (dst1, src1,
+// n1) and (dst2, src2, n2), laid out as in gather64. n1 <= 512 and n2 <= 8 * 256.
+__device__ __forceinline__ bool gather64x2(float* dst1, const unsigned long long* src1, int n1, int rs1, size_t rstride1,
+                                           float* dst2, const unsigned long long* src2, int n2, int rs2, size_t rstride2,
+                                           uint32_t tag, int* error) {
+    const int t = threadIdx.x;
+    const int m1 = (1 << rs1) - 1, m2 = (1 << rs2) - 1;
+    unsigned long long v1[2], v2[8];
+#pragma unroll
+    for (int j = 0; j < 2; j++) {
+        const int i = t + j * 256;
+        v1[j] = i < n1 ? ld_tag64(src1 + size_t(i >> rs1) * rstride1 + (i & m1)) : 0ull;
+    }
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        const int i = t + j * 256;
+        v2[j] = i < n2 ? ld_tag64(src2 + size_t(i >> rs2) * rstride2 + (i & m2)) : 0ull;
+    }
+    unsigned miss = 0;
+#pragma unroll
+    for (int j = 0; j < 2; j++) {
+        const int i = t + j * 256;
+        if (i < n1) {
+            if (uint32_t(v1[j] >> 32) == tag) dst1[i] = __uint_as_float(uint32_t(v1[j]));
+            else miss |= 1u << j;
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        const int i = t + j * 256;
+        if (i < n2) {
+            if (uint32_t(v2[j] >> 32) == tag) dst2[i] = __uint_as_float(uint32_t(v2[j]));
+            else miss |= 1u << (8 + j);
+        }
+    }
+    Spin s;
+    while (miss) {
+        const int k = __ffs(miss) - 1, second = k >= 8, i = t + (k & 7) * 256;
+        const unsigned long long* p = second ? src2 + size_t(i >> rs2) * rstride2 + (i & m2)
+                                             : src1 + size_t(i >> rs1) * rstride1 + (i & m1);
+        const unsigned long long w = ld_tag64(p);
+        if (uint32_t(w >> 32) == tag) {
+            (second ? dst2 : dst1)[i] = __uint_as_float(uint32_t(w));
+            miss &= miss - 1;
+        } else if (!spin_more(s, error, ERR_DATA)) {
+            return false;
+        }
+    }
+    return true;
+}
+
 // ---- weight phases ---------------------------------------------------------------------------
 // A task is (output row, 1536-weight segment of the row): lane l covers weights
 // [g*512 + 16l, +16) of the segment's groups g (at most 3). A warp carries up to RB tasks at a time.
@@ -561,10 +612,10 @@ __device__ __forceinline__ void chunk_partials(const PhaseWork& p, int c, const 
 //   sc   [HG][per_max] f32     scores, then exp(score - m)
 //   aux  knew, vnew [128] bf16 this step's key (cache format) and value; qkvs [768] bf16 the
 //        task's query rows, then this step's key and value rows as produced
-// The merge of a head reuses kraw + vraw for 32 split partials and kr for the split statistics.
+// The merge of a head reuses kraw for 16 split partials and kr for the split statistics.
 constexpr int QSM = 132;
 constexpr int KRS = 136;
-constexpr int MERGE_CHUNK = 32;
+constexpr int MERGE_CHUNK = 16;  // split partial rows per merge pass: 16 x 128 = 8 loads per thread
 struct AttnSizes {
     size_t qs, kraw, vraw, rope, kr, sc, aux, total;
 };
@@ -609,7 +660,7 @@ __device__ __forceinline__ AttnSmem attn_smem(uint8_t* base, int per_max) {
 // The attention copies complete on two mbarriers (key tile + RoPE rows, value tile). Thread
 // ISSUER issues every copy; all threads wait on the barrier, so they all track the same parities.
 enum { AB_K = 0, AB_V = 1 };
-constexpr int ISSUER = 224;  // warp 7: warp 0 polls the hints meanwhile
+constexpr int ISSUER = 192;  // warp 6: warp 0 polls the hints meanwhile; warp 7 issues the L2 prefetches
 struct AttnBars {
     uint64_t* bar;     // [2]
     uint32_t parity;   // bit i: parity of barrier i's next completion
@@ -874,12 +925,12 @@ __device__ __forceinline__ bool attention_merge(const MegaArgs& a, int S, int h,
     const int ngroups = (H + MEGA_HG - 1) / MEGA_HG;
     // the head's tasks (s, h / 4) for s < S
     if (!wait_hints(a.hints + 4 * gridDim.x + H + h / MEGA_HG, S, ngroups, tag, a.error)) return false;
-    float* pbuf = reinterpret_cast<float*>(sm.kraw);  // [MERGE_CHUNK][128] over kraw + vraw
+    float* pbuf = reinterpret_cast<float*>(sm.kraw);  // [MERGE_CHUNK][128] in kraw
     float* mxy = reinterpret_cast<float*>(sm.kr);      // [S][2] split (max, sum)
     float* mw = mxy + 2 * S;
     // the statistics and the first MERGE_CHUNK partial rows, read once each
-    bool ok = gather64(mxy, a.part_ml + size_t(h) * 2, 2 * S, 1, size_t(H) * 2, tag, a.error);
-    if (ok) ok = gather64(pbuf, a.part_o + size_t(h) * 128, min(MERGE_CHUNK, S) * 128, 7, size_t(H) * 128, tag, a.error);
+    bool ok = gather64x2(mxy, a.part_ml + size_t(h) * 2, 2 * S, 1, size_t(H) * 2, pbuf, a.part_o + size_t(h) * 128,
+                         min(MERGE_CHUNK, S) * 128, 7, size_t(H) * 128, tag, a.error);
     if (!__syncthreads_and(ok)) return false;
     // M: a max, exact in any order (every warp computes it); w_q and the split-order chain for L
     // run in every warp with the split statistics in registers, broadcast lane by lane
@@ -894,6 +945,7 @@ __device__ __forceinline__ bool attention_merge(const MegaArgs& a, int S, int h,
         const float w = q < S && l > 0.f ? pexp(mxy[2 * q] - M) : -1.f;
         if (t < 32 && q < S) mw[q] = w;
         const int nq = min(32, S - q0);
+#pragma unroll 8
         for (int j = 0; j < nq; j++) {
             const float wj = __shfl_sync(FULL_MASK, w, j), lj = __shfl_sync(FULL_MASK, l, j);
             if (wj >= 0.f) L = fmaf(wj, lj, L);

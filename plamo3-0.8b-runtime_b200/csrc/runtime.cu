@@ -420,6 +420,7 @@ static int setup_mega(plamo_runtime& rt) {
     if (sms < c.heads + 1) return 0;  // one merging CTA per head
     int per_max = 0, splits_max = 0;
     for (const Layer& L : rt.layers) { per_max = std::max(per_max, L.per_max); splits_max = std::max(splits_max, L.splits); }
+    if (splits_max > 256) return 0;  // the merge gathers a head's split statistics in one pass
     const int kmax = std::max(std::max(c.d, c.q_dim()), c.ffn);
     const int nphases = 5 * c.layers + 1;
     int tbl_bytes = 0;  // .p12: the largest per-CTA share of one phase's block table
