@@ -1184,7 +1184,9 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_decode_mega(MegaArgs a) {
             const bool have = c < pw.nchunk;
             float res[RB];
             if (have) chunk_partials<PACKED>(pw, c, b, xs4, res);
-            if (lane == 0 && c + 8 * MEGA_PF_ROUNDS < pw.nchunk) {  // rolling L2 prefetch of a later chunk of the warp
+            // rolling L2 prefetch of a later chunk of the warp (not in the lm_head phase: a long pure
+            // stream, where the register loads alone keep HBM busier than with the extra requests)
+            if (lane == 0 && ph.kind != MK_HEAD && c + 8 * MEGA_PF_ROUNDS < pw.nchunk) {
                 int r0, r1;
                 chunk_rows(pw, c + 8 * MEGA_PF_ROUNDS, r0, r1);
                 l2_prefetch_rows(pw, r0, r1, ~size_t(0));
