@@ -581,20 +581,43 @@ __device__ __forceinline__ void chunk_partials(const PhaseWork& p, int c, const 
         a0[r] = 0.f;
         a1[r] = 0.f;
     }
+    if (p.nseg == 1) {
+        // every task is its row's only segment: one read of each activation group serves all tasks
 #pragma unroll
-    for (int gi = 0; gi < GB; gi++) {
-#pragma unroll
-        for (int r = 0; r < RB; r++) {
-            const int g = 3 * sg[r] + gi, e0 = g * 512 + lane * 16;
-            if (ok[r] && g < p.G && e0 < p.K) {
+        for (int gi = 0; gi < GB; gi++) {
+            if (gi < p.G) {
                 uint32_t xp[8];
-                const uint4 xa = xs4[g * 64 + lane], xb = xs4[g * 64 + 32 + lane];
+                const uint4 xa = xs4[gi * 64 + lane], xb = xs4[gi * 64 + 32 + lane];
                 xp[0] = xa.x; xp[1] = xa.y; xp[2] = xa.z; xp[3] = xa.w;
                 xp[4] = xb.x; xp[5] = xb.y; xp[6] = xb.z; xp[7] = xb.w;
-                uint32_t wp[8];
-                weights16<PACKED>(b, r, gi, wp);
+                const bool lane_in = gi * 512 + lane * 16 < p.K;
 #pragma unroll
-                for (int k = 0; k < 8; k++) fma_bf16x2(wp[k], xp[k], a0[r], a1[r]);
+                for (int r = 0; r < RB; r++) {
+                    if (ok[r] && lane_in) {
+                        uint32_t wp[8];
+                        weights16<PACKED>(b, r, gi, wp);
+#pragma unroll
+                        for (int k = 0; k < 8; k++) fma_bf16x2(wp[k], xp[k], a0[r], a1[r]);
+                    }
+                }
+            }
+        }
+    } else {
+#pragma unroll
+        for (int gi = 0; gi < GB; gi++) {
+#pragma unroll
+            for (int r = 0; r < RB; r++) {
+                const int g = 3 * sg[r] + gi, e0 = g * 512 + lane * 16;
+                if (ok[r] && g < p.G && e0 < p.K) {
+                    uint32_t xp[8];
+                    const uint4 xa = xs4[g * 64 + lane], xb = xs4[g * 64 + 32 + lane];
+                    xp[0] = xa.x; xp[1] = xa.y; xp[2] = xa.z; xp[3] = xa.w;
+                    xp[4] = xb.x; xp[5] = xb.y; xp[6] = xb.z; xp[7] = xb.w;
+                    uint32_t wp[8];
+                    weights16<PACKED>(b, r, gi, wp);
+#pragma unroll
+                    for (int k = 0; k < 8; k++) fma_bf16x2(wp[k], xp[k], a0[r], a1[r]);
+                }
             }
         }
     }
