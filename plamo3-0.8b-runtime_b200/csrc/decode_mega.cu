@@ -379,7 +379,6 @@ __device__ __forceinline__ bool gather64x2(float* dst1, const unsigned long long
 // [g*512 + 16l, +16) of the segment's groups g (at most 3). A warp carries up to RB tasks at a time.
 constexpr int RB = 4;
 constexpr int GB = 3;
-constexpr int MEGA_PF_ROUNDS = 3;  // the rolling L2 prefetch runs this many chunk rounds ahead
 constexpr uint64_t MEGA_STAGGER_NS = 500;  // start offset between warp pairs in multi-round phases
 
 struct Batch {
@@ -392,7 +391,6 @@ struct PhaseWork {
     int kind, K, G, nseg, R;  // row length, 512-weight groups, segments per row, tasks per chunk
     const uint8_t* w;
     const uint32_t* off;
-    const uint32_t* rowoff;   // .p12: per-row block offsets (M + 1)
     int u0, nu;               // this CTA's outputs [u0, u0 + nu)
     int ntask, nchunk;
     int up;                   // SwiGLU: row offset of the up half
@@ -407,7 +405,6 @@ __device__ __forceinline__ PhaseWork phase_work(const MegaPhase& ph, int cta, in
     p.nseg = (p.G + 2) / 3;
     p.w = ph.lin.w;
     p.off = ph.lin.offsets;
-    p.rowoff = ph.rowoff;
     const int units = ph.out_rows;
     p.u0 = int((long long)units * cta / G);
     p.nu = int((long long)units * (cta + 1) / G) - p.u0;
@@ -425,49 +422,6 @@ __device__ __forceinline__ PhaseWork phase_work(const MegaPhase& ph, int cta, in
         p.nchunk = (p.ntask + p.R - 1) / p.R;
     }
     return p;
-}
-
-// L2 prefetch of weight rows: the bulk-copy engine pulls them from HBM into L2, nothing comes
-// back to the SM, so the stream does not sit in front of the latency-critical exchange loads. The
-// demand loads that follow hit L2.
-__device__ __forceinline__ void l2_prefetch_bytes(const uint8_t* p, size_t bytes) {
-    while (bytes >= 16) {
-        const uint32_t n = uint32_t(bytes < 32768 ? bytes & ~size_t(15) : 32768);
-        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(n) : "memory");
-        p += n;
-        bytes -= n;
-    }
-}
-// Rows [r0, r1) of this CTA's share of phase q (both halves of the SwiGLU phase), at most `cap` bytes per half.
-__device__ __forceinline__ void l2_prefetch_rows(const PhaseWork& q, int r0, int r1, size_t cap) {
-    if (r1 <= r0) return;
-    if (!q.off) {
-        const size_t rb = size_t(q.K) * 2, n = min(size_t(r1 - r0) * rb, cap);
-        l2_prefetch_bytes(q.w + size_t(r0) * rb, n);
-        if (q.up) l2_prefetch_bytes(q.w + size_t(r0 + q.up) * rb, n);
-        return;
-    }
-    // .p12: the rows' blocks (contiguous in the data region) and their block-table entries
-    const int bpr = q.K >> 7;
-    for (int half = 0; half < (q.up ? 2 : 1); half++) {
-        const int a0 = r0 + half * q.up, a1 = r1 + half * q.up;
-        const uint32_t lo = __ldg(q.rowoff + a0), hi = __ldg(q.rowoff + a1);
-        l2_prefetch_bytes(q.w + lo, min(size_t(hi - lo), cap));
-        const uint8_t* t0 = reinterpret_cast<const uint8_t*>(q.off + size_t(a0) * bpr);
-        const uint8_t* ta = reinterpret_cast<const uint8_t*>(reinterpret_cast<uintptr_t>(t0) & ~uintptr_t(15));
-        l2_prefetch_bytes(ta, min(size_t(a1 - a0) * bpr * 4 + size_t(t0 - ta), cap) & ~size_t(15));
-    }
-}
-// Output rows covered by chunk c (the gate half for SwiGLU).
-__device__ __forceinline__ void chunk_rows(const PhaseWork& p, int c, int& r0, int& r1) {
-    if (p.kind == MK_GU) {
-        r0 = p.u0 + c * p.upc;
-        r1 = min(r0 + p.upc, p.u0 + p.nu);
-    } else {
-        const int i0 = c * p.R, i1 = min(i0 + p.R, p.ntask);
-        r0 = p.u0 + i0 / p.nseg;
-        r1 = i1 > i0 ? p.u0 + (i1 - 1) / p.nseg + 1 : r0;
-    }
 }
 
 // Row and segment of task r of chunk c; false when the slot is empty.
@@ -684,7 +638,7 @@ __device__ __forceinline__ AttnSmem attn_smem(uint8_t* base, int per_max) {
 // The attention copies complete on two mbarriers (key tile + RoPE rows, value tile). Thread
 // ISSUER issues every copy; all threads wait on the barrier, so they all track the same parities.
 enum { AB_K = 0, AB_V = 1 };
-constexpr int ISSUER = 192;  // warp 6: warp 0 polls the hints meanwhile; warp 7 issues the L2 prefetches
+constexpr int ISSUER = 192;  // warp 6: warp 0 polls the hints meanwhile
 struct AttnBars {
     uint64_t* bar;     // [2]
     uint32_t parity;   // bit i: parity of barrier i's next completion
@@ -1076,8 +1030,8 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_decode_mega(MegaArgs a) {
 
     // the first weight phase's first chunk of this warp
     Batch b;
+    bool pref_cur = false, pref_next = false;  // b already holds this / the next phase's first chunk
     PhaseWork pw = phase_work(phases[a.first_weight], cta, G);
-    if (warp == 7 && lane == 0) l2_prefetch_rows(pw, pw.u0, pw.u0 + pw.nu, size_t(256) << 10);
 
     for (int p = 0; p < a.nphases && ok; p++) {
         const MegaPhase ph = phases[p];
@@ -1104,15 +1058,6 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_decode_mega(MegaArgs a) {
         // ---- weight phase p: pw describes it, b holds this warp's first chunk in flight
         const int nw = ph.next_weight;
         const PhaseWork pn = nw < a.nphases ? phase_work(phases[nw], cta, G) : PhaseWork{};
-        if (warp == 7 && lane == 0 && nw < a.nphases) {
-            // the next two weight phases' rows of this CTA into L2 (the first 256 KB of each)
-            l2_prefetch_rows(pn, pn.u0, pn.u0 + pn.nu, size_t(256) << 10);
-            const int nw2 = phases[nw].next_weight;
-            if (nw2 < a.nphases) {
-                const PhaseWork p2 = phase_work(phases[nw2], cta, G);
-                l2_prefetch_rows(p2, p2.u0, p2.u0 + p2.nu, size_t(256) << 10);
-            }
-        }
         const uint32_t tag = tag_of(ph.kind == MK_HEAD ? a.L : l);
         if (PACKED) {  // this CTA's block-table rows of the phase into shared memory (gate rows, then up rows)
             const int bpr = pw.K >> 7, n32 = pw.nu * bpr;
@@ -1201,33 +1146,28 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_decode_mega(MegaArgs a) {
             cp_async_wait_all();
             __syncthreads();
         }
-        // Phases of several chunk rounds: warp pair q starts its loads q x 0.5 us after pair 0, so
-        // the pairs take turns between waiting for HBM and summing and the stream does not pause
-        // while all warps compute at once (a 2-way split gains 5%, this 4-way one 7%).
+        // Phases of several chunk rounds: warp pair q starts q x 0.5 us after pair 0 (its first
+        // chunk's loads, or the sums of the chunk it prefetched), so the pairs take turns between
+        // waiting for HBM and summing and the stream does not pause while all warps compute.
         if (pw.nchunk > 8) {
             const uint64_t t0 = gtime(), dly = uint64_t(warp >> 1) * MEGA_STAGGER_NS;
             while (gtime() - t0 < dly) __nanosleep(128);
         }
-        if (warp < pw.nchunk) issue_chunk<PACKED>(pw, warp, b, pol, tbl);
+        if (warp < pw.nchunk && !pref_cur) issue_chunk<PACKED>(pw, warp, b, pol, tbl);
+        pref_cur = false;
         // ---- the warp's chunks; each chunk's successor (in this phase or the next weight phase)
         // is issued before the chunk's sums are reduced and stored
         for (int c = warp;; c += 8) {
             const bool have = c < pw.nchunk;
             float res[RB];
             if (have) chunk_partials<PACKED>(pw, c, b, xs4, res);
-            // rolling L2 prefetch of a later chunk of the warp (not in the lm_head phase: a long pure
-            // stream, where the register loads alone keep HBM busier than with the extra requests)
-            if (lane == 0 && ph.kind != MK_HEAD && c + 8 * MEGA_PF_ROUNDS < pw.nchunk) {
-                int r0, r1;
-                chunk_rows(pw, c + 8 * MEGA_PF_ROUNDS, r0, r1);
-                l2_prefetch_rows(pw, r0, r1, ~size_t(0));
-            }
-            
-            {  // the successor: chunk c + 8 of this phase, else this warp's first chunk of the next weight phase
+            {  // the successor: chunk c + 8 of this phase, else (raw weights) this warp's first chunk of
+               // the next weight phase, in flight across the phase boundary
                 const bool inph = c + 8 < pw.nchunk;
                 const PhaseWork nx = inph ? pw : pn;
                 const int nc = inph ? c + 8 : warp;
-                if (inph && nc < nx.nchunk) issue_chunk<PACKED>(nx, nc, b, pol, tbl);
+                if ((inph || (!PACKED && nw < a.nphases)) && nc < nx.nchunk) issue_chunk<PACKED>(nx, nc, b, pol, tbl);
+                if (!inph && !PACKED) pref_next = nw < a.nphases && nc < nx.nchunk;
             }
             if (!have) break;
             if (ph.kind == MK_O || ph.kind == MK_DOWN) {
@@ -1284,6 +1224,8 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_decode_mega(MegaArgs a) {
         if (a.trace && lane == 0)  // a phase ends for the CTA when its last warp is done
             atomicMax(a.trace + (size_t(cta) * (a.nphases + 1) + p) * MEGA_TRACE_STAMPS + 2, gtime());
         pw = pn;
+        pref_cur = pref_next;
+        pref_next = false;
     }
     // no bulk copy may still be writing this CTA's shared memory when its threads exit (only an
     // aborted step can leave one pending)

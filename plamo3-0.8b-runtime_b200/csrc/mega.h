@@ -11,7 +11,6 @@ enum MegaKind { MK_QKV = 0, MK_ATT = 1, MK_O = 2, MK_GU = 3, MK_DOWN = 4, MK_HEA
 struct MegaPhase {
     int kind, layer;
     Linear lin;
-    const uint32_t* rowoff;  // .p12: byte offset of each row's first block in the data region (M + 1)
     int out_rows;
     int next_weight;  // index of the next weight (non-attention) phase; nphases after the last
 };

@@ -438,29 +438,10 @@ static int setup_mega(plamo_runtime& rt) {
     };
     if (!fold_ok(c.d, c.q_dim()) || !fold_ok(c.d, c.ffn)) return 0;
     if (configure_mega(smem, rt.packed, mega_npt(c.d)) != cudaSuccess) { cudaGetLastError(); return 0; }
-    // per-row first-block byte offsets of a packed matrix (M + 1 entries), from its block table
-    auto rowoff = [&](const Linear& lin, const uint32_t*& out) -> int {
-        out = nullptr;
-        if (!lin.offsets) return 0;
-        const size_t bpr = size_t(lin.K) / 128, blocks = size_t(lin.M) * bpr;
-        std::vector<uint32_t> tab(blocks);
-        CK(cudaMemcpy(tab.data(), lin.offsets, blocks * 4, cudaMemcpyDeviceToHost));
-        std::vector<uint32_t> ro(size_t(lin.M) + 1);
-        for (size_t m = 0; m < size_t(lin.M); m++) ro[m] = tab[m * bpr] & ~63u;
-        const uint32_t last = tab[blocks - 1];
-        ro[lin.M] = (last & ~63u) + ((last & 63u) ? 192u : 256u);
-        uint32_t* dptr = nullptr;
-        if (rt.dalloc(dptr, ro.size())) return 1;
-        CK(cudaMemcpy(dptr, ro.data(), ro.size() * 4, cudaMemcpyHostToDevice));
-        out = dptr;
-        return 0;
-    };
     std::vector<MegaPhase> phases;
     std::vector<MegaLayer> layers;
     auto weight_phase = [&](int kind, int l, const Linear& lin, int rows) -> int {
-        MegaPhase ph{kind, l, lin, nullptr, rows, 0};
-        if (rowoff(lin, ph.rowoff)) return 1;
-        phases.push_back(ph);
+        phases.push_back(MegaPhase{kind, l, lin, rows, 0});
         return 0;
     };
     for (int l = 0; l < c.layers; l++) {
@@ -469,7 +450,7 @@ static int setup_mega(plamo_runtime& rt) {
                      L.keys, L.values, L.cap, L.splits, L.per_max, L.full ? 1 : 0};
         layers.push_back(ml);
         if (weight_phase(MK_QKV, l, L.qkv, c.qkv_rows())) return 1;
-        phases.push_back(MegaPhase{MK_ATT, l, Linear{}, nullptr, 0, 0});
+        phases.push_back(MegaPhase{MK_ATT, l, Linear{}, 0, 0});
         if (weight_phase(MK_O, l, L.o, c.d) || weight_phase(MK_GU, l, L.gate_up, c.ffn) ||
             weight_phase(MK_DOWN, l, L.down, c.d))
             return 1;
