@@ -377,7 +377,7 @@ __device__ __forceinline__ bool gather64x2(float* dst1, const unsigned long long
 // ---- weight phases ---------------------------------------------------------------------------
 // A task is (output row, 1536-weight segment of the row): lane l covers weights
 // [g*512 + 16l, +16) of the segment's groups g (at most 3). A warp carries up to RB tasks at a time.
-constexpr int RB = 4;
+constexpr int RB = 3;
 constexpr int GB = 3;
 constexpr uint64_t MEGA_STAGGER_NS = 500;  // start offset between warp pairs in multi-round phases
 
@@ -412,7 +412,7 @@ __device__ __forceinline__ PhaseWork phase_work(const MegaPhase& ph, int cta, in
     if (ph.kind == MK_GU) {
         // chunks hold whole gate/up pairs: (gate m, up m) or (gate m, gate m+1, up m, up m+1)
         p.ntask = 2 * p.nu;
-        p.upc = p.nu > 8 ? 2 : 1;
+        p.upc = (RB >= 4 && p.nu > 8) ? 2 : 1;
         p.R = 2 * p.upc;
         p.nchunk = (p.nu + p.upc - 1) / p.upc;
     } else {
@@ -1180,10 +1180,10 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_decode_mega(MegaArgs a) {
             }
             // whole-row phases: t = 0 + (a0 + a1) (one segment), then the butterfly; lane 8 r
             // holds task r's sum
-            float v[RB];
+            float v4[4];
 #pragma unroll
-            for (int r = 0; r < RB; r++) v[r] = 0.f + res[r];
-            const float sum = warp_reduce_transposed<RB>(v, lane);
+            for (int r = 0; r < 4; r++) v4[r] = r < RB ? 0.f + res[r] : 0.f;
+            const float sum = warp_reduce_transposed<4>(v4, lane);
             const int r = lane >> 3;
             int row = 0, seg = 0;
             const bool mine = (lane & 7) == 0 && task_of(pw, c, r, row, seg);
