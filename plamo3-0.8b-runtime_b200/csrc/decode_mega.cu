@@ -379,7 +379,7 @@ __device__ __forceinline__ bool gather64x2(float* dst1, const unsigned long long
 // [g*512 + 16l, +16) of the segment's groups g (at most 3). A warp carries up to RB tasks at a time.
 constexpr int RB = 3;
 constexpr int GB = 3;
-constexpr uint64_t MEGA_STAGGER_NS = 500;  // start offset between warp pairs in multi-round phases
+constexpr uint64_t MEGA_STAGGER_NS = 400;  // start offset between warp pairs in multi-round phases
 
 struct Batch {
     uint4 w[RB][GB][2];       // raw: 32 weight bytes; .p12 packed block: sign|mantissa bytes, codes
