@@ -394,7 +394,7 @@ struct PhaseWork {
     int u0, nu;               // this CTA's outputs [u0, u0 + nu)
     int ntask, nchunk;
     int up;                   // SwiGLU: row offset of the up half
-    int upc;                  // SwiGLU: outputs per chunk
+    int upc;                  // SwiGLU: outputs per gate/up chunk pair
 };
 
 __device__ __forceinline__ PhaseWork phase_work(const MegaPhase& ph, int cta, int G) {
@@ -410,11 +410,11 @@ __device__ __forceinline__ PhaseWork phase_work(const MegaPhase& ph, int cta, in
     p.nu = int((long long)units * (cta + 1) / G) - p.u0;
     p.up = ph.kind == MK_GU ? ph.out_rows : 0;
     if (ph.kind == MK_GU) {
-        // chunks hold whole gate/up pairs: (gate m, up m) or (gate m, gate m+1, up m, up m+1)
+        // chunk pairs: the gate rows of RB outputs, then their up rows (same warp, in a row)
         p.ntask = 2 * p.nu;
-        p.upc = (RB >= 4 && p.nu > 8) ? 2 : 1;
-        p.R = 2 * p.upc;
-        p.nchunk = (p.nu + p.upc - 1) / p.upc;
+        p.upc = RB;
+        p.R = RB;
+        p.nchunk = 2 * ((p.nu + RB - 1) / RB);
     } else {
         p.ntask = p.nu * p.nseg;
         p.upc = 0;
@@ -424,13 +424,20 @@ __device__ __forceinline__ PhaseWork phase_work(const MegaPhase& ph, int cta, in
     return p;
 }
 
+// A warp's chunks: c = warp, warp + 8, ...; SwiGLU phases walk chunk pairs (2j, 2j + 1) for
+// j = warp, warp + 8, ..., so a warp sums the gate rows and then the up rows of the same outputs.
+__device__ __forceinline__ int first_chunk(const PhaseWork& p, int warp) { return p.kind == MK_GU ? 2 * warp : warp; }
+__device__ __forceinline__ int next_chunk(const PhaseWork& p, int c) {
+    return p.kind == MK_GU ? ((c & 1) ? c + 15 : c + 1) : c + 8;
+}
+
 // Row and segment of task r of chunk c; false when the slot is empty.
 __device__ __forceinline__ bool task_of(const PhaseWork& p, int c, int r, int& row, int& seg) {
     if (r >= p.R) return false;
-    if (p.kind == MK_GU) {
-        const int u = c * p.upc + (r % p.upc);
+    if (p.kind == MK_GU) {  // chunk 2j: gate rows of outputs [upc j, upc j + upc), chunk 2j + 1: their up rows
+        const int u = (c >> 1) * p.upc + r;
         if (u >= p.nu) return false;
-        row = p.u0 + u + (r / p.upc) * p.up;
+        row = p.u0 + u + (c & 1) * p.up;
         seg = 0;
         return true;
     }
@@ -1153,19 +1160,20 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_decode_mega(MegaArgs a) {
             const uint64_t t0 = gtime(), dly = uint64_t(warp >> 1) * MEGA_STAGGER_NS;
             while (gtime() - t0 < dly) __nanosleep(128);
         }
-        if (warp < pw.nchunk && !pref_cur) issue_chunk<PACKED>(pw, warp, b, pol, tbl);
+        if (first_chunk(pw, warp) < pw.nchunk && !pref_cur) issue_chunk<PACKED>(pw, first_chunk(pw, warp), b, pol, tbl);
         pref_cur = false;
         // ---- the warp's chunks; each chunk's successor (in this phase or the next weight phase)
         // is issued before the chunk's sums are reduced and stored
-        for (int c = warp;; c += 8) {
+        float gstash = 0.f;  // SwiGLU: the gate sums of the warp's last gate chunk (lane 8 r: output r)
+        for (int c = first_chunk(pw, warp);; c = next_chunk(pw, c)) {
             const bool have = c < pw.nchunk;
             float res[RB];
             if (have) chunk_partials<PACKED>(pw, c, b, xs4, res);
-            {  // the successor: chunk c + 8 of this phase, else (raw weights) this warp's first chunk of
-               // the next weight phase, in flight across the phase boundary
-                const bool inph = c + 8 < pw.nchunk;
+            {  // the successor: the warp's next chunk of this phase, else (raw weights) its first chunk
+               // of the next weight phase, in flight across the phase boundary
+                const bool inph = next_chunk(pw, c) < pw.nchunk;
                 const PhaseWork nx = inph ? pw : pn;
-                const int nc = inph ? c + 8 : warp;
+                const int nc = inph ? next_chunk(pw, c) : first_chunk(pn, warp);
                 if ((inph || (!PACKED && nw < a.nphases)) && nc < nx.nchunk) issue_chunk<PACKED>(nx, nc, b, pol, tbl);
                 if (!inph && !PACKED) pref_next = nw < a.nphases && nc < nx.nchunk;
             }
@@ -1175,7 +1183,7 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_decode_mega(MegaArgs a) {
 #pragma unroll
                 for (int r = 0; r < RB; r++)
                     if (r < pw.R && c * pw.R + r < pw.ntask) part[(c * pw.R + r) * 32 + lane] = res[r];
-                if (c + 8 >= pw.nchunk) break;
+                if (next_chunk(pw, c) >= pw.nchunk) break;
                 continue;
             }
             // whole-row phases: t = 0 + (a0 + a1) (one segment), then the butterfly; lane 8 r
@@ -1188,11 +1196,12 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_decode_mega(MegaArgs a) {
             int row = 0, seg = 0;
             const bool mine = (lane & 7) == 0 && task_of(pw, c, r, row, seg);
             if (ph.kind == MK_GU) {
-                // gate sums in lanes 0 .. 8 upc - 8, the matching up sums 8 upc lanes higher
-                const float u = __shfl_down_sync(FULL_MASK, sum, 8 * pw.upc);
-                if (mine && r < pw.upc) {
-                    const float gq = rbf(sum), uq = rbf(u);
-                    st_tag(a.act + row, tagged(tag, f2bf(rbf(rbf(gq / (1.0f + pexp(-gq))) * uq))));
+                // a gate chunk parks its sums; the up chunk that follows finishes the outputs
+                if ((c & 1) == 0) {
+                    gstash = sum;
+                } else if (mine) {
+                    const float gq = rbf(gstash), uq = rbf(sum);
+                    st_tag(a.act + (row - pw.up), tagged(tag, f2bf(rbf(rbf(gq / (1.0f + pexp(-gq))) * uq))));
                 }
             } else if (mine) {
                 const uint32_t bits = f2bf(sum);
@@ -1204,7 +1213,7 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_decode_mega(MegaArgs a) {
                     best = key > best ? key : best;
                 }
             }
-            if (c + 8 >= pw.nchunk) break;
+            if (next_chunk(pw, c) >= pw.nchunk) break;
         }
         if (ph.kind == MK_O || ph.kind == MK_DOWN) {
             // fold each row's segment partials in segment order, then the butterfly (one warp per row)
