@@ -17,6 +17,9 @@ from HBM; the 1.45 GB of weights are far larger than the 126 MB L2, so no flush 
          algorithmic bytes = weight bytes streamed per launch.
   cpu_baseline  the CPU restatement of the same forward (oracle/, OpenMP on all host cores) on a
          bounded sample of the same workload (rank 0, N=1).
+  segments  aggregate throughput of independent segments (BASELINE config 5b shape): 32 seeded
+         512-token segments per GPU, batched prefill, then batched greedy decode steps (device
+         time, max over ranks); reported beside the bs1 headline, not folded into `value`.
 
 --impl reference runs the reference arm: the reference (Swift + Metal) cannot run on Linux, so its
 CPU path is the restatement in oracle/ (see DESIGN.md), timed on the host cores.
@@ -229,6 +232,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile-steps", type=int, default=16)
     ap.add_argument("--reference-max-steps", type=int, default=64)
+    ap.add_argument("--segment-lanes", type=int, default=32)
+    ap.add_argument("--segment-steps", type=int, default=32)
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -313,6 +318,36 @@ def main():
     bcast = rt.broadcast_seconds
     rt.close()
 
+    # ---- aggregate segment throughput (BASELINE config 5b shape): independent 512-token segments
+    # decoded together on each GPU (batched prefill, then batched greedy steps); the steps are
+    # timed with CUDA events on the runtime's stream (device time), max over ranks
+    seg = None
+    if args.segment_lanes > 0:
+        srt = P.Runtime(model, context=PROMPT + args.segment_steps + 8, device=local)
+        sb = P.Batch(srt, lanes=args.segment_lanes)
+        segs = [P.synthetic.seeded_tokens(PROMPT, srt.vocab, seed=1000 + rank * args.segment_lanes + k)
+                for k in range(args.segment_lanes)]
+        p0 = sb.gpu_seconds
+        nxt = sb.prefill(segs)
+        prefill_s = sb.gpu_seconds - p0
+        for _ in range(2):
+            nxt = sb.step(nxt)
+        if dist: dist.barrier()
+        torch.cuda.synchronize()
+        s0 = sb.gpu_seconds
+        for _ in range(args.segment_steps):
+            nxt = sb.step(nxt)
+        torch.cuda.synchronize()
+        st = torch.tensor([sb.gpu_seconds - s0, prefill_s], device="cuda", dtype=torch.float64)
+        if dist: dist.all_reduce(st, op=dist.ReduceOp.MAX)
+        sb.close()
+        srt.close()
+        seg = dict(lanes_per_gpu=args.segment_lanes, prompt_tokens=PROMPT, steps=args.segment_steps,
+                   decode_tok_s=world * args.segment_lanes * args.segment_steps / float(st[0]),
+                   step_ms=1e3 * float(st[0]) / args.segment_steps,
+                   prefill_tok_s=world * args.segment_lanes * PROMPT / float(st[1]),
+                   path="multi-kernel batched step (one weight pass for all lanes)")
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(model, prompt, args.cpu_budget, 64)
@@ -339,6 +374,8 @@ def main():
             line["cpu_baseline"] = cpu
         if world > 1:
             line["weight_broadcast_s"] = bcast
+        if seg:
+            line["segments"] = seg
         print(json.dumps(line), flush=True)
     if dist:
         dist.barrier()
