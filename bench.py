@@ -136,6 +136,23 @@ def ensure_model(root: Path, packed: bool, rank: int, dist) -> Path:
     return d
 
 
+def segment_block(rank: int, world: int, total: int) -> range:
+    """Indices of the independent segments rank `rank` of `world` decodes: one contiguous block,
+    ranks' blocks disjoint and together covering all `total` (no exchange between ranks)."""
+    return range(total * rank // world, total * (rank + 1) // world)
+
+
+def segment_seed(index: int) -> int:
+    """Seed of segment `index`'s 512-token prompt (segment k uses seed 1000 + k)."""
+    return 1000 + index
+
+
+def aggregate_rate(units_per_rank: int, world: int, max_seconds: float) -> float:
+    """Whole-job throughput of `world` ranks that each processed `units_per_rank` units, timed as
+    the slowest rank's device time."""
+    return world * units_per_rank / max_seconds
+
+
 def linear_bytes(model_dir: Path, packed: bool) -> int:
     """Algorithmic weight bytes streamed per decode token by the projection GEMVs."""
     P = pkg()
@@ -325,8 +342,8 @@ def main():
     if args.segment_lanes > 0:
         srt = P.Runtime(model, context=PROMPT + args.segment_steps + 8, device=local)
         sb = P.Batch(srt, lanes=args.segment_lanes)
-        segs = [P.synthetic.seeded_tokens(PROMPT, srt.vocab, seed=1000 + rank * args.segment_lanes + k)
-                for k in range(args.segment_lanes)]
+        segs = [P.synthetic.seeded_tokens(PROMPT, srt.vocab, seed=segment_seed(k))
+                for k in segment_block(rank, world, world * args.segment_lanes)]
         p0 = sb.gpu_seconds
         nxt = sb.prefill(segs)
         prefill_s = sb.gpu_seconds - p0
@@ -343,9 +360,9 @@ def main():
         sb.close()
         srt.close()
         seg = dict(lanes_per_gpu=args.segment_lanes, prompt_tokens=PROMPT, steps=args.segment_steps,
-                   decode_tok_s=world * args.segment_lanes * args.segment_steps / float(st[0]),
+                   decode_tok_s=aggregate_rate(args.segment_lanes * args.segment_steps, world, float(st[0])),
                    step_ms=1e3 * float(st[0]) / args.segment_steps,
-                   prefill_tok_s=world * args.segment_lanes * PROMPT / float(st[1]),
+                   prefill_tok_s=aggregate_rate(args.segment_lanes * PROMPT, world, float(st[1])),
                    path="multi-kernel batched step (one weight pass for all lanes)")
 
     cpu = None
@@ -353,7 +370,7 @@ def main():
         cpu = cpu_baseline(model, prompt, args.cpu_budget, 64)
 
     if rank == 0:
-        value = world * args.steps / elapsed_max
+        value = aggregate_rate(args.steps, world, elapsed_max)
         tok_bytes = wbytes
         line = dict(
             metric="decode tok/s (bs1)", value=value, unit="tok/s", n_gpus=world, steps=args.steps,
