@@ -20,6 +20,10 @@ from HBM; the 1.45 GB of weights are far larger than the 126 MB L2, so no flush 
   segments  aggregate throughput of independent segments (BASELINE config 5b shape): 32 seeded
          512-token segments per GPU, batched prefill, then batched greedy decode steps (device
          time, max over ranks); reported beside the bs1 headline, not folded into `value`.
+         `segments` runs the order-exact CUDA-core projections, `segments_tensor` the tcgen05
+         tensor-core GEMM (plamo_set_tensor_gemm).
+  prefill  the 512-token prompt prefilled on both paths (device time, median of 5, max over
+         ranks), with its algorithmic FLOPs against the measured dense bf16 tensor peak.
 
 --impl reference runs the reference arm: the reference (Swift + Metal) cannot run on Linux, so its
 CPU path is the restatement in oracle/ (see DESIGN.md), timed on the host cores.
@@ -228,6 +232,18 @@ def run_reference(args):
     return 0
 
 
+def prefill_flop(tokens: int, layers: int = 16, window: int = 2048, linear_params: int = 725_090_304,
+                 head_params: int = 165_150_720) -> float:
+    """Algorithmic FLOPs of prefilling `tokens` prompt tokens at the reference dims: every non-head
+    projection on every token, q.k and p.v over each token's visible keys (8192 FLOP per key and
+    layer: 16 heads x 128 x 2 x 2), and the lm_head on the last row."""
+    attn = 0
+    for layer in range(layers):
+        full = layer % 8 == 7
+        attn += sum(t + 1 if full else min(t + 1, window) for t in range(tokens))
+    return 2.0 * (linear_params - head_params) * tokens + 8192.0 * attn + 2.0 * head_params
+
+
 def workload_config(args):
     return {"workload": "BASELINE config 2: reference-dims PLaMo-3 0.8B (d1536 L16 H16/KV1 F6144 V107520), "
                         f"{PROMPT}-token seeded prompt, prefill then greedy bs1 decode"
@@ -251,6 +267,7 @@ def main():
     ap.add_argument("--reference-max-steps", type=int, default=64)
     ap.add_argument("--segment-lanes", type=int, default=32)
     ap.add_argument("--segment-steps", type=int, default=32)
+    ap.add_argument("--prefill-reps", type=int, default=5)
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -337,10 +354,11 @@ def main():
 
     # ---- aggregate segment throughput (BASELINE config 5b shape): independent 512-token segments
     # decoded together on each GPU (batched prefill, then batched greedy steps); the steps are
-    # timed with CUDA events on the runtime's stream (device time), max over ranks
-    seg = None
-    if args.segment_lanes > 0:
+    # timed with CUDA events on the runtime's stream (device time), max over ranks. Measured on the
+    # order-exact CUDA-core path and with the projections on the tcgen05 tensor cores.
+    def segments(tensor: bool):
         srt = P.Runtime(model, context=PROMPT + args.segment_steps + 8, device=local)
+        srt.set_tensor_gemm(tensor)
         sb = P.Batch(srt, lanes=args.segment_lanes)
         segs = [P.synthetic.seeded_tokens(PROMPT, srt.vocab, seed=segment_seed(k))
                 for k in segment_block(rank, world, world * args.segment_lanes)]
@@ -359,11 +377,44 @@ def main():
         if dist: dist.all_reduce(st, op=dist.ReduceOp.MAX)
         sb.close()
         srt.close()
-        seg = dict(lanes_per_gpu=args.segment_lanes, prompt_tokens=PROMPT, steps=args.segment_steps,
-                   decode_tok_s=aggregate_rate(args.segment_lanes * args.segment_steps, world, float(st[0])),
-                   step_ms=1e3 * float(st[0]) / args.segment_steps,
-                   prefill_tok_s=aggregate_rate(args.segment_lanes * PROMPT, world, float(st[1])),
-                   path="multi-kernel batched step (one weight pass for all lanes)")
+        return dict(lanes_per_gpu=args.segment_lanes, prompt_tokens=PROMPT, steps=args.segment_steps,
+                    decode_tok_s=aggregate_rate(args.segment_lanes * args.segment_steps, world, float(st[0])),
+                    step_ms=1e3 * float(st[0]) / args.segment_steps,
+                    prefill_tok_s=aggregate_rate(args.segment_lanes * PROMPT, world, float(st[1])),
+                    path=("tcgen05 tensor-core projections (fp32 accumulate, within the restatement's reordering "
+                          "drift)" if tensor else "order-exact CUDA-core projections (bit-identical to the restatement)")
+                    + "; one weight pass for all lanes per step")
+
+    seg = seg_tc = None
+    if args.segment_lanes > 0:
+        seg = segments(False)
+        seg_tc = segments(True)
+
+    # ---- prefill of the 512-token prompt, device time, max over ranks: the
+    # order-exact path and the tcgen05 path, against the dense bf16 tensor roofline
+    pre = None
+    if args.prefill_reps > 0:
+        prt = P.Runtime(model, context=PROMPT + 16, device=local)
+        pre = dict(tokens=PROMPT, flop=prefill_flop(PROMPT))
+        for mode in ("exact", "tensor"):
+            prt.set_tensor_gemm(mode == "tensor")
+            times = []
+            for i in range(args.prefill_reps + 1):  # the first run warms up
+                prt.reset()
+                g0 = prt.gpu_seconds
+                prt.prefill(prompt)
+                if i:
+                    times.append(prt.gpu_seconds - g0)
+            tt = torch.tensor([sorted(times)[len(times) // 2]], device="cuda", dtype=torch.float64)
+            if dist: dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            t_s = float(tt.item())
+            tflops = pre["flop"] / t_s / 1e12
+            pre[mode] = dict(ms=1e3 * t_s, tok_s=aggregate_rate(PROMPT, world, t_s), tflops=tflops,
+                             tensor_frac=tflops / pk["bf16"])
+        pre["peak_tflops"] = pk["bf16"]
+        pre["note"] = ("flop = 2 x non-head linear params x tokens + 8192 x visible keys per layer and token + "
+                       "last-row lm_head; tensor_frac against the measured bf16 burst peak")
+        prt.close()
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -393,6 +444,10 @@ def main():
             line["weight_broadcast_s"] = bcast
         if seg:
             line["segments"] = seg
+        if seg_tc:
+            line["segments_tensor"] = seg_tc
+        if pre:
+            line["prefill"] = pre
         print(json.dumps(line), flush=True)
     if dist:
         dist.barrier()

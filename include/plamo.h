@@ -118,6 +118,14 @@ PLAMO_API int plamo_step_launches(plamo_runtime*);
  * sm_100a; PLAMO_PERSISTENT=0 in the environment selects the multi-kernel graph instead). */
 PLAMO_API int plamo_persistent_decode(const plamo_runtime*);
 
+/* Dense contractions on the tensor cores: with enable != 0, every projection over 16 or more rows
+ * of raw bf16 weights (prefill calls, batched steps and batched prefill of this runtime and its
+ * batches) runs as a tcgen05 GEMM with fp32 accumulation. The results then match the default path
+ * within the rounding of the accumulation order (next-token logits within RMSE 1e-2 and max |diff|
+ * 5e-2, the tolerance of the reference's verify scripts), not bit for bit; batch-1 decode and
+ * .p12 weights are unaffected. Off by default. Returns 0, or 1 for a null handle. */
+PLAMO_API int plamo_set_tensor_gemm(plamo_runtime*, int enable);
+
 /* Profiling: runs `steps` batch-1 decode steps (as plamo_decode_chain) with every kernel launch
  * bracketed by CUDA events. class_ms[6] / launches[6] receive the summed device milliseconds and
  * launch counts per kernel class: 0 GEMV (projections, lm_head), 1 QK-norm + RoPE + KV append,

@@ -29,6 +29,16 @@ extern "C" {
 PLAMO_API int plamo_k_linear(const void* w, const uint32_t* offsets, const uint16_t* x, int rows, int K, int M, int mode,
                    uint16_t* y, uint64_t* argmax_keys, void* stream);
 
+/* The same projection on the tensor cores (tcgen05 GEMM, fp32 accumulation in tensor memory):
+ * raw bf16 weights only (offsets are not taken), K a multiple of 64, any rows >= 1. The outputs
+ * match plamo_k_linear within the rounding of the accumulation order. splits > 0 forces a K split
+ * over that many CTAs per tile (<= 16 and <= K / 64), whose fp32 partials need
+ * splits * rows * M floats of `workspace`; splits == 0 lets the launcher choose, splitting only
+ * into the workspace given (workspace may then be NULL). */
+PLAMO_API int plamo_k_linear_tc(const void* w, const uint16_t* x, int rows, int K, int M, int mode, uint16_t* y,
+                                uint64_t* argmax_keys, int splits, float* workspace, size_t workspace_floats,
+                                void* stream);
+
 /* Converts argmax keys to indices (0xFFFFFFFF when a row had only NaN). */
 PLAMO_API int plamo_k_argmax_keys(const uint64_t* keys, int rows, uint32_t* out, void* stream);
 

@@ -327,14 +327,16 @@ class OracleBatch:
 # ---------------------------------------------------------------------------------------
 # noise floor of the restatement itself
 
-def _reordered(fn):
-    """Runs fn with every projection sum walked backwards and every global-layer attention row
-    through 16-key split-K partitions: the same arithmetic in another fp32 summation order."""
+def _reordered(fn, mode: str = "reverse"):
+    """Runs fn with every global-layer attention row through 16-key split-K partitions and every
+    projection sum either walked backwards ("reverse": the same arithmetic in another fp32 order)
+    or summed exactly and rounded once ("exact": the correctly rounded dot product, which is what
+    fp32 accumulation on the tensor cores approaches)."""
     L = lib()
     L.oracle_set_split_partition.argtypes = [ctypes.c_int]
     L.oracle_set_dot_reverse.argtypes = [ctypes.c_int]
     L.oracle_set_split_partition(16)
-    L.oracle_set_dot_reverse(1)
+    L.oracle_set_dot_reverse(2 if mode == "exact" else 1)
     try:
         return fn()
     finally:
@@ -342,7 +344,8 @@ def _reordered(fn):
         L.oracle_set_dot_reverse(0)
 
 
-def noise_floor(directory, context: int, prompt, steps: int, model: Model | None = None) -> dict:
+def noise_floor(directory, context: int, prompt, steps: int, model: Model | None = None,
+                mode: str = "reverse") -> dict:
     """Teacher-forced logit differences between the restatement and its reordered twin.
 
     A model whose activations are rounded to bf16 after every op amplifies fp32 reordering into
@@ -352,7 +355,7 @@ def noise_floor(directory, context: int, prompt, steps: int, model: Model | None
     a = OracleRuntime(directory, context, model=model)
     b = OracleRuntime(directory, context, model=model)
     nxt = a.prefill(prompt)
-    _reordered(lambda: b.prefill(prompt))
+    _reordered(lambda: b.prefill(prompt), mode)
     rmse, maxabs = [], []
     for step in range(steps + 1):
         e = a.logits() - b.logits()
@@ -362,7 +365,7 @@ def noise_floor(directory, context: int, prompt, steps: int, model: Model | None
             break
         tok = nxt
         nxt = a.forward([tok])
-        _reordered(lambda: b.forward([tok]))
+        _reordered(lambda: b.forward([tok]), mode)
     return dict(rmse=max(rmse), maxabs=max(maxabs), rmse_mean=float(np.mean(rmse)))
 
 

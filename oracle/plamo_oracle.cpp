@@ -66,7 +66,8 @@ constexpr float GLOBAL_MSCALE = 1.5545177444479562f; // K:266-267
 // ---- GEMV / GEMM rows: K:92-114 (linear), K:149-200 (matrix) --------------------------
 // y[t][m] = sum_k W[m][k] * x[t][k], fp32 accumulation, output bf16-rounded (or bf16 bits
 // for the lm_head, K:111,196).
-int g_dot_reverse = 0;  // noise-floor experiments: walk K backwards (same sum, other fp32 order)
+// noise-floor experiments: 1 walks segments and each lane's chains backwards, 2 rounds the exact sum once
+int g_dot_reverse = 0;
 
 // Sum over 32 "lanes" by the xor-butterfly tree (offsets 16, 8, 4, 2, 1).
 inline float butterfly32(float (&v)[32]) {
@@ -84,6 +85,11 @@ inline float butterfly32(float (&v)[32]) {
 // (even + odd) is added to its running total segment by segment; the 32 lane totals meet in the
 // butterfly tree.
 inline float dot_bf16(const uint16_t* w, const float* x, int K) {
+    if (g_dot_reverse == 2) {  // correctly rounded twin: exact products, double sum, one rounding
+        double acc = 0.0;
+        for (int k = 0; k < K; k++) acc += double(bf(w[k])) * double(x[k]);
+        return float(acc);
+    }
     const int G = (K + 511) / 512, S = (G + 2) / 3;
     float lanes[32];
     for (int l = 0; l < 32; l++) {
@@ -94,7 +100,8 @@ inline float dot_bf16(const uint16_t* w, const float* x, int K) {
             for (int g = 3 * seg; g < std::min(G, 3 * seg + 3); g++) {
                 const int e0 = g * 512 + 16 * l;
                 if (e0 >= K) continue;
-                for (int k = 0; k < 8; k++) {
+                for (int kk = 0; kk < 8; kk++) {
+                    const int k = g_dot_reverse ? 7 - kk : kk;
                     a0 = std::fma(bf(w[e0 + 2 * k]), x[e0 + 2 * k], a0);
                     a1 = std::fma(bf(w[e0 + 2 * k + 1]), x[e0 + 2 * k + 1], a1);
                 }

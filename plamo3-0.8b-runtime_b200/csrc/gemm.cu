@@ -18,6 +18,7 @@
 // tree order.
 #include "common.cuh"
 #include "kernels.h"
+#include "mbarrier.cuh"
 
 #include <mutex>
 
@@ -62,43 +63,6 @@ constexpr int NSTAGE = 4;
 constexpr int RED_STRIDE = 33;  // floats per output row of lane partials (conflict-free reads)
 constexpr int RED_BYTES = 8 * 32 * RED_STRIDE * 4;
 constexpr int GEMM_SMEM = 1024 + NSTAGE * STAGE_BYTES + RED_BYTES + 64;
-
-__device__ __forceinline__ uint32_t smem_addr(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
-__device__ __forceinline__ void bar_init(uint64_t* b, uint32_t n) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(b)), "r"(n) : "memory");
-}
-__device__ __forceinline__ void bar_expect(uint64_t* b, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(b)), "r"(bytes) : "memory");
-}
-__device__ __forceinline__ bool bar_test(uint64_t* b, uint32_t parity) {
-    uint32_t ok;
-    asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
-                 : "=r"(ok)
-                 : "r"(smem_addr(b)), "r"(parity)
-                 : "memory");
-    return ok != 0;
-}
-__device__ __forceinline__ uint64_t now_ns() {
-    uint64_t t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
-}
-// Bounded wait (2 s): a copy that never lands ends the kernel's use of the stage instead of hanging.
-__device__ __forceinline__ bool bar_wait(uint64_t* b, uint32_t parity) {
-    if (bar_test(b, parity)) return true;
-    const uint64_t t0 = now_ns();
-    for (uint32_t i = 1;; i++) {
-        if (bar_test(b, parity)) return true;
-        if ((i & 63u) == 0 && now_ns() - t0 > 2000000000ull) return false;
-    }
-}
-__device__ __forceinline__ void tma3(void* dst, const CUtensorMap* map, int c1, int c2, uint64_t* b) {
-    asm volatile(
-        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(
-            smem_addr(dst)),
-        "l"(map), "r"(0), "r"(c1), "r"(c2), "r"(smem_addr(b))
-        : "memory");
-}
 
 // bf16 pair x bf16 pair into the even / odd chains (sm_100 mixed-precision fma: the same result
 // as fmaf on the widened operands).

@@ -1,0 +1,424 @@
+// Tensor-core GEMM for the dense contractions of prefill and of batched steps with many rows:
+// Y[r][m] = sum_k X[r][k] W[m][k], bf16 operands, fp32 accumulation on the 5th-generation tensor
+// cores (tcgen05.mma kind::f16, accumulators in tensor memory), operands staged by TMA.
+//
+// Unlike the CUDA-core kernels (kernels.cu, gemm.cu) this path does not reproduce the order-exact
+// summation of the CPU restatement: the tensor core adds its products in its own order, so an
+// output can differ from the exact path by an ulp of the bf16 result. The runtime uses it only when
+// asked (plamo_set_tensor_gemm), the parity tests hold it to the logits tolerance of the reference
+// checks (RMSE <= 1e-2, max |diff| <= 5e-2) instead of bit equality.
+//
+// Tile: 128 weight rows (the MMA's M, one tensor-memory lane each) x BN activation rows (the MMA's
+// N, one fp32 tensor-memory column each). Each stage holds 64 k of both operands, one 128-byte
+// line per row in the 128-byte swizzle that TMA writes and the MMA's shared-memory descriptor
+// reads (8-row groups 1024 bytes apart); the four K = 16 MMAs of a stage advance the descriptors'
+// start address by 32 bytes. SwiGLU tiles take gate rows m0..m0+63 into lanes 0..63 and the
+// matching up rows into lanes 64..127, so one tile finishes 64 outputs.
+//
+// Roles (128 threads): lane 0 of warp 0 issues the TMA copies (STAGES deep, a stage is refilled
+// once the MMAs that read it have committed to its `empty` barrier); lane 0 of warp 1 issues the
+// MMAs; then all four warps drain tensor memory (warp w reads lanes 32w..32w+31) and write bf16
+// outputs, SwiGLU products or logits with argmax keys. A tile with few weight rows (small M at few
+// activation rows) splits K over `splits` CTAs that store fp32 partials; a second kernel adds them
+// in split order and applies the same epilogue.
+#include "common.cuh"
+#include "kernels.h"
+#include "mbarrier.cuh"
+
+namespace plamo {
+
+namespace {
+
+constexpr int TC_BM = 128;       // weight rows per tile (MMA M = tensor-memory lanes)
+constexpr int TC_BK = 64;        // k per stage: one 128-byte swizzled line per row
+constexpr int TC_UK = 16;        // k per tcgen05.mma of kind::f16
+constexpr int TC_THREADS = 128;  // four warps: every tensor-memory lane quarter has its warp
+constexpr int TC_SPLITS_MAX = 16;
+
+template <int BN>
+struct TcTile {
+    static constexpr int A_BYTES = TC_BM * 128;
+    static constexpr int B_BYTES = BN * 128;
+    static constexpr int STAGE = A_BYTES + B_BYTES;  // a multiple of 1024 (swizzle atoms stay aligned)
+    static constexpr int STAGES = BN == 128 ? 6 : (BN == 64 ? 4 : 5);
+    static constexpr int SMEM = 1024 + STAGES * STAGE + 256;
+};
+
+// Instruction descriptor of kind::f16: fp32 accumulator, bf16 A and B, both K-major, N and M.
+constexpr uint32_t tc_idesc(int n) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(n >> 3) << 17) | (uint32_t(TC_BM >> 4) << 24);
+}
+
+// Shared-memory matrix descriptor: K-major operand in the 128-byte swizzle, rows 128 bytes apart,
+// 8-row groups 1024 bytes apart (stride byte offset), descriptor version 1, layout type 2.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+    return uint64_t((saddr & 0x3FFFFu) >> 4) | (uint64_t(1) << 16) | (uint64_t(1024 >> 4) << 32) |
+           (uint64_t(1) << 46) | (uint64_t(2) << 61);
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_alloc(uint32_t* slot, uint32_t ncols) {  // whole warp
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(slot)), "r"(ncols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {  // whole warp
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void umma_bf16(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(d),
+        "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// Arrives on `bar` once every MMA this thread issued so far has completed.
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
+                 : "memory");
+}
+// 16 consecutive fp32 columns of this thread's tensor-memory lane.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, "
+        "[%16];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+          "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ float swiglu(float g, float u) {
+    const float gq = rbf(g), uq = rbf(u);
+    return rbf(rbf(gq / (1.0f + pexp(-gq))) * uq);
+}
+
+template <int BN, int MODE>
+__global__ void __launch_bounds__(TC_THREADS, 1)
+    k_gemm_tc(GemvArgs a, const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmw, int splits,
+              int* error) {
+    using T = TcTile<BN>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + T::STAGES * T::STAGE);
+    uint64_t* empty = full + T::STAGES;
+    uint64_t* done = empty + T::STAGES;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+    int* stop = reinterpret_cast<int*>(tmem_slot + 1);
+
+    const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+    const int M = a.lin.M, Mout = MODE == GEMV_SWIGLU ? M / 2 : M;
+    const int per = MODE == GEMV_SWIGLU ? TC_BM / 2 : TC_BM;
+    const int nn = (a.rows + BN - 1) / BN, nkb = a.lin.K / TC_BK;
+    int idx = int(blockIdx.x);
+    const int nt = idx % nn;
+    idx /= nn;
+    const int ks = idx % splits, mt = idx / splits;
+    const int m0 = mt * per, n0 = nt * BN;
+    const int kb0 = nkb * ks / splits, nk = nkb * (ks + 1) / splits - kb0;
+
+    if (t == 0) {
+        for (int i = 0; i < T::STAGES; i++) {
+            bar_init(&full[i], 1);
+            bar_init(&empty[i], 1);
+        }
+        bar_init(done, 1);
+        *stop = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncwarp();
+    if (warp == 0) tmem_alloc(tmem_slot, BN);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    int issued = 0;
+    if (warp == 0) {
+        if (lane == 0) {
+            for (int i = 0; i < nk; i++) {
+                const int s = i % T::STAGES;
+                if (i >= T::STAGES && !bar_wait(&empty[s], uint32_t((i / T::STAGES) & 1) ^ 1u)) {
+                    atomicCAS(error, 0, 1);
+                    *stop = 1;
+                    break;
+                }
+                uint8_t* st = smem + s * T::STAGE;
+                const int kx = (kb0 + i) * TC_BK;
+                bar_expect(&full[s], T::STAGE);
+                if (MODE == GEMV_SWIGLU) {
+                    tma2(st, &tmw, kx, m0, &full[s]);
+                    tma2(st + T::A_BYTES / 2, &tmw, kx, Mout + m0, &full[s]);
+                } else {
+                    tma2(st, &tmw, kx, m0, &full[s]);
+                }
+                tma2(st + T::A_BYTES, &tmx, kx, n0, &full[s]);
+                issued = i + 1;
+            }
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        if (lane == 0) {
+            const uint32_t idesc = tc_idesc(BN);
+            for (int i = 0; i < nk; i++) {
+                const int s = i % T::STAGES;
+                if (!bar_wait(&full[s], uint32_t(i / T::STAGES) & 1u)) {
+                    atomicCAS(error, 0, 2);
+                    *stop = 1;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t sa = smem_addr(smem + s * T::STAGE), sb = sa + T::A_BYTES;
+#pragma unroll
+                for (int kk = 0; kk < TC_BK / TC_UK; kk++)
+                    umma_bf16(tmem, sw128_desc(sa + kk * 32), sw128_desc(sb + kk * 32), idesc, uint32_t(i | kk));
+                umma_commit(&empty[s]);
+            }
+            umma_commit(done);  // also after an abort: the MMAs in flight finish before tensor memory is freed
+        }
+        __syncwarp();
+    }
+    __syncthreads();  // `stop` is settled
+    const bool finished = __syncthreads_and(bar_wait(done, 0)) != 0;  // uniform: the epilogue has barriers
+    tc_fence_after();
+    if (!finished && t == 0) atomicCAS(error, 0, 3);
+
+    if (finished && !*stop) {
+        const int row = warp * 32 + lane;  // tensor-memory lane = weight row of the tile
+        const uint32_t lane_base = uint32_t(warp * 32) << 16;
+        float* xch = reinterpret_cast<float*>(smem);  // SwiGLU: up values [64][17] (stages are drained)
+        for (int c0 = 0; c0 < BN && n0 + c0 < a.rows; c0 += 16) {
+            uint32_t v[16];
+            tmem_ld16(tmem + lane_base + uint32_t(c0), v);
+            if (splits > 1) {
+                // fp32 partials [split][row][M], by raw weight row
+                int col = m0 + row;
+                bool ok = col < Mout;
+                if (MODE == GEMV_SWIGLU) {
+                    const int i = row & 63;
+                    col = (row < 64 ? 0 : Mout) + m0 + i;
+                    ok = m0 + i < Mout;
+                }
+                if (ok) {
+#pragma unroll
+                    for (int j = 0; j < 16; j++) {
+                        const int r = n0 + c0 + j;
+                        if (r < a.rows) a.part[(size_t(ks) * a.rows + r) * M + col] = __uint_as_float(v[j]);
+                    }
+                }
+            } else if (MODE == GEMV_SWIGLU) {
+                if (warp >= 2) {
+#pragma unroll
+                    for (int j = 0; j < 16; j++) xch[(row - 64) * 17 + j] = __uint_as_float(v[j]);
+                }
+                __syncthreads();
+                if (warp < 2 && m0 + row < Mout) {
+#pragma unroll
+                    for (int j = 0; j < 16; j++) {
+                        const int r = n0 + c0 + j;
+                        if (r < a.rows) {
+                            const int orow = a.out_map ? a.out_map[r] : r;
+                            a.y[size_t(orow) * a.ystride + m0 + row] =
+                                uint16_t(f2bf(swiglu(__uint_as_float(v[j]), xch[row * 17 + j])));
+                        }
+                    }
+                }
+                __syncthreads();
+            } else {
+                const int m = m0 + row;
+#pragma unroll
+                for (int j = 0; j < 16; j++) {
+                    const int r = n0 + c0 + j;
+                    const bool rok = r < a.rows, ok = rok && m < Mout;
+                    const int orow = rok ? (a.out_map ? a.out_map[r] : r) : 0;
+                    const uint32_t b = f2bf(__uint_as_float(v[j]));
+                    if (ok) a.y[size_t(orow) * a.ystride + m] = uint16_t(b);
+                    if (MODE == GEMV_LOGITS) {
+                        unsigned long long key = ok ? argmax_key(bf2f(b), uint32_t(m)) : 0ull;
+#pragma unroll
+                        for (int o = 16; o > 0; o >>= 1) {
+                            const unsigned long long other = __shfl_xor_sync(FULL_MASK, key, o);
+                            key = other > key ? other : key;
+                        }
+                        if (lane == 0 && rok && key) atomicMax(a.keys + orow, key);
+                    }
+                }
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tmem, BN);
+        // copies issued into this CTA's shared memory land before it exits (only an aborted
+        // producer can leave some in flight)
+        if (lane == 0)
+            for (int i = issued - T::STAGES < 0 ? 0 : issued - T::STAGES; i < issued; i++)
+                bar_wait(&full[i % T::STAGES], uint32_t(i / T::STAGES) & 1u);
+    }
+}
+
+// Adds the split partials of one output in split order and applies the mode's epilogue.
+template <int MODE>
+__global__ void __launch_bounds__(256) k_gemm_tc_finish(GemvArgs a, int splits) {
+    const int r = int(blockIdx.y), m = int(blockIdx.x) * 256 + int(threadIdx.x);
+    const int M = a.lin.M, Mout = MODE == GEMV_SWIGLU ? M / 2 : M;
+    const size_t sstride = size_t(a.rows) * M;
+    const float* p = a.part + size_t(r) * M;
+    const int orow = a.out_map ? a.out_map[r] : r;
+    unsigned long long key = 0ull;
+    if (m < Mout) {
+        float v = p[m];
+        for (int s = 1; s < splits; s++) v = v + p[s * sstride + m];
+        if (MODE == GEMV_SWIGLU) {
+            float u = p[Mout + m];
+            for (int s = 1; s < splits; s++) u = u + p[s * sstride + Mout + m];
+            a.y[size_t(orow) * a.ystride + m] = uint16_t(f2bf(swiglu(v, u)));
+        } else {
+            const uint32_t b = f2bf(v);
+            a.y[size_t(orow) * a.ystride + m] = uint16_t(b);
+            if (MODE == GEMV_LOGITS) key = argmax_key(bf2f(b), uint32_t(m));
+        }
+    }
+    if (MODE == GEMV_LOGITS) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const unsigned long long other = __shfl_xor_sync(FULL_MASK, key, o);
+            key = other > key ? other : key;
+        }
+        if ((threadIdx.x & 31) == 0 && key) atomicMax(a.keys + orow, key);
+    }
+}
+
+// [rows][K] bf16 row-major as a 2-D tensor map: box of 64 k x box_rows rows, 128-byte swizzle,
+// rows past the matrix read as zeros.
+bool encode_kmajor(CUtensorMap* map, const void* base, int rows, int K, int box_rows) {
+    PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
+    if (!encode || K % TC_BK || (reinterpret_cast<uintptr_t>(base) & 15)) return false;
+    const cuuint64_t dims[2] = {cuuint64_t(K), cuuint64_t(rows)};
+    const cuuint64_t strides[1] = {cuuint64_t(K) * 2};
+    const cuuint32_t box[2] = {TC_BK, cuuint32_t(box_rows)};
+    const cuuint32_t unit[2] = {1, 1};
+    return encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, unit,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+struct TcDevice {
+    int sms = 0;
+    int* error = nullptr;
+};
+
+TcDevice* tc_device() {
+    static TcDevice dev[64];
+    int d = 0;
+    if (cudaGetDevice(&d) != cudaSuccess || d < 0 || d >= 64) return nullptr;
+    TcDevice& t = dev[d];
+    if (!t.sms) {
+        if (cudaDeviceGetAttribute(&t.sms, cudaDevAttrMultiProcessorCount, d) != cudaSuccess) return nullptr;
+        if (cudaMalloc(&t.error, sizeof(int)) != cudaSuccess || cudaMemset(t.error, 0, sizeof(int)) != cudaSuccess) {
+            t.sms = 0;
+            return nullptr;
+        }
+    }
+    return &t;
+}
+
+template <int BN, int MODE>
+cudaError_t tc_launch(const GemvArgs& a, int splits, int tiles, TcDevice& dev, cudaStream_t s) {
+    CUtensorMap tmx, tmw;
+    if (!encode_kmajor(&tmx, a.x, a.rows, a.lin.K, BN) ||
+        !encode_kmajor(&tmw, a.lin.w, a.lin.M, a.lin.K, MODE == GEMV_SWIGLU ? TC_BM / 2 : TC_BM))
+        return cudaErrorInvalidValue;
+    k_gemm_tc<BN, MODE><<<tiles * splits, TC_THREADS, TcTile<BN>::SMEM, s>>>(a, tmx, tmw, splits, dev.error);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess || splits == 1) return e;
+    const int Mout = MODE == GEMV_SWIGLU ? a.lin.M / 2 : a.lin.M;
+    k_gemm_tc_finish<MODE><<<dim3((Mout + 255) / 256, a.rows), 256, 0, s>>>(a, splits);
+    return cudaGetLastError();
+}
+
+template <int BN>
+cudaError_t tc_mode(const GemvArgs& a, GemvMode mode, int splits, int tiles, TcDevice& dev, cudaStream_t s) {
+    switch (mode) {
+        case GEMV_PLAIN: return tc_launch<BN, GEMV_PLAIN>(a, splits, tiles, dev, s);
+        case GEMV_SWIGLU: return tc_launch<BN, GEMV_SWIGLU>(a, splits, tiles, dev, s);
+        default: return tc_launch<BN, GEMV_LOGITS>(a, splits, tiles, dev, s);
+    }
+}
+
+template <int BN>
+cudaError_t tc_attr() {
+    cudaError_t e = cudaFuncSetAttribute(k_gemm_tc<BN, GEMV_PLAIN>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcTile<BN>::SMEM);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(k_gemm_tc<BN, GEMV_SWIGLU>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcTile<BN>::SMEM);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(k_gemm_tc<BN, GEMV_LOGITS>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcTile<BN>::SMEM);
+    return e;
+}
+
+}  // namespace
+
+cudaError_t configure_gemm_tc() {
+    cudaError_t e = tc_attr<32>();
+    if (e == cudaSuccess) e = tc_attr<64>();
+    if (e == cudaSuccess) e = tc_attr<128>();
+    return e;
+}
+
+// Raw weights, K a multiple of 64, 16-byte aligned operands (tensor maps).
+bool gemm_tc_supported(const GemvArgs& a) {
+    return a.lin.offsets == nullptr && a.rows >= 1 && a.lin.K >= TC_BK && a.lin.K % TC_BK == 0 && a.lin.M >= 1 &&
+           (reinterpret_cast<uintptr_t>(a.lin.w) & 15) == 0 && (reinterpret_cast<uintptr_t>(a.x) & 15) == 0 &&
+           tensor_map_encoder() != nullptr;
+}
+
+int gemm_tc_plan(const GemvArgs& a, GemvMode mode, int sms, int* bn_out, int* tiles_out) {
+    const int Mout = mode == GEMV_SWIGLU ? a.lin.M / 2 : a.lin.M;
+    const int per = mode == GEMV_SWIGLU ? TC_BM / 2 : TC_BM;
+    const int mtiles = (Mout + per - 1) / per, nkb = a.lin.K / TC_BK;
+    int bn = a.rows <= 32 ? 32 : 64;
+    if (a.rows > 64 && mtiles * ((a.rows + 127) / 128) >= sms) bn = 128;
+    const int tiles = mtiles * ((a.rows + bn - 1) / bn);
+    // split K while the tiles leave SMs idle, each split keeps >= 4 stages of k, and the
+    // partials fit the caller's workspace
+    int splits = 1;
+    while (splits * 2 <= TC_SPLITS_MAX && tiles * splits * 2 <= sms && nkb / (splits * 2) >= 4 && a.part &&
+           size_t(splits) * 2 * a.rows * a.lin.M <= a.part_cap)
+        splits *= 2;
+    *bn_out = bn;
+    *tiles_out = tiles;
+    return splits;
+}
+
+cudaError_t launch_gemm_tc(const GemvArgs& a, GemvMode mode, cudaStream_t s, int splits_override) {
+    if (!gemm_tc_supported(a) || (mode == GEMV_SWIGLU && a.lin.M % 2) || (mode == GEMV_LOGITS && !a.keys))
+        return cudaErrorInvalidValue;
+    TcDevice* dev = tc_device();
+    if (!dev) return cudaErrorInvalidDevice;
+    int bn = 0, tiles = 0;
+    int splits = gemm_tc_plan(a, mode, dev->sms, &bn, &tiles);
+    if (splits_override > 0) {
+        splits = splits_override;
+        if (splits > a.lin.K / TC_BK || splits > TC_SPLITS_MAX ||
+            (splits > 1 && (!a.part || size_t(splits) * a.rows * a.lin.M > a.part_cap)))
+            return cudaErrorInvalidValue;
+    }
+    switch (bn) {
+        case 32: return tc_mode<32>(a, mode, splits, tiles, *dev, s);
+        case 64: return tc_mode<64>(a, mode, splits, tiles, *dev, s);
+        default: return tc_mode<128>(a, mode, splits, tiles, *dev, s);
+    }
+}
+
+int gemm_tc_error(int* out) {
+    TcDevice* dev = tc_device();
+    if (!dev) return 1;
+    return cudaMemcpy(out, dev->error, sizeof(int), cudaMemcpyDeviceToHost) == cudaSuccess ? 0 : 1;
+}
+
+}  // namespace plamo

@@ -74,6 +74,30 @@ int plamo_k_linear(const void* w, const uint32_t* offsets, const uint16_t* x, in
     return e == cudaSuccess ? 0 : kfail(e);
 }
 
+int plamo_k_linear_tc(const void* w, const uint16_t* x, int rows, int K, int M, int mode, uint16_t* y,
+                      uint64_t* argmax_keys, int splits, float* workspace, size_t workspace_floats, void* stream) {
+    if (!w || !x || !y || rows < 1 || K < 64 || K % 64 || M < 1 || mode < 0 || mode > 2 || (mode == 1 && M % 2) ||
+        (mode == 2 && !argmax_keys) || splits < 0 || splits > 16 || splits > K / 64 ||
+        (splits > 1 && (!workspace || size_t(splits) * rows * M > workspace_floats))) {
+        g_error = "Invalid linear arguments";
+        return 1;
+    }
+    if (!configured()) { g_error = "Cannot configure kernels"; return 1; }
+    GemvArgs a;
+    a.lin.w = static_cast<const uint8_t*>(w);
+    a.lin.M = M;
+    a.lin.K = K;
+    a.x = x;
+    a.rows = rows;
+    a.y = y;
+    a.ystride = mode == 1 ? M / 2 : M;
+    a.keys = reinterpret_cast<unsigned long long*>(argmax_keys);
+    a.part = workspace;
+    a.part_cap = workspace ? workspace_floats : 0;
+    cudaError_t e = launch_gemm_tc(a, GemvMode(mode), static_cast<cudaStream_t>(stream), splits);
+    return e == cudaSuccess ? 0 : kfail(e);
+}
+
 int plamo_k_exp(const float* x, float* y, long long n, void* stream) {
     if (!x || !y || n < 1) { g_error = "Invalid exp arguments"; return 1; }
     k_exp<<<unsigned((n + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(x, y, n);

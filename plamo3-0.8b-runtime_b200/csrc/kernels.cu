@@ -575,6 +575,8 @@ static cudaError_t gemv_rows(const GemvArgs& a, int mode, cudaStream_t s) {
 
 cudaError_t launch_gemv(const GemvArgs& a, int mode, cudaStream_t s) {
     if (a.lin.K % 128 || a.lin.K > 8192 || a.rows < 1) return cudaErrorInvalidValue;
+    // dense contraction on the tensor cores, when the caller chose that path
+    if (a.tensor && a.rows >= TC_MIN_ROWS && gemm_tc_supported(a)) return launch_gemm_tc(a, GemvMode(mode), s);
     // many rows of raw weights: the tiled GEMM (same sums, weights read once per 32 rows)
     if (gemm_supported(a)) return launch_gemm(a, GemvMode(mode), s);
     // Rows beyond what the staged activations allow (16, fewer for very long K) run in passes;
@@ -625,6 +627,7 @@ cudaError_t configure_kernels() {
     if (e == cudaSuccess)
         e = cudaFuncSetAttribute(k_attn_partial, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     if (e == cudaSuccess) e = configure_gemm();
+    if (e == cudaSuccess) e = configure_gemm_tc();
     return e;
 }
 

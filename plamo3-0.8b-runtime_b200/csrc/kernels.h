@@ -34,6 +34,9 @@ struct GemvArgs {
     int ystride = 0;
     const int* out_map = nullptr;  // optional row -> output row (batch lanes)
     unsigned long long* keys = nullptr;  // GEMV_LOGITS: argmax keys per output row
+    int tensor = 0;                // dense rows (>= 16) of raw weights go to the tcgen05 GEMM
+    float* part = nullptr;         // tcgen05 split-K partials (optional workspace)
+    size_t part_cap = 0;           // floats in `part`
 };
 
 struct AttnArgs {
@@ -90,6 +93,14 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();
 bool gemm_supported(const GemvArgs& a);
 cudaError_t launch_gemm(const GemvArgs& a, GemvMode mode, cudaStream_t s);
 cudaError_t configure_gemm();
+// tcgen05 GEMM (gemm_tc.cu): bf16 operands, fp32 accumulation on the tensor cores; matches the
+// exact path to within the rounding of the accumulation, not bit for bit. splits_override > 0
+// forces the K split (tests).
+bool gemm_tc_supported(const GemvArgs& a);
+cudaError_t launch_gemm_tc(const GemvArgs& a, GemvMode mode, cudaStream_t s, int splits_override = 0);
+cudaError_t configure_gemm_tc();
+int gemm_tc_error(int* out);
+constexpr int TC_MIN_ROWS = 16;  // fewer rows stay on the order-exact GEMV
 cudaError_t launch_qkv(const QkvArgs& a, cudaStream_t s);
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s);
 cudaError_t launch_finalize(unsigned long long* keys, const int* key_map, int rows, int* result,

@@ -75,6 +75,8 @@ struct Work {
     int* out_map;
     float* part_o;
     float2* part_ml;
+    float* part_tc;         // tcgen05 GEMM split-K partials
+    size_t part_tc_cap;     // floats
     RowDesc* h_desc;
     int* h_ids;
     int* h_out_map;
@@ -99,6 +101,7 @@ struct plamo_runtime {
     Config c;
     int context = 0, chunk = 16, local_cap = 0;
     bool packed = false;
+    bool tensor = false;  // projections over >= 16 rows on the tcgen05 GEMM (plamo_set_tensor_gemm)
     std::string name;
     uint8_t* arena = nullptr;
     size_t arena_bytes = 0, weight_bytes = 0;
@@ -210,6 +213,9 @@ static int pin_alloc(Owner& o, T*& p, size_t count) {
 // Attention runs over at most ATT_ROWS rows per launch, so its split partials are sized for them
 // (a wide prefill would otherwise need rows x splits x heads x 128 floats at once).
 constexpr int ATT_ROWS = 64;
+// Split-K partials of the tcgen05 GEMM (8 MiB): splits of the small projections at up to a few
+// dozen rows; larger calls have tiles enough for every SM and do not split.
+constexpr size_t TC_PART_FLOATS = size_t(2) << 20;
 
 template <typename Owner>
 static int alloc_work(Owner& o, plamo_runtime& rt, Work& w, int rows) {
@@ -218,11 +224,13 @@ static int alloc_work(Owner& o, plamo_runtime& rt, Work& w, int rows) {
     int max_splits = 1;
     for (const Layer& L : rt.layers) max_splits = std::max(max_splits, L.splits);
     w.rows_cap = rows;
+    w.part_tc_cap = TC_PART_FLOATS;
     if (dev_alloc(o, rt, w.x, R * c.d) || dev_alloc(o, rt, w.h, R * c.d) || dev_alloc(o, rt, w.qkv, R * c.qkv_rows()) ||
         dev_alloc(o, rt, w.q, R * c.q_dim()) || dev_alloc(o, rt, w.att, R * c.q_dim()) || dev_alloc(o, rt, w.proj, R * c.d) ||
         dev_alloc(o, rt, w.act, R * c.ffn) || dev_alloc(o, rt, w.geo, R) || dev_alloc(o, rt, w.desc, R) ||
         dev_alloc(o, rt, w.ids, R) || dev_alloc(o, rt, w.out_map, R) ||
         dev_alloc(o, rt, w.part_o, RA * max_splits * c.heads * 128) || dev_alloc(o, rt, w.part_ml, RA * max_splits * c.heads) ||
+        dev_alloc(o, rt, w.part_tc, TC_PART_FLOATS) ||
         pin_alloc(o, w.h_desc, R) || pin_alloc(o, w.h_ids, R) || pin_alloc(o, w.h_out_map, R))
         return 1;
     return 0;
@@ -319,9 +327,13 @@ static int enqueue_forward(plamo_runtime& rt, Work& w, int rows, const CacheView
     LAUNCH(K_NORM, launch_embed_norm(w.ids, rows, c.vocab, rt.embed, rt.layers[0].pre_mixer, c.d, w.x, w.h, nout ? o.keys : nullptr,
                                      w.out_map, nout, s));
     const float post_mlp_offset = float(1.0 / std::pow(5.0, 1.5));  // Runtime.swift:450
+    GemvArgs tc;  // path selection shared by every projection of the pass
+    tc.tensor = rt.tensor ? 1 : 0;
+    tc.part = w.part_tc;
+    tc.part_cap = w.part_tc_cap;
     for (int l = 0; l < c.layers; l++) {
         const Layer& L = rt.layers[l];
-        GemvArgs g;
+        GemvArgs g = tc;
         g.lin = L.qkv; g.x = w.h; g.rows = rows; g.y = w.qkv; g.ystride = c.qkv_rows();
         LAUNCH(K_GEMV, launch_gemv(g, GEMV_PLAIN, s));
         QkvArgs q;
@@ -341,17 +353,17 @@ static int enqueue_forward(plamo_runtime& rt, Work& w, int rows, const CacheView
             b.desc = w.desc + r0; b.geo = w.geo + r0;
             LAUNCH(K_ATTN, launch_attention(b, s));
         }
-        g = GemvArgs();
+        g = tc;
         g.lin = L.o; g.x = w.att; g.rows = rows; g.y = w.proj; g.ystride = c.d;
         LAUNCH(K_GEMV, launch_gemv(g, GEMV_PLAIN, s));
         NormArgs n;
         n.w = L.post_mixer; n.src = w.proj; n.x = w.x; n.next_w = L.pre_mlp; n.next = w.h; n.rows = rows; n.n = c.d;
         n.offset = 0.2f; n.residual = 1;
         LAUNCH(K_NORM, launch_norm(n, s));
-        g = GemvArgs();
+        g = tc;
         g.lin = L.gate_up; g.x = w.h; g.rows = rows; g.y = w.act; g.ystride = c.ffn;
         LAUNCH(K_GEMV, launch_gemv(g, GEMV_SWIGLU, s));
-        g = GemvArgs();
+        g = tc;
         g.lin = L.down; g.x = w.act; g.rows = rows; g.y = w.proj; g.ystride = c.d;
         LAUNCH(K_GEMV, launch_gemv(g, GEMV_PLAIN, s));
         n = NormArgs();
@@ -364,7 +376,7 @@ static int enqueue_forward(plamo_runtime& rt, Work& w, int rows, const CacheView
     n.w = rt.final_norm; n.src = w.x + size_t(rows - nout) * c.d; n.x = w.h; n.y2 = o.hidden; n.out_map = w.out_map;
     n.rows = nout; n.n = c.d; n.offset = 1.0f; n.residual = 0;
     LAUNCH(K_NORM, launch_norm(n, s));
-    GemvArgs g;
+    GemvArgs g = tc;
     g.lin = rt.head; g.x = w.h; g.rows = nout; g.y = o.logits; g.ystride = c.vocab; g.out_map = w.out_map; g.keys = o.keys;
     LAUNCH(K_GEMV, launch_gemv(g, GEMV_LOGITS, s));
     LAUNCH(K_HEAD, launch_finalize(o.keys, w.out_map, nout, o.result, chain ? w.ids : nullptr, chain ? w.desc : nullptr,
@@ -1108,6 +1120,11 @@ size_t plamo_weight_bytes(const plamo_runtime* rt) { return rt ? rt->weight_byte
 size_t plamo_device_bytes(const plamo_runtime* rt) { return rt ? rt->device_bytes : 0; }
 const char* plamo_device_name(const plamo_runtime* rt) { return rt ? rt->name.c_str() : ""; }
 double plamo_broadcast_seconds(const plamo_runtime* rt) { return rt ? rt->bcast_seconds : 0; }
+int plamo_set_tensor_gemm(plamo_runtime* rt, int enable) {
+    if (!rt) return fail("Invalid runtime");
+    rt->tensor = enable != 0;
+    return 0;
+}
 
 int plamo_dims(const plamo_runtime* rt, int32_t out[10]) {
     if (!rt || !out) return fail("Invalid arguments");

@@ -92,9 +92,12 @@ def library() -> ctypes.CDLL:
         "plamo_profile_decode": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.POINTER(ctypes.c_double), _i32p]),
         "plamo_persistent_decode": (ctypes.c_int, [_vp]),
         "plamo_trace_decode": (ctypes.c_int, [_vp, _vp, ctypes.c_size_t, _i32p]),
+        "plamo_set_tensor_gemm": (ctypes.c_int, [_vp, ctypes.c_int]),
         "plamo_last_error": (ctypes.c_char_p, []),
         # kernel-level entry points (include/plamo_kernels.h)
         "plamo_k_linear": (ctypes.c_int, [_vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp, _vp, _vp]),
+        "plamo_k_linear_tc": (ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp, _vp,
+                                             ctypes.c_int, _vp, ctypes.c_size_t, _vp]),
         "plamo_k_argmax_keys": (ctypes.c_int, [_vp, ctypes.c_int, _vp, _vp]),
         "plamo_k_norm": (ctypes.c_int, [_vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_float, ctypes.c_int, _vp, _vp, _vp]),
         "plamo_k_argmax": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int, _vp, _vp, _vp]),
@@ -217,6 +220,11 @@ class Runtime:
         det = buf[G * (P + 1) * S: need].reshape(G, D).astype(np.int64)
         origin = t[:, -1, 0].min()
         return t - origin, np.where(det > 0, det - origin, -1)
+
+    def set_tensor_gemm(self, enable: bool = True):
+        """Projections over >= 16 rows on the tcgen05 tensor-core GEMM (prefill, batched steps):
+        results within the accumulation-order tolerance of the default path, not bit for bit."""
+        _check(library().plamo_set_tensor_gemm(self._h, int(bool(enable))))
 
     @property
     def persistent(self) -> bool:
@@ -360,6 +368,11 @@ def decode_batch(batch: Batch, prompts, limits, stop_on_truncation: bool = False
 
 def k_linear(w, offsets, x, rows, K, M, mode, y, keys=0, stream=0):
     _check(library().plamo_k_linear(w, offsets or None, x, rows, K, M, mode, y, keys or None, stream or None))
+
+
+def k_linear_tc(w, x, rows, K, M, mode, y, keys=0, splits=0, workspace=0, workspace_floats=0, stream=0):
+    _check(library().plamo_k_linear_tc(w, x, rows, K, M, mode, y, keys or None, int(splits), workspace or None,
+                                       int(workspace_floats), stream or None))
 
 
 def k_argmax_keys(keys, rows, out, stream=0):
