@@ -253,6 +253,44 @@ def workload_config(args):
             "l2": "weights (1.45 GB) exceed L2 (126 MB): no flush needed"}
 
 
+def kernel_case(args):
+    """One projection (rows x K activations, M x K seeded weights; mode 0 plain, 1 SwiGLU, 2 logits)
+    on the tcgen05 GEMM and on the order-exact CUDA-core path: CUDA-event time per call over
+    --steps calls after --warmup, achieved TFLOP/s against the measured bf16 peak. Used for kernel
+    profiles (a small case that ncu captures in seconds)."""
+    import torch
+    rows, K, M, mode = (int(v) for v in args.kernel_case.split(","))
+    R = pkg().runtime
+    g = torch.Generator().manual_seed(0)
+    w = (torch.randn(M, K, generator=g) * 0.02).bfloat16().cuda()
+    x = torch.randn(rows, K, generator=g).bfloat16().cuda()
+    y = torch.zeros(rows, M // 2 if mode == 1 else M, dtype=torch.bfloat16, device="cuda")
+    keys = torch.zeros(rows, dtype=torch.int64, device="cuda")
+    ws = torch.zeros(2 << 20, dtype=torch.float32, device="cuda")
+    pk = peaks()
+    out = dict(case=dict(rows=rows, K=K, M=M, mode=mode), flop=2.0 * rows * K * M, weight_bytes=2 * K * M)
+    calls = {
+        "tcgen05": lambda: R.k_linear_tc(w.data_ptr(), x.data_ptr(), rows, K, M, mode, y.data_ptr(), keys.data_ptr(),
+                                         0, ws.data_ptr(), ws.numel()),
+        "exact": lambda: R.k_linear(w.data_ptr(), 0, x.data_ptr(), rows, K, M, mode, y.data_ptr(), keys.data_ptr()),
+    }
+    for name, fn in calls.items():
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / args.steps
+        tf = out["flop"] / us / 1e6
+        out[name] = dict(us=us, tflops=tf, tensor_frac=tf / pk["bf16"], weight_gbs=out["weight_bytes"] / us / 1e3)
+    print(json.dumps(out), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -268,11 +306,15 @@ def main():
     ap.add_argument("--segment-lanes", type=int, default=32)
     ap.add_argument("--segment-steps", type=int, default=32)
     ap.add_argument("--prefill-reps", type=int, default=5)
+    ap.add_argument("--kernel-case", default=None,
+                    help="rows,K,M,mode: time one projection on the tcgen05 GEMM and the exact GEMM, then exit")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     if args.impl == "reference":
         return run_reference(args)
+    if args.kernel_case:
+        return kernel_case(args)
 
     import torch
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -370,9 +412,11 @@ def main():
         if dist: dist.barrier()
         torch.cuda.synchronize()
         s0 = sb.gpu_seconds
+        torch.cuda.nvtx.range_push("segment_steps_" + ("tensor" if tensor else "exact"))  # ncu --nvtx-include
         for _ in range(args.segment_steps):
             nxt = sb.step(nxt)
         torch.cuda.synchronize()
+        torch.cuda.nvtx.range_pop()
         st = torch.tensor([sb.gpu_seconds - s0, prefill_s], device="cuda", dtype=torch.float64)
         if dist: dist.all_reduce(st, op=dist.ReduceOp.MAX)
         sb.close()
@@ -402,7 +446,11 @@ def main():
             for i in range(args.prefill_reps + 1):  # the first run warms up
                 prt.reset()
                 g0 = prt.gpu_seconds
+                if i == 1:
+                    torch.cuda.nvtx.range_push("prefill_" + mode)  # one timed prefill, for ncu --nvtx-include
                 prt.prefill(prompt)
+                if i == 1:
+                    torch.cuda.nvtx.range_pop()
                 if i:
                     times.append(prt.gpu_seconds - g0)
             tt = torch.tensor([sorted(times)[len(times) // 2]], device="cuda", dtype=torch.float64)

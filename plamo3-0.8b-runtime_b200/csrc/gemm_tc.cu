@@ -18,7 +18,8 @@
 // Roles (128 threads): lane 0 of warp 0 issues the TMA copies (STAGES deep, a stage is refilled
 // once the MMAs that read it have committed to its `empty` barrier); lane 0 of warp 1 issues the
 // MMAs; then all four warps drain tensor memory (warp w reads lanes 32w..32w+31) and write bf16
-// outputs, SwiGLU products or logits with argmax keys. A tile with few weight rows (small M at few
+// outputs, SwiGLU products (gate and up halves exchanged through shared memory, so all four warps
+// share that math) or logits with argmax keys. A tile with few weight rows (small M at few
 // activation rows) splits K over `splits` CTAs that store fp32 partials; a second kernel adds them
 // in split order and applies the same epilogue.
 #include "common.cuh"
@@ -188,7 +189,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     if (finished && !*stop) {
         const int row = warp * 32 + lane;  // tensor-memory lane = weight row of the tile
         const uint32_t lane_base = uint32_t(warp * 32) << 16;
-        float* xch = reinterpret_cast<float*>(smem);  // SwiGLU: up values [64][17] (stages are drained)
+        // SwiGLU exchange (the stages are drained): gate values of columns 8..15 for warps 2-3,
+        // up values of columns 0..7 for warps 0-1, [64][9] each
+        float* xg = reinterpret_cast<float*>(smem);
+        float* xu = xg + 64 * 9;
         for (int c0 = 0; c0 < BN && n0 + c0 < a.rows; c0 += 16) {
             uint32_t v[16];
             tmem_ld16(tmem + lane_base + uint32_t(c0), v);
@@ -209,19 +213,26 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     }
                 }
             } else if (MODE == GEMV_SWIGLU) {
-                if (warp >= 2) {
+                // warps 0-1 hold the gate sums and finish columns 0..7, warps 2-3 the up sums and
+                // finish columns 8..15: each passes the other half of its columns across
+                const bool gate = warp < 2;
+                const int i = row & 63;
 #pragma unroll
-                    for (int j = 0; j < 16; j++) xch[(row - 64) * 17 + j] = __uint_as_float(v[j]);
+                for (int j = 0; j < 8; j++) {
+                    if (gate) xg[i * 9 + j] = __uint_as_float(v[8 + j]);
+                    else xu[i * 9 + j] = __uint_as_float(v[j]);
                 }
                 __syncthreads();
-                if (warp < 2 && m0 + row < Mout) {
+                if (m0 + i < Mout) {
 #pragma unroll
-                    for (int j = 0; j < 16; j++) {
-                        const int r = n0 + c0 + j;
+                    for (int j = 0; j < 8; j++) {
+                        const int col = gate ? j : 8 + j;
+                        const int r = n0 + c0 + col;
                         if (r < a.rows) {
                             const int orow = a.out_map ? a.out_map[r] : r;
-                            a.y[size_t(orow) * a.ystride + m0 + row] =
-                                uint16_t(f2bf(swiglu(__uint_as_float(v[j]), xch[row * 17 + j])));
+                            const float g = gate ? __uint_as_float(v[j]) : xg[i * 9 + j];
+                            const float u = gate ? xu[i * 9 + j] : __uint_as_float(v[8 + j]);
+                            a.y[size_t(orow) * a.ystride + m0 + i] = uint16_t(f2bf(swiglu(g, u)));
                         }
                     }
                 }
