@@ -349,7 +349,7 @@ constexpr int AT = 64;  // keys per staged K / V tile
 int attention_per_max(int cap, int splits) { return ((cap + splits - 1) / splits + 31) & ~31; }
 size_t attention_smem(int H, int KV, int per_max) {
     return sizeof(float) * (size_t(H) * QS + size_t(AT) * (KV * 128 + 1) + size_t(AT) * 64 + size_t(H) * per_max) +
-           size_t(AT) * KV * 128 * 2;
+           2 * size_t(AT) * KV * 128 * 2;  // key / value staging, and the first value tile fetched early
 }
 
 // Stages rows [k0, k0 + tk) of the key (or value) cache window into shared memory as raw bf16 with
@@ -362,6 +362,22 @@ __device__ __forceinline__ void stage_rows(uint4* dst, const uint16_t* base, int
         const int phys = (first + k0 + j) % cap;
         dst[i] = __ldg(reinterpret_cast<const uint4*>(base + size_t(phys) * KV * 128) + c);
     }
+}
+
+// The same rows copied with cp.async (16 bytes a thread, L2 to shared memory), so the copy runs
+// while the block computes; complete after cp_async_wait_all and a barrier.
+__device__ __forceinline__ void stage_rows_async(uint4* dst, const uint16_t* base, int first, int k0, int tk, int cap,
+                                                 int KV) {
+    const int rowv = KV * 16;
+    for (int i = threadIdx.x; i < tk * rowv; i += blockDim.x) {
+        const int j = i / rowv, c = i - j * rowv;
+        const int phys = (first + k0 + j) % cap;
+        const uint4* src = reinterpret_cast<const uint4*>(base + size_t(phys) * KV * 128) + c;
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(dst + i))),
+                     "l"(src)
+                     : "memory");
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
 }
 
 __global__ void __launch_bounds__(256) k_attn_partial(AttnArgs a) {
@@ -384,11 +400,14 @@ __global__ void __launch_bounds__(256) k_attn_partial(AttnArgs a) {
     uint32_t* rope = reinterpret_cast<uint32_t*>(kr + AT * KS);  // [AT][64]
     float* sc = reinterpret_cast<float*>(rope + AT * 64);        // [H][per_max]
     uint4* raw = reinterpret_cast<uint4*>(sc + H * a.per_max);   // [AT][KV*128] bf16
+    uint4* vfirst = raw + AT * KV * 16;                          // [AT][KV*128] bf16: value tile 0
     const uint16_t* raw16 = reinterpret_cast<const uint16_t*>(raw);
     const uint16_t* kbase = a.keys + size_t(lane_id) * a.lane_stride;
     const uint16_t* vbase = a.values + size_t(lane_id) * a.lane_stride;
-    for (int i = t; i < H * 128; i += 256) qs[(i >> 7) * QS + (i & 127)] = bf2f(a.q[size_t(r) * H * 128 + i]);
     const int n = hi - lo;
+    // the first value tile streams in while the keys are staged, rotated and scored
+    stage_rows_async(vfirst, vbase, g.first, lo, min(AT, n), a.cap, KV);
+    for (int i = t; i < H * 128; i += 256) qs[(i >> 7) * QS + (i & 127)] = bf2f(a.q[size_t(r) * H * 128 + i]);
     // pass 1: scores of every visible key of this split
     for (int t0 = 0; t0 < n; t0 += AT) {
         const int tk = min(AT, n - t0);
@@ -445,10 +464,12 @@ __global__ void __launch_bounds__(256) k_attn_partial(AttnArgs a) {
     for (int t0 = 0; t0 < n; t0 += AT) {
         const int tk = min(AT, n - t0);
         __syncthreads();
-        stage_rows(raw, vbase, g.first, lo + t0, tk, a.cap, KV);
+        if (t0 == 0) asm volatile("cp.async.wait_all;" ::: "memory");
+        else stage_rows(raw, vbase, g.first, lo + t0, tk, a.cap, KV);
         __syncthreads();
+        const uint16_t* vtile = t0 == 0 ? reinterpret_cast<const uint16_t*>(vfirst) : raw16;
         for (int i = 0; i < tk; i++) {
-            const uint16_t* vr = raw16 + i * KV * 128;
+            const uint16_t* vr = vtile + i * KV * 128;
             if (KV == 1) {
                 const float v = bf2f(vr[d]);
 #pragma unroll
@@ -473,18 +494,37 @@ __global__ void __launch_bounds__(256) k_attn_partial(AttnArgs a) {
     }
 }
 
+// Splits are taken in order, eight at a time: their statistics and partials are loaded together
+// before the dependent max / fma chains run over them.
 __global__ void __launch_bounds__(128) k_attn_merge(AttnArgs a) {
     const int r = blockIdx.x / a.H, h = blockIdx.x - r * a.H, d = threadIdx.x;
     const float2* ml = a.part_ml + size_t(r) * a.splits * a.H;
+    const float* po = a.part_o + size_t(r) * a.splits * a.H * 128 + h * 128 + d;
+    const size_t po_split = size_t(a.H) * 128;
     float M = -INFINITY;
-    for (int s = 0; s < a.splits; s++) M = fmaxf(M, ml[s * a.H + h].x);
+    for (int s0 = 0; s0 < a.splits; s0 += 8) {
+        float m[8];
+#pragma unroll
+        for (int j = 0; j < 8; j++) m[j] = s0 + j < a.splits ? ml[(s0 + j) * a.H + h].x : -INFINITY;
+#pragma unroll
+        for (int j = 0; j < 8; j++) M = fmaxf(M, m[j]);
+    }
     float L = 0.f, o = 0.f;
-    for (int s = 0; s < a.splits; s++) {
-        const float2 st = ml[s * a.H + h];
-        if (st.y > 0.f) {
-            const float w = pexp(st.x - M);
-            L = fmaf(w, st.y, L);
-            o = fmaf(a.part_o[((size_t(r) * a.splits + s) * a.H + h) * 128 + d], w, o);
+    for (int s0 = 0; s0 < a.splits; s0 += 8) {
+        float2 st[8];
+        float pv[8];
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            st[j] = s0 + j < a.splits ? ml[(s0 + j) * a.H + h] : make_float2(-INFINITY, 0.f);
+            pv[j] = s0 + j < a.splits ? po[(s0 + j) * po_split] : 0.f;  // used only when the split had keys
+        }
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            if (st[j].y > 0.f) {
+                const float w = pexp(st[j].x - M);
+                L = fmaf(w, st[j].y, L);
+                o = fmaf(pv[j], w, o);
+            }
         }
     }
     a.out[size_t(r) * a.H * 128 + h * 128 + d] = uint16_t(f2bf(o / L));

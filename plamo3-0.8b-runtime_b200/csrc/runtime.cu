@@ -68,6 +68,7 @@ struct CacheView {
 
 struct Work {
     int rows_cap = 0;
+    int att_rows = 0;  // rows per attention launch (its split partials hold that many)
     uint16_t *x, *h, *qkv, *q, *att, *proj, *act;
     RowGeo* geo;
     RowDesc* desc;
@@ -210,9 +211,11 @@ static int pin_alloc(Owner& o, T*& p, size_t count) {
     return 0;
 }
 
-// Attention runs over at most ATT_ROWS rows per launch, so its split partials are sized for them
-// (a wide prefill would otherwise need rows x splits x heads x 128 floats at once).
+// Attention runs over a bounded number of rows per launch, so its split partials are sized for
+// them (a wide prefill would otherwise need rows x splits x heads x 128 floats at once): as many
+// rows as ATT_PART_BYTES of partials hold, and at least ATT_ROWS.
 constexpr int ATT_ROWS = 64;
+constexpr size_t ATT_PART_BYTES = size_t(64) << 20;
 // Split-K partials of the tcgen05 GEMM (8 MiB): splits of the small projections at up to a few
 // dozen rows; larger calls have tiles enough for every SM and do not split.
 constexpr size_t TC_PART_FLOATS = size_t(2) << 20;
@@ -220,9 +223,11 @@ constexpr size_t TC_PART_FLOATS = size_t(2) << 20;
 template <typename Owner>
 static int alloc_work(Owner& o, plamo_runtime& rt, Work& w, int rows) {
     const Config& c = rt.c;
-    const size_t R = size_t(rows), RA = size_t(std::min(rows, ATT_ROWS));
     int max_splits = 1;
     for (const Layer& L : rt.layers) max_splits = std::max(max_splits, L.splits);
+    const size_t row_part = size_t(max_splits) * c.heads * (128 * sizeof(float) + sizeof(float2));
+    w.att_rows = int(std::min<size_t>(rows, std::max<size_t>(ATT_ROWS, ATT_PART_BYTES / row_part)));
+    const size_t R = size_t(rows), RA = size_t(w.att_rows);
     w.rows_cap = rows;
     w.part_tc_cap = TC_PART_FLOATS;
     if (dev_alloc(o, rt, w.x, R * c.d) || dev_alloc(o, rt, w.h, R * c.d) || dev_alloc(o, rt, w.qkv, R * c.qkv_rows()) ||
@@ -346,9 +351,9 @@ static int enqueue_forward(plamo_runtime& rt, Work& w, int rows, const CacheView
         a.q = w.q; a.keys = cv.keys[l]; a.values = cv.values[l]; a.desc = w.desc; a.geo = w.geo; a.rope_local = rt.rope_local;
         a.part_o = w.part_o; a.part_ml = w.part_ml; a.out = w.att; a.lane_stride = cv.stride[l]; a.rows = rows;
         a.H = c.heads; a.KV = c.kv_heads; a.cap = L.cap; a.full = L.full; a.splits = L.splits; a.per_max = L.per_max;
-        for (int r0 = 0; r0 < rows; r0 += ATT_ROWS) {
+        for (int r0 = 0; r0 < rows; r0 += w.att_rows) {
             AttnArgs b = a;
-            b.rows = std::min(ATT_ROWS, rows - r0);
+            b.rows = std::min(w.att_rows, rows - r0);
             b.q = w.q + size_t(r0) * c.q_dim(); b.out = w.att + size_t(r0) * c.q_dim();
             b.desc = w.desc + r0; b.geo = w.geo + r0;
             LAUNCH(K_ATTN, launch_attention(b, s));
