@@ -52,6 +52,31 @@ bool encode_rows_map(CUtensorMap* map, const void* base, int rows, int K, int li
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// One error word per device shared by the tiled GEMMs (this file and gemm_tc.cu): a stage wait
+// that gives up stores a non-zero code.
+int* gemm_error_word(bool create) {
+    static std::mutex mu;
+    static int* words[64] = {nullptr};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+    std::lock_guard<std::mutex> lock(mu);
+    if (!words[dev] && create) {
+        int* w = nullptr;
+        if (cudaMalloc(&w, sizeof(int)) != cudaSuccess || cudaMemset(w, 0, sizeof(int)) != cudaSuccess) return nullptr;
+        words[dev] = w;
+    }
+    return words[dev];
+}
+
+int gemm_take_error() {
+    int* w = gemm_error_word(false);
+    if (!w) return 0;
+    int v = 0;
+    if (cudaMemcpy(&v, w, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return -1;
+    if (v) cudaMemset(w, 0, sizeof(int));
+    return v;
+}
+
 namespace {
 
 constexpr int TR = 32;  // activation rows per tile (4 per warp)
@@ -238,16 +263,13 @@ cudaError_t gemm_launch(const GemvArgs& a, cudaStream_t s) {
         return cudaErrorInvalidValue;
     const int tiles = ((Mout + per - 1) / per) * ((a.rows + TR - 1) / TR);
     static int sms[64] = {0};
-    static int* err[64] = {nullptr};
     int dev = 0;
     cudaGetDevice(&dev);
-    if (!sms[dev & 63]) {
-        cudaDeviceGetAttribute(&sms[dev & 63], cudaDevAttrMultiProcessorCount, dev);
-        if (cudaMalloc(&err[dev & 63], sizeof(int)) != cudaSuccess) return cudaErrorMemoryAllocation;
-        cudaMemset(err[dev & 63], 0, sizeof(int));
-    }
+    if (!sms[dev & 63]) cudaDeviceGetAttribute(&sms[dev & 63], cudaDevAttrMultiProcessorCount, dev);
+    int* err = gemm_error_word(true);
+    if (!err) return cudaErrorMemoryAllocation;
     const int grid = tiles < sms[dev & 63] ? tiles : sms[dev & 63];  // persistent: one CTA per SM
-    k_gemm<MODE><<<grid, 256, GEMM_SMEM, s>>>(a, tmx, tmw, err[dev & 63]);
+    k_gemm<MODE><<<grid, 256, GEMM_SMEM, s>>>(a, tmx, tmw, err);
     return cudaGetLastError();
 }
 

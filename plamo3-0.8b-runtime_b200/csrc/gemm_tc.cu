@@ -321,7 +321,7 @@ bool encode_kmajor(CUtensorMap* map, const void* base, int rows, int K, int box_
 
 struct TcDevice {
     int sms = 0;
-    int* error = nullptr;
+    int* error = nullptr;  // the device's tiled-GEMM error word (gemm.cu)
 };
 
 TcDevice* tc_device() {
@@ -330,8 +330,8 @@ TcDevice* tc_device() {
     if (cudaGetDevice(&d) != cudaSuccess || d < 0 || d >= 64) return nullptr;
     TcDevice& t = dev[d];
     if (!t.sms) {
-        if (cudaDeviceGetAttribute(&t.sms, cudaDevAttrMultiProcessorCount, d) != cudaSuccess) return nullptr;
-        if (cudaMalloc(&t.error, sizeof(int)) != cudaSuccess || cudaMemset(t.error, 0, sizeof(int)) != cudaSuccess) {
+        t.error = gemm_error_word(true);
+        if (!t.error || cudaDeviceGetAttribute(&t.sms, cudaDevAttrMultiProcessorCount, d) != cudaSuccess) {
             t.sms = 0;
             return nullptr;
         }
@@ -426,10 +426,5 @@ cudaError_t launch_gemm_tc(const GemvArgs& a, GemvMode mode, cudaStream_t s, int
     }
 }
 
-int gemm_tc_error(int* out) {
-    TcDevice* dev = tc_device();
-    if (!dev) return 1;
-    return cudaMemcpy(out, dev->error, sizeof(int), cudaMemcpyDeviceToHost) == cudaSuccess ? 0 : 1;
-}
 
 }  // namespace plamo

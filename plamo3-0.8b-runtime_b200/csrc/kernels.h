@@ -99,7 +99,10 @@ cudaError_t configure_gemm();
 bool gemm_tc_supported(const GemvArgs& a);
 cudaError_t launch_gemm_tc(const GemvArgs& a, GemvMode mode, cudaStream_t s, int splits_override = 0);
 cudaError_t configure_gemm_tc();
-int gemm_tc_error(int* out);
+// Error word of the tiled GEMMs on the current device (created on first use when `create`);
+// gemm_take_error reads and clears it (0: no stage wait gave up since the last call).
+int* gemm_error_word(bool create);
+int gemm_take_error();
 constexpr int TC_MIN_ROWS = 16;  // fewer rows stay on the order-exact GEMV
 cudaError_t launch_qkv(const QkvArgs& a, cudaStream_t s);
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s);

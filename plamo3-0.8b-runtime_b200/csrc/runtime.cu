@@ -406,6 +406,14 @@ static int finish(plamo_runtime& rt, double* seconds) {
     return 0;
 }
 
+// After a call that may have run the tiled GEMMs (more than one row): a stage wait that gave up
+// fails the call instead of returning its partial results.
+static int check_gemm() {
+    const int code = gemm_take_error();
+    if (code) return fail("GEMM stage wait timed out (code " + std::to_string(code) + ")");
+    return 0;
+}
+
 static int capture_decode_graph(plamo_runtime& rt) {
     cudaGraph_t g = nullptr;
     CK(cudaStreamBeginCapture(rt.stream, cudaStreamCaptureModeThreadLocal));
@@ -644,6 +652,7 @@ static int prefill_rows(plamo_runtime& rt, Work& w, const CacheView& cv, Outputs
         CK(cudaEventRecord(rt.e0, rt.stream));
         if (enqueue_forward(rt, w, rows, cv, nout, o, false)) return 1;
         if (finish(rt, seconds)) return 1;
+        if (rows > 1 && check_gemm()) return 1;
     }
     return 0;
 }
@@ -671,6 +680,7 @@ static int forward_impl(plamo_runtime& rt, const int32_t* ids, int n, bool outpu
     if (output) CK(cudaMemcpyAsync(rt.out.h_result, rt.out.result, sizeof(int), cudaMemcpyDeviceToHost, rt.stream));
     if (finish(rt, &rt.gpu_seconds)) return 1;
     if (step && mega_check(rt)) return 1;
+    if (!step && n > 1 && check_gemm()) return 1;
     rt.position += n;
     rt.last_rows = output ? 1 : 0;
     if (output) rt.last_result = rt.out.h_result[0];
@@ -1247,7 +1257,7 @@ int plamo_batch_step(plamo_batch* b, const int32_t* tokens, int n, int32_t* next
     CK(cudaEventRecord(rt.e0, rt.stream));
     if (enqueue_forward(rt, w, rows, b->cache, rows, b->out, false)) { b->ready = false; return 1; }
     CK(cudaMemcpyAsync(b->out.h_result, b->out.result, sizeof(int) * n, cudaMemcpyDeviceToHost, rt.stream));
-    if (finish(rt, &b->gpu_seconds)) { b->ready = false; return 1; }
+    if (finish(rt, &b->gpu_seconds) || (rows > 1 && check_gemm())) { b->ready = false; return 1; }
     for (int l = 0; l < n; l++)
         if (tokens[l] >= 0) b->positions[l] += 1;
     for (int l = 0; l < n; l++) next_ids[l] = b->out.h_result[l];
