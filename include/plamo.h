@@ -126,6 +126,23 @@ PLAMO_API int plamo_persistent_decode(const plamo_runtime*);
  * .p12 weights are unaffected. Off by default. Returns 0, or 1 for a null handle. */
 PLAMO_API int plamo_set_tensor_gemm(plamo_runtime*, int enable);
 
+/* Sampler.select (Sampler.swift:9-31) on the device, over the logits of slot 0 as
+ * plamo_logits would return them: for ids in history[0..n) (Main.swift passes the generated
+ * tokens), the repetition penalty (positive logits divided by `penalty`, others multiplied), then
+ * `presence` subtracted, then `frequency` x the id's count subtracted, applied when penalty != 1 or
+ * presence != 0 or frequency != 0; with no_repeat_ngram > 1, ids that would complete an n-gram
+ * already in the history (Sampler.forbidden, Sampler.swift:54-70) become -inf; then the first
+ * index of the largest value (NaN and -inf never win; 0 when nothing is above -inf). Only the
+ * history travels to the device; the logits stay where the head wrote them and are not modified.
+ * Returns 0 and writes *out_id, or 1 ("Invalid select arguments" / a CUDA error). */
+PLAMO_API int plamo_select(plamo_runtime*, const int32_t* history, int n, float penalty, int no_repeat_ngram,
+                           float frequency, float presence, int32_t* out_id);
+
+/* Sampler.repetitionPeriod (Sampler.swift:35-51), host code: the shortest period 1...32 such that
+ * the tail of tokens[0..n) is that block repeated max(repeats, ceil(24 / period)) times; 0 when
+ * there is none (the Swift nil) or repeats < 2. Needs no device. */
+PLAMO_API int plamo_repetition_period(const int32_t* tokens, int n, int repeats);
+
 /* Profiling: runs `steps` batch-1 decode steps (as plamo_decode_chain) with every kernel launch
  * bracketed by CUDA events. class_ms[6] / launches[6] receive the summed device milliseconds and
  * launch counts per kernel class: 0 GEMV (projections, lm_head), 1 QK-norm + RoPE + KV append,

@@ -39,6 +39,14 @@ PLAMO_API int plamo_k_linear_tc(const void* w, const uint16_t* x, int rows, int 
                                 uint64_t* argmax_keys, int splits, float* workspace, size_t workspace_floats,
                                 void* stream);
 
+/* Sampler.select on caller-owned device buffers: logits [V] bf16, history [n] ids, scratch counts
+ * [V] int32 and flags [V] bytes (cleared by the call); key_out receives the winning argmax key
+ * (0 when no value is above -inf: the selected id is then 0, else 0xFFFFFFFF - low 32 bits).
+ * Same semantics as plamo_select. */
+PLAMO_API int plamo_k_select(const uint16_t* logits, int V, const int32_t* history, int n, float penalty,
+                             int no_repeat_ngram, float frequency, float presence, int32_t* counts, uint8_t* flags,
+                             uint64_t* key_out, void* stream);
+
 /* Converts argmax keys to indices (0xFFFFFFFF when a row had only NaN). */
 PLAMO_API int plamo_k_argmax_keys(const uint64_t* keys, int rows, uint32_t* out, void* stream);
 

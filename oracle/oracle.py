@@ -440,3 +440,70 @@ def packed_decode(data: np.ndarray, entries: np.ndarray, count: int) -> np.ndarr
     out = np.empty(count, dtype=np.uint16)
     lib().oracle_packed_decode(data.ctypes.data, entries.ctypes.data, count, _p(out, _u16p))
     return out
+
+
+# ---------------------------------------------------------------------------------------
+# decoding controls (Sampler.swift), restated for the device sampler's parity tests
+
+def sampler_forbidden(history, n: int) -> set:
+    """Sampler.forbidden (Sampler.swift:54-70): ids that would complete an n-gram whose first n-1
+    tokens equal the history's last n-1 tokens."""
+    if n <= 1 or len(history) < n:
+        return set()
+    span = n - 1
+    last = len(history) - span
+    out = set()
+    for start in range(last):
+        if all(history[start + o] == history[last + o] for o in range(span)):
+            out.add(history[start + span])
+    return out
+
+
+def sampler_select(logits, history, penalty: float, no_repeat_ngram: int, frequency: float = 0.0,
+                   presence: float = 0.0) -> int:
+    """Sampler.select (Sampler.swift:9-31) in fp32: per history id (count c) the repetition penalty
+    (x / p when x > 0, else x * p), minus presence, minus frequency * c; -inf for forbidden ids;
+    then the first index whose value exceeds every earlier one, starting from -inf (0 if none)."""
+    v = np.array(logits, dtype=np.float32).copy()
+    V = len(v)
+    p, fr, pr = np.float32(penalty), np.float32(frequency), np.float32(presence)
+    if p != 1 or pr != 0 or fr != 0:
+        counts = {}
+        for i in history:
+            if 0 <= i < V:
+                counts[i] = counts.get(i, 0) + 1
+        for i, c in counts.items():
+            x = v[i]
+            if p != 1:
+                x = x / p if x > 0 else x * p
+            if pr != 0:
+                x = x - pr
+            if fr != 0:
+                x = x - fr * np.float32(c)
+            v[i] = x
+    if no_repeat_ngram > 1:
+        for i in sampler_forbidden(list(history), no_repeat_ngram):
+            if 0 <= i < V:
+                v[i] = -np.inf
+    with np.errstate(invalid="ignore"):
+        ok = v > -np.inf
+    if not ok.any():
+        return 0
+    best = v[ok].max()
+    return int(np.flatnonzero(ok & (v == best))[0])
+
+
+def sampler_repetition_period(tokens, repeats: int):
+    """Sampler.repetitionPeriod (Sampler.swift:35-51): shortest period 1...32 whose block repeats
+    max(repeats, ceil(24 / period)) times at the tail, else None."""
+    if repeats < 2 or len(tokens) < repeats:
+        return None
+    for period in range(1, 33):
+        count = max(repeats, (24 + period - 1) // period)
+        span = period * count
+        if len(tokens) < span:
+            continue
+        start = len(tokens) - span
+        if all(tokens[start + o] == tokens[start + o % period] for o in range(span)):
+            return period
+    return None

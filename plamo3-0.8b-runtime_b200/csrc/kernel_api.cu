@@ -98,6 +98,17 @@ int plamo_k_linear_tc(const void* w, const uint16_t* x, int rows, int K, int M, 
     return e == cudaSuccess ? 0 : kfail(e);
 }
 
+int plamo_k_select(const uint16_t* logits, int V, const int32_t* history, int n, float penalty, int no_repeat_ngram,
+                   float frequency, float presence, int32_t* counts, uint8_t* flags, uint64_t* key_out, void* stream) {
+    if (!logits || V < 1 || n < 0 || (n > 0 && !history) || !counts || !flags || !key_out) {
+        g_error = "Invalid select arguments";
+        return 1;
+    }
+    cudaError_t e = launch_select(logits, V, history, n, penalty, no_repeat_ngram, frequency, presence, counts, flags,
+                                  reinterpret_cast<unsigned long long*>(key_out), static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? 0 : kfail(e);
+}
+
 int plamo_k_exp(const float* x, float* y, long long n, void* stream) {
     if (!x || !y || n < 1) { g_error = "Invalid exp arguments"; return 1; }
     k_exp<<<unsigned((n + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(x, y, n);

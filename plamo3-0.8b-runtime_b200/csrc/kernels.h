@@ -113,6 +113,13 @@ cudaError_t launch_argmax(const uint16_t* logits, int rows, int n, unsigned long
                           cudaStream_t s);
 cudaError_t launch_packed_decode(const uint8_t* data, const uint32_t* entries, long long count, uint16_t* out,
                                  cudaStream_t s);
+// Sampler.select on the device (sampler.cu): counts [V] ints and flags [V] bytes of scratch, key
+// receives the winning 64-bit argmax key (0: no value above -inf, id 0).
+cudaError_t launch_select(const uint16_t* logits, int V, const int* hist, int n, float penalty, int ngram,
+                          float frequency, float presence, int* counts, uint8_t* flags, unsigned long long* key,
+                          cudaStream_t s);
+int select_key_to_id(unsigned long long key);
+int repetition_period(const int32_t* tokens, int n, int repeats);
 cudaError_t configure_kernels();
 int attention_per_max(int cap, int splits);
 size_t attention_smem(int H, int KV, int per_max);

@@ -132,6 +132,14 @@ struct plamo_runtime {
     cudaGraphExec_t mega_graph = nullptr;
     bool mega_graph_tried = false;
     int* h_error = nullptr;
+    // plamo_select scratch, allocated on first use: counts [V], flags [V], history [sel_cap] ids
+    int* sel_counts = nullptr;
+    uint8_t* sel_flags = nullptr;
+    int* sel_hist = nullptr;
+    int* h_sel_hist = nullptr;
+    unsigned long long* sel_key = nullptr;
+    unsigned long long* h_sel_key = nullptr;
+    int sel_cap = 0;
     std::vector<void*> allocs, host_allocs;
 
     template <typename T>
@@ -1135,6 +1143,38 @@ size_t plamo_weight_bytes(const plamo_runtime* rt) { return rt ? rt->weight_byte
 size_t plamo_device_bytes(const plamo_runtime* rt) { return rt ? rt->device_bytes : 0; }
 const char* plamo_device_name(const plamo_runtime* rt) { return rt ? rt->name.c_str() : ""; }
 double plamo_broadcast_seconds(const plamo_runtime* rt) { return rt ? rt->bcast_seconds : 0; }
+int plamo_select(plamo_runtime* rt, const int32_t* history, int n, float penalty, int no_repeat_ngram, float frequency,
+                 float presence, int32_t* out_id) {
+    if (!rt || !out_id || n < 0 || (n > 0 && !history)) return fail("Invalid select arguments");
+    CK(cudaSetDevice(rt->device));
+    const int V = rt->c.vocab;
+    if (!rt->sel_counts) {
+        if (rt->dalloc(rt->sel_counts, V) || rt->dalloc(rt->sel_flags, V) || rt->dalloc(rt->sel_key, 1) ||
+            rt->halloc(rt->h_sel_key, 1))
+            return 1;
+    }
+    if (n > rt->sel_cap) {  // history buffers grow to the longest history seen (older ones freed at close)
+        const int cap = std::max(n, std::max(rt->sel_cap * 2, rt->context));
+        if (rt->dalloc(rt->sel_hist, cap) || rt->halloc(rt->h_sel_hist, cap)) return 1;
+        rt->sel_cap = cap;
+    }
+    if (n > 0) {
+        std::copy(history, history + n, rt->h_sel_hist);
+        CK(cudaMemcpyAsync(rt->sel_hist, rt->h_sel_hist, sizeof(int) * size_t(n), cudaMemcpyHostToDevice, rt->stream));
+    }
+    CK(launch_select(rt->out.logits, V, rt->sel_hist, n, penalty, no_repeat_ngram, frequency, presence, rt->sel_counts,
+                     rt->sel_flags, rt->sel_key, rt->stream));
+    CK(cudaMemcpyAsync(rt->h_sel_key, rt->sel_key, sizeof(unsigned long long), cudaMemcpyDeviceToHost, rt->stream));
+    const cudaError_t e = cudaStreamSynchronize(rt->stream);
+    if (e != cudaSuccess) return fail(std::string("CUDA execution failed: ") + cudaGetErrorString(e));
+    *out_id = select_key_to_id(*rt->h_sel_key);
+    return 0;
+}
+
+int plamo_repetition_period(const int32_t* tokens, int n, int repeats) {
+    return tokens && n > 0 ? repetition_period(tokens, n, repeats) : 0;
+}
+
 int plamo_set_tensor_gemm(plamo_runtime* rt, int enable) {
     if (!rt) return fail("Invalid runtime");
     rt->tensor = enable != 0;

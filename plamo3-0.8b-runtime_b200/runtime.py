@@ -93,11 +93,16 @@ def library() -> ctypes.CDLL:
         "plamo_persistent_decode": (ctypes.c_int, [_vp]),
         "plamo_trace_decode": (ctypes.c_int, [_vp, _vp, ctypes.c_size_t, _i32p]),
         "plamo_set_tensor_gemm": (ctypes.c_int, [_vp, ctypes.c_int]),
+        "plamo_select": (ctypes.c_int, [_vp, _i32p, ctypes.c_int, ctypes.c_float, ctypes.c_int, ctypes.c_float,
+                                        ctypes.c_float, _i32p]),
+        "plamo_repetition_period": (ctypes.c_int, [_i32p, ctypes.c_int, ctypes.c_int]),
         "plamo_last_error": (ctypes.c_char_p, []),
         # kernel-level entry points (include/plamo_kernels.h)
         "plamo_k_linear": (ctypes.c_int, [_vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp, _vp, _vp]),
         "plamo_k_linear_tc": (ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp, _vp,
                                              ctypes.c_int, _vp, ctypes.c_size_t, _vp]),
+        "plamo_k_select": (ctypes.c_int, [_vp, ctypes.c_int, _vp, ctypes.c_int, ctypes.c_float, ctypes.c_int,
+                                          ctypes.c_float, ctypes.c_float, _vp, _vp, _vp, _vp]),
         "plamo_k_argmax_keys": (ctypes.c_int, [_vp, ctypes.c_int, _vp, _vp]),
         "plamo_k_norm": (ctypes.c_int, [_vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_float, ctypes.c_int, _vp, _vp, _vp]),
         "plamo_k_argmax": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int, _vp, _vp, _vp]),
@@ -220,6 +225,15 @@ class Runtime:
         det = buf[G * (P + 1) * S: need].reshape(G, D).astype(np.int64)
         origin = t[:, -1, 0].min()
         return t - origin, np.where(det > 0, det - origin, -1)
+
+    def select(self, history, penalty: float = 1.0, no_repeat_ngram: int = 0, frequency: float = 0.0,
+               presence: float = 0.0) -> int:
+        """Sampler.select (Sampler.swift:9-31) on the device over the current logits (slot 0)."""
+        arr, ptr = _ids(history)
+        out = ctypes.c_int32(0)
+        _check(library().plamo_select(self._h, ptr, len(arr), float(penalty), int(no_repeat_ngram), float(frequency),
+                                      float(presence), ctypes.byref(out)))
+        return out.value
 
     def set_tensor_gemm(self, enable: bool = True):
         """Projections over >= 16 rows on the tcgen05 tensor-core GEMM (prefill, batched steps):
@@ -357,6 +371,13 @@ class Batch:
         return [(ids[i, :out_lens[i]].tolist(), "stop" if reasons[i] == 0 else "length") for i in range(count.value)]
 
 
+def repetition_period(tokens, repeats: int):
+    """Sampler.repetitionPeriod (Sampler.swift:35-51): the period, or None."""
+    arr, ptr = _ids(tokens)
+    p = library().plamo_repetition_period(ptr, len(arr), int(repeats))
+    return p or None
+
+
 def decode_batch(batch: Batch, prompts, limits, stop_on_truncation: bool = False):
     """Free-function form of BatchDecode.swift:41-47 (Batch.generate)."""
     return batch.generate(prompts, limits, stop_on_truncation)
@@ -373,6 +394,16 @@ def k_linear(w, offsets, x, rows, K, M, mode, y, keys=0, stream=0):
 def k_linear_tc(w, x, rows, K, M, mode, y, keys=0, splits=0, workspace=0, workspace_floats=0, stream=0):
     _check(library().plamo_k_linear_tc(w, x, rows, K, M, mode, y, keys or None, int(splits), workspace or None,
                                        int(workspace_floats), stream or None))
+
+
+def k_select(logits, V, history, n, penalty, no_repeat_ngram, frequency, presence, counts, flags, key_out, stream=0):
+    _check(library().plamo_k_select(logits, V, history or None, n, float(penalty), int(no_repeat_ngram),
+                                    float(frequency), float(presence), counts, flags, key_out, stream or None))
+
+
+def select_key_to_id(key: int) -> int:
+    """The id a plamo_k_select key stands for (0 when no value was above -inf)."""
+    return 0 if key == 0 else 0xFFFFFFFF - (key & 0xFFFFFFFF)
 
 
 def k_argmax_keys(keys, rows, out, stream=0):
