@@ -143,6 +143,21 @@ PLAMO_API int plamo_select(plamo_runtime*, const int32_t* history, int n, float 
  * there is none (the Swift nil) or repeats < 2. Needs no device. */
 PLAMO_API int plamo_repetition_period(const int32_t* tokens, int n, int repeats);
 
+/* Writes model.p12 beside model.safetensors in model_dir: the lossless plamo-bf16-pack-v2 archive
+ * of scripts/pack_weights.py:89-135, byte for byte what that packer writes (every 2-D tensor but
+ * the input embedding block-packed, 1-D tensors raw, safetensors-header order). source_sha256: the
+ * manifest's digest (NULL: the SHA-256 of model.safetensors, which the loader then accepts).
+ * stats (optional, 5 values): original linear bytes, packed linear bytes, archive bytes, packed
+ * blocks, blocks. Returns 0, or 1 with plamo_last_error set ("Packing changed BF16 bits" if a
+ * block fails its round trip). Host code; needs no device. */
+PLAMO_API int plamo_pack_p12(const char* model_dir, const char* source_sha256, uint64_t* stats);
+
+/* The block codec alone (pack_weights.py:19-74): packs count bf16 values (a multiple of 128) into
+ * data (capacity data_cap, at most 2 * count bytes) and one tagged u32 entry per block; data_bytes
+ * receives the bytes used. Host code. */
+PLAMO_API int plamo_pack_blocks(const uint16_t* values, size_t count, uint8_t* data, size_t data_cap, uint32_t* entries,
+                                size_t* data_bytes);
+
 /* Profiling: runs `steps` batch-1 decode steps (as plamo_decode_chain) with every kernel launch
  * bracketed by CUDA events. class_ms[6] / launches[6] receive the summed device milliseconds and
  * launch counts per kernel class: 0 GEMV (projections, lm_head), 1 QK-norm + RoPE + KV append,

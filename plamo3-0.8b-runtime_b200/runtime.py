@@ -96,6 +96,9 @@ def library() -> ctypes.CDLL:
         "plamo_select": (ctypes.c_int, [_vp, _i32p, ctypes.c_int, ctypes.c_float, ctypes.c_int, ctypes.c_float,
                                         ctypes.c_float, _i32p]),
         "plamo_repetition_period": (ctypes.c_int, [_i32p, ctypes.c_int, ctypes.c_int]),
+        "plamo_pack_p12": (ctypes.c_int, [ctypes.c_char_p, ctypes.c_char_p, ctypes.POINTER(ctypes.c_uint64)]),
+        "plamo_pack_blocks": (ctypes.c_int, [_vp, ctypes.c_size_t, _vp, ctypes.c_size_t, _vp,
+                                             ctypes.POINTER(ctypes.c_size_t)]),
         "plamo_last_error": (ctypes.c_char_p, []),
         # kernel-level entry points (include/plamo_kernels.h)
         "plamo_k_linear": (ctypes.c_int, [_vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp, _vp, _vp]),
@@ -376,6 +379,25 @@ def repetition_period(tokens, repeats: int):
     arr, ptr = _ids(tokens)
     p = library().plamo_repetition_period(ptr, len(arr), int(repeats))
     return p or None
+
+
+def pack_p12(model_dir, source_sha256: str | None = None) -> dict:
+    """Writes model_dir/model.p12 with the library's C++ packer (pack_weights.py's archive bytes)."""
+    stats = (ctypes.c_uint64 * 5)()
+    _check(library().plamo_pack_p12(str(model_dir).encode(), source_sha256.encode() if source_sha256 else None, stats))
+    keys = ("original_linear_bytes", "packed_linear_bytes", "archive_bytes", "compressed_blocks", "blocks")
+    return dict(zip(keys, (int(v) for v in stats)))
+
+
+def pack_blocks(values):
+    """C++ block codec: (data uint8, tagged entries uint32) for a flat uint16 array."""
+    v = np.ascontiguousarray(values, dtype=np.uint16).reshape(-1)
+    data = np.empty(2 * v.size, dtype=np.uint8)
+    entries = np.empty(v.size // 128, dtype=np.uint32)
+    used = ctypes.c_size_t(0)
+    _check(library().plamo_pack_blocks(v.ctypes.data, v.size, data.ctypes.data, data.size, entries.ctypes.data,
+                                       ctypes.byref(used)))
+    return data[: used.value], entries
 
 
 def decode_batch(batch: Batch, prompts, limits, stop_on_truncation: bool = False):

@@ -63,3 +63,49 @@ def test_oracle_packed_decode_golden(oracle):
     g = np.load(GOLDEN / "packed_decode.npz")
     out = oracle.packed_decode(g["payload"], g["entries"], g["expected"].size)
     assert np.array_equal(out, g["expected"])
+
+
+def test_cpp_codec_matches_reference_vectors(pkg, vectors):
+    """The library's C++ block codec (plamo_pack_blocks) gives the reference packer's bytes and
+    tagged entries for every golden input."""
+    for name in _names(vectors):
+        data, entries = pkg.runtime.pack_blocks(vectors[f"{name}.values"])
+        assert np.array_equal(data, vectors[f"{name}.data"]), name
+        assert np.array_equal(entries, vectors[f"{name}.entries"]), name
+
+
+def test_cpp_codec_round_trip(pkg):
+    for values in [np.arange(65536, dtype="<u2"), np.zeros(256, dtype="<u2"), np.full(128, 0x8000, dtype="<u2"),
+                   np.tile(np.array([0, 0x8000, 0x3F80, 0xBF80], dtype="<u2"), 64)]:
+        data, entries = pkg.runtime.pack_blocks(values)
+        off, mins = pkg.packing.untag(entries)
+        assert np.array_equal(pkg.packing.unpack(data, off, mins).reshape(-1), values)
+    with pytest.raises(pkg.PlamoError):
+        pkg.runtime.pack_blocks(np.zeros(100, dtype="<u2"))  # not whole blocks
+
+
+def test_cpp_archive_matches_reference_packer(pkg, micro_dir, tmp_path):
+    """plamo_pack_p12 writes the reference main()'s archive byte for byte (pack_weights.py:89-135)."""
+    import shutil
+    for f in ["config.json", "config-mlx.json", "model.safetensors"]:
+        shutil.copy(micro_dir / f, tmp_path / f)
+    stats = pkg.runtime.pack_p12(tmp_path)
+    ref = (micro_dir / "model.p12").read_bytes()
+    assert (tmp_path / "model.p12").read_bytes() == ref
+    assert stats["archive_bytes"] == len(ref) and 0 < stats["compressed_blocks"] <= stats["blocks"]
+    assert not (tmp_path / "model.p12.part").exists()
+
+
+def test_cpp_archive_matches_python_writer(pkg, tiny_dir, tmp_path):
+    import shutil
+    for f in ["config.json", "config-mlx.json", "model.safetensors"]:
+        if (tiny_dir / f).exists():
+            shutil.copy(tiny_dir / f, tmp_path / f)
+    pkg.runtime.pack_p12(tmp_path, source_sha256="ab" * 32)
+    py = tmp_path / "py"
+    py.mkdir()
+    shutil.copy(tiny_dir / "model.safetensors", py / "model.safetensors")
+    pkg.packing.write_p12(py, source_sha="ab" * 32)
+    assert (tmp_path / "model.p12").read_bytes() == (py / "model.p12").read_bytes()
+    with pytest.raises(pkg.PlamoError):
+        pkg.runtime.pack_p12(tmp_path / "missing")
