@@ -152,6 +152,12 @@ PLAMO_API int plamo_repetition_period(const int32_t* tokens, int n, int repeats)
  * block fails its round trip). Host code; needs no device. */
 PLAMO_API int plamo_pack_p12(const char* model_dir, const char* source_sha256, uint64_t* stats);
 
+/* The loader's check of one tensor's .p12 block table (Packed.swift:63-89): entry i's offset is
+ * the running end of the blocks before it (192 bytes packed, 256 raw by the entry's tag), every
+ * block fits in the data_bytes data region, and the chain ends exactly there. 1 when valid, else 0.
+ * Host code; plamo_open applies it to every packed tensor. */
+PLAMO_API int plamo_p12_chain_valid(const uint32_t* entries, size_t count, size_t data_bytes);
+
 /* The block codec alone (pack_weights.py:19-74): packs count bf16 values (a multiple of 128) into
  * data (capacity data_cap, at most 2 * count bytes) and one tagged u32 entry per block; data_bytes
  * receives the bytes used. Host code. */

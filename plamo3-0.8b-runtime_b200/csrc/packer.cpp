@@ -122,6 +122,10 @@ std::string span_json(std::pair<size_t, size_t> s) {
 
 extern "C" {
 
+int plamo_p12_chain_valid(const uint32_t* entries, size_t count, size_t data_bytes) {
+    return (entries || count == 0) && plamo::validate_chain(entries, count, data_bytes) ? 1 : 0;
+}
+
 int plamo_pack_blocks(const uint16_t* values, size_t count, uint8_t* data, size_t data_cap, uint32_t* entries,
                       size_t* data_bytes) {
     if (!values || !data || !entries || !data_bytes || count % BLOCK) {

@@ -97,6 +97,7 @@ def library() -> ctypes.CDLL:
                                         ctypes.c_float, _i32p]),
         "plamo_repetition_period": (ctypes.c_int, [_i32p, ctypes.c_int, ctypes.c_int]),
         "plamo_pack_p12": (ctypes.c_int, [ctypes.c_char_p, ctypes.c_char_p, ctypes.POINTER(ctypes.c_uint64)]),
+        "plamo_p12_chain_valid": (ctypes.c_int, [_vp, ctypes.c_size_t, ctypes.c_size_t]),
         "plamo_pack_blocks": (ctypes.c_int, [_vp, ctypes.c_size_t, _vp, ctypes.c_size_t, _vp,
                                              ctypes.POINTER(ctypes.c_size_t)]),
         "plamo_last_error": (ctypes.c_char_p, []),
@@ -387,6 +388,12 @@ def pack_p12(model_dir, source_sha256: str | None = None) -> dict:
     _check(library().plamo_pack_p12(str(model_dir).encode(), source_sha256.encode() if source_sha256 else None, stats))
     keys = ("original_linear_bytes", "packed_linear_bytes", "archive_bytes", "compressed_blocks", "blocks")
     return dict(zip(keys, (int(v) for v in stats)))
+
+
+def p12_chain_valid(entries, data_bytes: int) -> bool:
+    """The loader's block-table check (Packed.swift:63-89) for one tensor."""
+    e = np.ascontiguousarray(entries, dtype=np.uint32)
+    return bool(library().plamo_p12_chain_valid(e.ctypes.data if e.size else None, e.size, int(data_bytes)))
 
 
 def pack_blocks(values):

@@ -109,3 +109,40 @@ def test_cpp_archive_matches_python_writer(pkg, tiny_dir, tmp_path):
     assert (tmp_path / "model.p12").read_bytes() == (py / "model.p12").read_bytes()
     with pytest.raises(pkg.PlamoError):
         pkg.runtime.pack_p12(tmp_path / "missing")
+
+
+def _chain_rule(entries, nbytes):
+    """The validity rule of PackedFormatTests.swift:45-53, restated."""
+    end = 0
+    for entry in entries:
+        offset = int(entry) & ~63
+        size = 256 if int(entry) & 63 == 0 else 192
+        if offset != end or offset > nbytes - size:
+            return False
+        end = offset + size
+    return end == nbytes
+
+
+def test_loader_chain_fuzz(pkg):
+    """PackedFormatTests.swift:43-72: chains of 0..19 blocks (raw, tag 1, tag 63), every data size
+    around the true end, and every entry with bits flipped; the loader's check agrees with the
+    rule each time."""
+    valid = pkg.runtime.p12_chain_valid
+    checked = 0
+    for count in range(20):
+        entries, end = [], 0
+        for i in range(count):
+            tag = 0 if i % 3 == 0 else (1 if i % 3 == 1 else 63)
+            entries.append(end | tag)
+            end += 256 if tag == 0 else 192
+        cases = [(entries, end)] + [(entries, b) for b in (0, max(0, end - 1), end + 1, end + 64)]
+        for i in range(len(entries)):
+            for change in (1, 63, 64, 256, 0xFFFFFFFF):
+                bad = list(entries)
+                bad[i] ^= change
+                cases.append((bad, end))
+        for e, nbytes in cases:
+            assert valid(e, nbytes) == _chain_rule(e, nbytes), (count, e, nbytes)
+            checked += 1
+    assert valid([], 0) and not valid([], 64)
+    assert checked > 900
