@@ -26,7 +26,7 @@ from HBM; the 1.45 GB of weights are far larger than the 126 MB L2, so no flush 
          ranks), with its algorithmic FLOPs against the measured dense bf16 tensor peak.
 
 --impl reference runs the reference arm: the reference (Swift + Metal) cannot run on Linux, so its
-CPU path is the restatement in oracle/ (see DESIGN.md), timed on the host cores.
+CPU path is the restatement in oracle/, timed on the host cores.
 """
 from __future__ import annotations
 

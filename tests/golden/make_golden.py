@@ -1,8 +1,8 @@
 """Generates the golden fixtures in tests/golden from the reference's own code.
 
-Run in a container where the reference checkout is mounted (default /root/reference, or
-$PLAMO_REFERENCE). The reference packer (scripts/pack_weights.py) is pure numpy; importing it
-pulls in `from reference import MODEL`, whose module imports `mlx.core`, so mlx is stubbed.
+Run where the reference checkout is available, with $PLAMO_REFERENCE pointing at it. The
+reference packer (scripts/pack_weights.py) is pure numpy; importing it pulls in
+`from reference import MODEL`, whose module imports `mlx.core`, so mlx is stubbed.
 
 Fixtures:
   packer_vectors.npz  reference pack()/tag() outputs for pack_weights.self_test's bit patterns
@@ -31,10 +31,12 @@ import numpy as np
 
 HERE = Path(__file__).resolve().parent
 REPO = HERE.parents[1]
-REFERENCE = Path(os.environ.get("PLAMO_REFERENCE", "/root/reference"))
+REFERENCE = Path(os.environ["PLAMO_REFERENCE"]) if os.environ.get("PLAMO_REFERENCE") else None
 
 
 def load_reference_packer():
+    if REFERENCE is None:
+        raise SystemExit("set PLAMO_REFERENCE to the reference checkout")
     mlx = types.ModuleType("mlx")
     core = types.ModuleType("mlx.core")
     mlx.core = core
