@@ -139,3 +139,15 @@ def test_tiny_batch_matches_scalar(oracle, tiny_dir):
             assert out[lane] == nxt[lane]
             assert np.array_equal(batch.logits_bits(lane), logits[lane])
             assert np.array_equal(batch.hidden_state(lane).view(np.uint32), hid[lane].view(np.uint32))
+
+
+def test_noise_floor_twins(oracle, micro_dir):
+    """The restatement's two twins (sums reordered; each dot product summed exactly and rounded
+    once) run on the micro model and report finite, non-negative drift; the tensor-mode tests
+    measure against them."""
+    import numpy as np
+    prompt = [1] + [(7 * i) % 200 + 2 for i in range(11)]
+    for mode in ("reverse", "exact"):
+        f = oracle.noise_floor(micro_dir, 64, prompt, 2, mode=mode)
+        assert set(f) == {"rmse", "maxabs", "rmse_mean"}
+        assert all(np.isfinite(v) and v >= 0 for v in f.values()), (mode, f)
