@@ -42,6 +42,8 @@ from pathlib import Path
 
 REPO = Path(__file__).resolve().parent
 PROMPT = 512
+# the synthetic checkpoint's .p12 archive is bound to the safetensors file beside it (opt-in)
+os.environ.setdefault("PLAMO_P12_LOCAL_SOURCE", "1")
 
 
 def _load(name, path, package=False):

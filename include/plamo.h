@@ -28,7 +28,9 @@ typedef struct plamo_batch plamo_batch;
 
 /* Runtime.init(directory:context:packed:) — Runtime.swift:164-286.
  * Loads <model_dir>/config.json, config-mlx.json and model.safetensors (+ model.p12 when packed),
- * validates them (Runtime.swift:181-189, :33-101; Packed.swift:12-91) and makes the weights
+ * validates them (Runtime.swift:181-189, :33-101; Packed.swift:12-91; an archive must name the
+ * reference checkpoint's digest, or with PLAMO_P12_LOCAL_SOURCE=1 the model.safetensors beside it)
+ * and makes the weights
  * resident on CUDA device `device`. context: 1...32768. */
 PLAMO_API int plamo_open(const char* model_dir, int context, int packed, int device, plamo_runtime** out);
 
@@ -118,6 +120,15 @@ PLAMO_API int plamo_step_launches(plamo_runtime*);
  * sm_100a; PLAMO_PERSISTENT=0 in the environment selects the multi-kernel graph instead). */
 PLAMO_API int plamo_persistent_decode(const plamo_runtime*);
 
+/* Failure-path check of the persistent decode kernel (no reference counterpart; the reference's
+ * command buffers report errors through their status, Runtime.swift:462): runs the kernel's bounded
+ * poll on a device word that nothing ever sets, with a limit of limit_ns (1 us ... 2 s) instead of
+ * the 2 s every decode wait uses. The poll gives up, raises the kernel's error word, and the call
+ * fails exactly as a timed-out decode step does ("decode step aborted: a bounded device wait timed
+ * out (code 12)"); afterwards the runtime is usable and its next steps are exact. Needs the
+ * persistent kernel (plamo_persistent_decode). */
+PLAMO_API int plamo_debug_wait_timeout(plamo_runtime*, unsigned long long limit_ns);
+
 /* Dense contractions on the tensor cores: with enable != 0, every projection over 16 or more rows
  * of raw bf16 weights (prefill calls, batched steps and batched prefill of this runtime and its
  * batches) runs as a tcgen05 GEMM with fp32 accumulation. The results then match the default path
@@ -146,7 +157,9 @@ PLAMO_API int plamo_repetition_period(const int32_t* tokens, int n, int repeats)
 /* Writes model.p12 beside model.safetensors in model_dir: the lossless plamo-bf16-pack-v2 archive
  * of scripts/pack_weights.py:89-135, byte for byte what that packer writes (every 2-D tensor but
  * the input embedding block-packed, 1-D tensors raw, safetensors-header order). source_sha256: the
- * manifest's digest (NULL: the SHA-256 of model.safetensors, which the loader then accepts).
+ * manifest's digest (NULL: the SHA-256 of model.safetensors, which the loader accepts only when
+ * PLAMO_P12_LOCAL_SOURCE=1 is set in the environment; by default it accepts the reference
+ * checkpoint's digest alone, as Packed.swift:35 does).
  * stats (optional, 5 values): original linear bytes, packed linear bytes, archive bytes, packed
  * blocks, blocks. Returns 0, or 1 with plamo_last_error set ("Packing changed BF16 bits" if a
  * block fails its round trip). Host code; needs no device. */

@@ -82,7 +82,9 @@ PLAMO_API int plamo_k_attention(const uint16_t* q, const uint16_t* keys, const u
  * its scratch. Same arguments and results as plamo_k_attention. The partial results live in one
  * fixed 2 MiB device array per device (splits x heads at most 4032; larger requests fail with an
  * error and launch nothing). The first call on a device looks the array up (cudaGetSymbolAddress,
- * with that device current): make it before any stream capture. Calls are asynchronous on
+ * with that device current): make it before any stream capture. The address is kept for the life
+ * of the process, so a device reset (cudaDeviceReset) in between invalidates it: do not call this
+ * entry point on a device after resetting that device. Calls are asynchronous on
  * `stream` (they return once enqueued) and all calls on a device share the array, which keeps the
  * last call's contents: calls whose execution may overlap (other streams, other threads) race. */
 PLAMO_API int plamo_k_attention_static(const uint16_t* q, const uint16_t* keys, const uint16_t* values, int heads,

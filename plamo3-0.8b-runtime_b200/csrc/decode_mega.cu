@@ -138,11 +138,11 @@ struct Spin {
     uint64_t t0 = 0;
     uint32_t i = 0;
 };
-__device__ __forceinline__ bool spin_more(Spin& s, int* error, int code) {
+__device__ __forceinline__ bool spin_more(Spin& s, int* error, int code, uint64_t limit_ns = WAIT_NS) {
     if (s.i++ == 0) s.t0 = gtime();
     if ((s.i & 15u) == 0) {
         if (*reinterpret_cast<volatile int*>(error)) return false;
-        if (gtime() - s.t0 > WAIT_NS) {
+        if (gtime() - s.t0 > limit_ns) {
             atomicCAS(error, 0, code);
             return false;
         }
@@ -1279,6 +1279,23 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_decode_mega(MegaArgs a) {
     *a.ticket = 0u;
     *a.step = step + 1u;
     __threadfence();
+}
+
+// The persistent kernel's bounded poll on a word that nothing sets, with a caller-chosen limit: the
+// failure path of every exchange wait (the poll gives up, raises `error` with ERR_DATA and returns)
+// made to run on purpose, for the host's recovery test. One warp polls, as wait_hints does.
+__global__ void k_wait_unset(const uint32_t* word, int* error, unsigned long long limit_ns) {
+    Spin s;
+    for (;;) {
+        const bool set = ld_tag(word) != 0u;
+        if (__all_sync(FULL_MASK, set)) return;
+        if (!__all_sync(FULL_MASK, spin_more(s, error, ERR_DATA, limit_ns))) return;
+    }
+}
+
+cudaError_t launch_wait_unset(const uint32_t* word, int* error, unsigned long long limit_ns, cudaStream_t s) {
+    k_wait_unset<<<1, 32, 0, s>>>(word, error, limit_ns);
+    return cudaGetLastError();
 }
 
 static const void* mega_kernel(bool packed, int npt) {

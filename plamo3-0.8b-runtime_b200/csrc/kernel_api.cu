@@ -209,6 +209,8 @@ int plamo_k_attention(const uint16_t* q, const uint16_t* keys, const uint16_t* v
 // Fixed device scratch of plamo_k_attention_static: a file-scope device array (every device has
 // its own instance), found once per device with cudaGetSymbolAddress, shared by all calls on the
 // device. Layout: RowDesc at 0, RowGeo at 64, partial outputs at 256, then the (max, sum) pairs.
+// The looked-up address stays valid while the device's primary context lives; a cudaDeviceReset
+// would reload the module elsewhere, which is why the header rules out calls after a reset.
 constexpr size_t STATIC_ATTN_BYTES = size_t(2) << 20;
 static __device__ __align__(256) unsigned char g_attn_static[STATIC_ATTN_BYTES];
 static void* g_attn_static_ptr[64];

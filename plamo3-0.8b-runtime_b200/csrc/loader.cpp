@@ -5,6 +5,8 @@
 //   .p12 manifest and chain   Packed.swift:12-91 (format from scripts/pack_weights.py)
 #include "loader.h"
 
+#include <cstdlib>
+
 #include <fcntl.h>
 #include <sys/mman.h>
 #include <sys/stat.h>
@@ -366,9 +368,13 @@ bool ModelFiles::load(const std::string& dir, bool packed, std::string& err) {
         size_t(payload) != p12.size - p12_data_start || !tensors || tensors->type != Json::OBJ) {
         err = incompatible; return false;
     }
-    // The reference binds an archive to the original checkpoint's digest (Packed.swift:35). Archives
-    // of other checkpoints (the seeded synthetic ones) are bound to the safetensors file beside them.
-    if (sha->str != kReferenceSourceSha && sha->str != sha256_hex(st.data, st.size)) { err = incompatible; return false; }
+    // The reference binds an archive to the original checkpoint's digest (Packed.swift:35) and so
+    // does this loader by default. With PLAMO_P12_LOCAL_SOURCE=1 in the environment it also accepts
+    // an archive bound to the safetensors file beside it (the seeded synthetic checkpoints of the
+    // tests and benchmarks); an archive of another checkpoint is still refused.
+    const char* local = getenv("PLAMO_P12_LOCAL_SOURCE");
+    const bool local_ok = local && local[0] == '1' && sha->str == sha256_hex(st.data, st.size);
+    if (sha->str != kReferenceSourceSha && !local_ok) { err = incompatible; return false; }
     p12_payload = size_t(payload);
     for (const auto& kv : tensors->obj) {
         TensorRef t;

@@ -84,5 +84,7 @@ int mega_npt(int d);
 cudaError_t configure_mega(size_t smem, bool packed, int npt);
 int mega_occupancy(size_t smem, bool packed, int npt);
 cudaError_t launch_mega(const MegaArgs& a, int grid, size_t smem, cudaStream_t s);
+// One bounded poll of `word` (which nothing sets) that gives up after limit_ns and raises `error`.
+cudaError_t launch_wait_unset(const uint32_t* word, int* error, unsigned long long limit_ns, cudaStream_t s);
 
 }  // namespace plamo

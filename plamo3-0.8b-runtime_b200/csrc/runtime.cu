@@ -25,6 +25,7 @@
 #include <mutex>
 #include <set>
 #include <string>
+#include <utility>
 #include <vector>
 
 namespace plamo {
@@ -131,7 +132,9 @@ struct plamo_runtime {
     size_t mega_smem = 0;
     cudaGraphExec_t mega_graph = nullptr;
     bool mega_graph_tried = false;
+    std::vector<std::pair<void*, size_t>> mega_words;  // tagged exchange buffers (pointer, bytes)
     int* h_error = nullptr;
+    uint32_t* unset_word = nullptr;  // plamo_debug_wait_timeout: a word nothing writes (zero)
     // plamo_select scratch, allocated on first use: counts [V], flags [V], history [sel_cap] ids
     int* sel_counts = nullptr;
     uint8_t* sel_flags = nullptr;
@@ -534,12 +537,20 @@ static int setup_mega(plamo_runtime& rt) {
     a.ids = rt.work.ids;
     a.desc = rt.work.desc;
     // tagged buffers start at zero: tag 0 is never current
+    rt.mega_words = {{(void*)nullptr, size_t(c.qkv_rows()) * 4}, {nullptr, size_t(c.q_dim()) * 4}, {nullptr, size_t(c.d) * 4},
+                     {nullptr, size_t(c.d) * 4}, {nullptr, size_t(c.ffn) * 4},
+                     {nullptr, size_t(splits_max) * c.heads * 128 * 8}, {nullptr, size_t(splits_max) * c.heads * 2 * 8},
+                     {nullptr, (size_t(4) * sms + c.heads + size_t(splits_max) * ((c.heads + MEGA_HG - 1) / MEGA_HG)) * 4}};
     if (rt.dalloc(a.qkv, c.qkv_rows()) || rt.dalloc(a.att, c.q_dim()) ||
         rt.dalloc(a.po, c.d) || rt.dalloc(a.pd, c.d) || rt.dalloc(a.act, c.ffn) ||
         rt.dalloc(a.part_o, size_t(splits_max) * c.heads * 128) || rt.dalloc(a.part_ml, size_t(splits_max) * c.heads * 2) ||
         rt.dalloc(a.hints, size_t(4) * sms + c.heads + size_t(splits_max) * ((c.heads + MEGA_HG - 1) / MEGA_HG)) ||
         rt.dalloc(a.step, 1) || rt.dalloc(a.ticket, 1) || rt.dalloc(a.error, 1) || rt.halloc(rt.h_error, 1))
         return 1;
+    {
+        void* ptrs[8] = {a.qkv, a.att, a.po, a.pd, a.act, a.part_o, a.part_ml, a.hints};
+        for (int i = 0; i < 8; i++) rt.mega_words[i].first = ptrs[i];
+    }
     a.logits = rt.out.logits;
     a.hidden = rt.out.hidden;
     a.amkey = rt.out.keys;
@@ -583,6 +594,18 @@ static int decode_step(plamo_runtime& rt) {
     return 0;
 }
 
+// Clears every tagged exchange word of the persistent kernel (tag 0 is never current). Tags repeat
+// after 65535 / (L + 1) steps, and a consumer takes any word whose tag is current: a word that is
+// read is normally rewritten in the same step, so a repeat cannot be mistaken for fresh data. Two
+// cases break that rule, and both clear the words: an aborted step (some words of that step were
+// never written) and a reset (the key splits of a shorter history go unused and become active
+// again later, holding words of steps long past).
+static int mega_clear_exchange(plamo_runtime& rt) {
+    if (!rt.mega) return 0;
+    for (const auto& w : rt.mega_words) CK(cudaMemsetAsync(w.first, 0, w.second, rt.stream));
+    return 0;
+}
+
 // After a synchronised persistent-kernel step: a bounded device wait that timed out aborts the
 // call with an error (and re-arms the counters), it never hangs the stream.
 static int mega_check(plamo_runtime& rt) {
@@ -592,7 +615,9 @@ static int mega_check(plamo_runtime& rt) {
     cudaMemset(rt.margs.error, 0, sizeof(int));
     cudaMemset(rt.margs.ticket, 0, sizeof(unsigned));
     cudaMemset(rt.margs.amkey, 0, sizeof(unsigned long long));
-    // the aborted step left some exchange words unwritten: move every tag past it
+    // the aborted step left some exchange words unwritten: clear them and move every tag past it
+    mega_clear_exchange(rt);
+    cudaStreamSynchronize(rt.stream);
     unsigned step = 0;
     cudaMemcpy(&step, rt.margs.step, sizeof(unsigned), cudaMemcpyDeviceToHost);
     step += 1u;
@@ -1017,6 +1042,24 @@ int plamo_step_launches(plamo_runtime* rt) {
 
 int plamo_persistent_decode(const plamo_runtime* rt) { return rt && rt->mega ? 1 : 0; }
 
+// Failure path of the persistent kernel's bounded waits, run on purpose: one poll of a device word
+// that nothing sets gives up after limit_ns, raises the kernel's error word, and the call fails
+// the way an aborted decode step does (mega_check: message, re-armed counters, cleared exchange
+// words, tags moved on). The runtime stays usable.
+int plamo_debug_wait_timeout(plamo_runtime* rt, unsigned long long limit_ns) {
+    if (!rt) return fail("Invalid runtime");
+    if (!rt->mega) return fail("The persistent decode kernel is not active");
+    if (limit_ns < 1000ull || limit_ns > 2000000000ull) return fail("Wait limit must be 1 us ... 2 s");
+    CK(cudaSetDevice(rt->device));
+    if (!rt->unset_word && rt->dalloc(rt->unset_word, 1)) return 1;
+    CK(launch_wait_unset(rt->unset_word, rt->margs.error, limit_ns, rt->stream));
+    CK(cudaMemcpyAsync(rt->h_error, rt->margs.error, sizeof(int), cudaMemcpyDeviceToHost, rt->stream));
+    const cudaError_t e = cudaStreamSynchronize(rt->stream);
+    if (e != cudaSuccess) return fail(std::string("CUDA execution failed: ") + cudaGetErrorString(e));
+    if (mega_check(*rt)) return 1;
+    return fail("The bounded wait did not time out");
+}
+
 // One device-chained decode step of the persistent kernel with its phase timeline recorded
 // (launched directly, outside the captured graph, with the trace pointer set).
 int plamo_trace_decode(plamo_runtime* rt, uint64_t* out, size_t cap, int32_t* shape) {
@@ -1135,6 +1178,7 @@ int plamo_hidden(plamo_runtime* rt, float* out) {
 void plamo_reset(plamo_runtime* rt) {
     if (!rt) return;
     rt->position = 0; rt->gpu_seconds = 0; rt->last_rows = 0;  // Runtime.swift:319
+    if (rt->mega && cudaSetDevice(rt->device) == cudaSuccess) mega_clear_exchange(*rt);
 }
 
 int plamo_position(const plamo_runtime* rt) { return rt ? rt->position : 0; }

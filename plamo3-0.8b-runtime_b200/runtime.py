@@ -91,6 +91,7 @@ def library() -> ctypes.CDLL:
         "plamo_step_launches": (ctypes.c_int, [_vp]),
         "plamo_profile_decode": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.POINTER(ctypes.c_double), _i32p]),
         "plamo_persistent_decode": (ctypes.c_int, [_vp]),
+        "plamo_debug_wait_timeout": (ctypes.c_int, [_vp, ctypes.c_ulonglong]),
         "plamo_trace_decode": (ctypes.c_int, [_vp, _vp, ctypes.c_size_t, _i32p]),
         "plamo_set_tensor_gemm": (ctypes.c_int, [_vp, ctypes.c_int]),
         "plamo_select": (ctypes.c_int, [_vp, _i32p, ctypes.c_int, ctypes.c_float, ctypes.c_int, ctypes.c_float,
@@ -247,6 +248,11 @@ class Runtime:
     @property
     def persistent(self) -> bool:
         return bool(library().plamo_persistent_decode(self._h))
+
+    def debug_wait_timeout(self, limit_ns: int = 20_000):
+        """Runs the persistent kernel's bounded poll on a device word nothing sets, with a short
+        limit: raises PlamoError with the timed-out decode step's message; the runtime stays usable."""
+        _check(library().plamo_debug_wait_timeout(self._h, int(limit_ns)))
 
     def logits(self, slot: int = 0) -> np.ndarray:
         out = np.empty(self.vocab, dtype=np.float32)

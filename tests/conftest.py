@@ -12,6 +12,10 @@ REPO = Path(__file__).resolve().parents[1]
 PKG_DIR = REPO / "plamo3-0.8b-runtime_b200"
 GOLDEN = REPO / "tests" / "golden"
 
+# The seeded test checkpoints' .p12 archives are bound to the safetensors file beside them, which
+# the loader accepts only when asked to (by default it accepts the reference checkpoint's digest).
+os.environ.setdefault("PLAMO_P12_LOCAL_SOURCE", "1")
+
 
 def load_package():
     if "plamo_b200" in sys.modules:

@@ -103,6 +103,16 @@ def test_tiny_packed_equals_raw(cuda, pkg, tiny_dir):
     assert packed.weight_bytes < raw.weight_bytes
 
 
+def test_p12_bound_to_reference_digest_by_default(cuda, pkg, tiny_dir, monkeypatch):
+    """Packed.swift:35-38: an archive whose source digest is not the reference checkpoint's is
+    refused unless PLAMO_P12_LOCAL_SOURCE=1 accepts one bound to the safetensors file beside it."""
+    monkeypatch.delenv("PLAMO_P12_LOCAL_SOURCE", raising=False)
+    with pytest.raises(pkg.PlamoError, match="Incompatible packed archive"):
+        pkg.Runtime(tiny_dir, context=64, packed=True)
+    monkeypatch.setenv("PLAMO_P12_LOCAL_SOURCE", "1")
+    pkg.Runtime(tiny_dir, context=64, packed=True).close()
+
+
 def test_decode_chain_equals_forward_loop(cuda, pkg, tiny_dir):
     rt = pkg.Runtime(tiny_dir, context=200)
     prompt = pkg.synthetic.seeded_tokens(30, rt.vocab, seed=3)
@@ -163,6 +173,32 @@ def test_persistent_long_context_multi_tile(cuda, pkg, tiny_dir, monkeypatch):
         mk, mv = mega.debug_kv(layer)
         gk, gv = multi.debug_kv(layer)
         assert np.array_equal(mk, gk) and np.array_equal(mv, gv), layer
+
+
+def test_bounded_wait_timeout_fails_the_call_and_recovers(cuda, pkg, tiny_dir):
+    """The failure path of the persistent kernel's bounded waits (Runtime.swift:462 throws on a
+    failed command buffer): a device poll on a word that nothing sets gives up after 20 us instead
+    of hanging, the call fails with the decode step's timeout message, and the runtime's later
+    steps are bit-identical to those of a runtime that never failed."""
+    import time
+    rt = pkg.Runtime(tiny_dir, context=200)
+    twin = pkg.Runtime(tiny_dir, context=200)
+    assert rt.persistent and twin.persistent
+    prompt = pkg.synthetic.seeded_tokens(30, rt.vocab, seed=6)
+    a, b = rt.prefill(prompt), twin.prefill(prompt)
+    for _ in range(4):
+        a, b = rt.forward([a]), twin.forward([b])
+    for _ in range(2):
+        t0 = time.perf_counter()
+        with pytest.raises(pkg.PlamoError, match="bounded device wait timed out"):
+            rt.debug_wait_timeout(20_000)
+        assert time.perf_counter() - t0 < 1.0
+    assert rt.position == twin.position
+    for step in range(24):
+        assert a == b, step
+        assert np.array_equal(rt.logits().view(np.uint32), twin.logits().view(np.uint32)), step
+        a, b = rt.forward([a]), twin.forward([b])
+    assert rt.decode_chain(16) == twin.decode_chain(16)
 
 
 def test_reset_and_errors(cuda, pkg, tiny_dir):

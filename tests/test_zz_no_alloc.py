@@ -1,6 +1,10 @@
 """plamo_k_attention_static (fixed device scratch, no allocation) against plamo_k_attention on the
 same inputs: two calls in a row through the C ABI, the first with more splits than the second, so
-the second runs on scratch that still holds the first call's partials."""
+the second runs on scratch that still holds the first call's partials. Callers that reserved their
+device memory up front (a serving loop that must not hit an out-of-memory error or a cudaFree's
+device-wide wait mid-stream) rely on the entry point allocating nothing: after a warm-up call, the
+device's free memory must not change across a call with more splits than any before it, and the
+entry point must work on a non-default stream synchronised alone."""
 import numpy as np
 import pytest
 
@@ -45,6 +49,22 @@ def test_static_scratch_attention_matches_allocating_entry_point(pkg, oracle):
         assert np.isfinite(g).all()
         # the same kernels on the same inputs: identical bits (well inside the 2e-3 attention tolerance)
         assert np.array_equal(g.view(np.uint32), r.view(np.uint32)), (count, splits)
+    # no allocation: free device memory is unchanged across a call that needs more scratch than any
+    # call before it (the allocating entry point would grow its buffer here); the call runs on a
+    # non-default stream and only that stream is synchronised
+    args = _case(oracle, torch, keep, 32768, True, 13)
+    ref = torch.zeros(16 * 128, dtype=torch.int16, device="cuda")
+    got = torch.full((16 * 128,), -1, dtype=torch.int16, device="cuda")
+    side = torch.cuda.Stream()
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info()
+    rt.k_attention_static(*args, 240, got.data_ptr(), stream=side.cuda_stream)
+    side.synchronize()
+    free1, _ = torch.cuda.mem_get_info()
+    assert free1 == free0, (free0, free1)
+    rt.k_attention(*args, 240, ref.data_ptr())
+    torch.cuda.synchronize()
+    assert np.array_equal(got.cpu().numpy(), ref.cpu().numpy())
     with pytest.raises(pkg.PlamoError, match="static 2 MiB buffer"):
         rt.k_attention_static(*args, 4096, got.data_ptr())
     torch.cuda.synchronize()
