@@ -246,6 +246,27 @@ def prefill_flop(tokens: int, layers: int = 16, window: int = 2048, linear_param
     return 2.0 * (linear_params - head_params) * tokens + 8192.0 * attn + 2.0 * head_params
 
 
+def kv_read_bytes(p: int, layers: int = 16, window: int = 2048, pattern: int = 8) -> int:
+    """K+V bytes a decode row at position p reads (512 per visible key and layer: one KV head of
+    128 bf16 keys and values); local layers see min(p + 1, window) keys, global ones p + 1."""
+    n_global = layers // pattern
+    return 512 * ((layers - n_global) * min(p + 1, window) + n_global * (p + 1))
+
+
+def decode_row_bytes(p: int) -> int:
+    """Per-row bytes of a decode step beyond the shared weights (SURVEY 8(d) formula): KV reads at
+    position p, the 16 layers' KV writes, the embedding row and the bf16 logits."""
+    return kv_read_bytes(p) + 16 * 512 + 3072 + 215_040
+
+
+NORM_BYTES = 207_872  # every norm vector read once per step
+
+
+def decode_step_bytes(weight_bytes: int, positions) -> int:
+    """Algorithmic HBM bytes of one decode step over rows at `positions` (one weight pass)."""
+    return weight_bytes + NORM_BYTES + sum(decode_row_bytes(p) for p in positions)
+
+
 def workload_config(args):
     return {"workload": "BASELINE config 2: reference-dims PLaMo-3 0.8B (d1536 L16 H16/KV1 F6144 V107520), "
                         f"{PROMPT}-token seeded prompt, prefill then greedy bs1 decode"
@@ -293,6 +314,116 @@ def kernel_case(args):
     return 0
 
 
+def measure_batch4(P, model, local, dist, args, pk, wbytes):
+    """four independent 512-token segments (seeds 2000 + lane) prefilled
+    together, then 2,048 batched greedy steps each, so every lane's 2,064-slot local ring wraps
+    (Batch.swift:109-179, the --batch4 mode). Device time of the steps (CUDA events per call),
+    wall time of the whole call sequence beside it; HBM roofline of the batched step."""
+    import torch
+    lanes, steps = 4, args.batch4_steps
+    rt = P.Runtime(model, context=PROMPT + steps + 8, device=local)
+    b = P.Batch(rt, lanes=lanes)
+    prompts = [P.synthetic.seeded_tokens(PROMPT, rt.vocab, seed=2000 + lane) for lane in range(lanes)]
+    p0 = b.gpu_seconds
+    nxt = b.prefill(prompts)
+    prefill_s = b.gpu_seconds - p0
+    if dist: dist.barrier()
+    torch.cuda.synchronize()
+    g0, w0 = b.gpu_seconds, time.perf_counter()
+    for _ in range(steps):
+        nxt = b.step(nxt)
+    wall = time.perf_counter() - w0
+    dev = b.gpu_seconds - g0
+    b.close()
+    rt.close()
+    t = torch.tensor([dev, wall, prefill_s], device="cuda", dtype=torch.float64)
+    if dist: dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    dev, wall, prefill_s = (float(x) for x in t.tolist())
+    nbytes = sum(decode_step_bytes(wbytes, [PROMPT + i] * lanes) for i in range(steps))
+    return dict(lanes=lanes, prompt_tokens=PROMPT, steps=steps, ring_wraps=PROMPT + steps > 2064,
+                decode_tok_s=lanes * steps / dev, step_ms=1e3 * dev / steps,
+                e2e_tok_s=lanes * steps / wall, prefill_ms=1e3 * prefill_s,
+                hbm_frac=nbytes / dev / 1e9 / pk["hbm"],
+                path="order-exact CUDA-core projections (bit-identical to the restatement); one weight pass per step")
+
+
+def measure_long(P, model, local, dist, args, pk, wbytes):
+    """BASELINE config 5a: one 28,672-token prompt in a 32,768-token context (global layers keep
+    the full history; split-K flash-decode), prefilled on the order-exact path and on the tcgen05
+    path (device time), then greedy decode of the remaining 4,096 - 1 tokens device-chained on the
+    persistent kernel: tok/s and the HBM roofline including the growing KV reads."""
+    import torch
+    prompt_len, context = args.long_prompt, 32768
+    rt = P.Runtime(model, context=context, device=local)
+    prompt = P.synthetic.seeded_tokens(prompt_len, rt.vocab, seed=5)
+    out = dict(prompt_tokens=prompt_len, context=context, flop=prefill_flop(prompt_len))
+    for mode in ("tensor", "exact"):  # the decode below continues from the order-exact prefill
+        rt.set_tensor_gemm(mode == "tensor")
+        rt.reset()
+        if dist: dist.barrier()
+        g0 = rt.gpu_seconds
+        rt.prefill(prompt)
+        t_s = rt.gpu_seconds - g0
+        tt = torch.tensor([t_s], device="cuda", dtype=torch.float64)
+        if dist: dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        t_s = float(tt.item())
+        out["prefill_" + mode] = dict(ms=1e3 * t_s, tok_s=prompt_len / t_s, tflops=out["flop"] / t_s / 1e12,
+                                      tensor_frac=out["flop"] / t_s / 1e12 / pk["bf16"])
+    steps = context - prompt_len - 1
+    if dist: dist.barrier()
+    g0 = rt.gpu_seconds
+    rt.decode_chain(steps)
+    dev = rt.gpu_seconds - g0
+    tt = torch.tensor([dev], device="cuda", dtype=torch.float64)
+    if dist: dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+    dev = float(tt.item())
+    rt.close()
+    nbytes = sum(decode_step_bytes(wbytes, [prompt_len + i]) for i in range(steps))
+    out["decode"] = dict(steps=steps, positions=[prompt_len, prompt_len + steps - 1], tok_s=steps / dev,
+                         ms_per_token=1e3 * dev / steps, gb_per_token=nbytes / steps / 1e9,
+                         hbm_frac=nbytes / dev / 1e9 / pk["hbm"])
+    return out
+
+
+def measure_segment_job(P, model, local, rank, world, dist, args, pk, wbytes):
+    """BASELINE config 5b, the whole fixed job: 256 independent 512-token segments (segment k seeded
+    1000 + k) partitioned into contiguous blocks over the ranks (no exchange), each rank running
+    waves of 32 lanes: batched prefill of the wave, then 512 batched greedy steps. Device time of
+    the rank's whole job (prefill + steps), max over ranks, so the rate is strong-scaled: the same
+    256 x 512 tokens whatever the GPU count. Roofline: sum of the waves' prefill FLOP at the bf16
+    peak plus their decode-step bytes at the HBM peak, over the measured time."""
+    import torch
+    total, lanes, steps = args.job_segments, args.segment_lanes, args.job_steps
+    mine = list(segment_block(rank, world, total))
+    rt = P.Runtime(model, context=PROMPT + steps + 8, device=local)
+    b = P.Batch(rt, lanes=lanes)
+    roof_s, waves, dev = 0.0, 0, 0.0
+    prompts = {k: P.synthetic.seeded_tokens(PROMPT, rt.vocab, seed=segment_seed(k)) for k in mine}
+    if dist: dist.barrier()
+    torch.cuda.synchronize()
+    for w0 in range(0, len(mine), lanes):
+        wave = mine[w0:w0 + lanes]
+        b.reset()
+        nxt = b.prefill([prompts[k] for k in wave])  # the batch's device clock restarts here
+        for _ in range(steps - 1):
+            nxt = b.step(nxt)
+        dev += b.gpu_seconds
+        waves += 1
+        roof_s += len(wave) * prefill_flop(PROMPT) / (pk["bf16"] * 1e12)
+        roof_s += sum(decode_step_bytes(wbytes, [PROMPT + i] * len(wave)) for i in range(steps - 1)) / (pk["hbm"] * 1e9)
+    b.close()
+    rt.close()
+    t = torch.tensor([dev, roof_s], device="cuda", dtype=torch.float64)
+    if dist: dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    dev_max, roof_max = (float(x) for x in t.tolist())
+    return dict(segments=total, segments_per_gpu=len(mine), lanes=lanes, waves_per_gpu=waves,
+                prompt_tokens=PROMPT, new_tokens=steps, job_s=dev_max,
+                segment_tok_s=total * steps / dev_max, total_tok_s=total * (PROMPT + steps) / dev_max,
+                roofline_frac=roof_max / dev_max, scaling="strong (fixed 256-segment job)",
+                path="order-exact CUDA-core projections (bit-identical to the restatement); tokens = greedy "
+                     "tokens generated (the first comes from the prefill)")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -308,6 +439,10 @@ def main():
     ap.add_argument("--segment-lanes", type=int, default=32)
     ap.add_argument("--segment-steps", type=int, default=32)
     ap.add_argument("--prefill-reps", type=int, default=5)
+    ap.add_argument("--batch4-steps", type=int, default=2048, help="config 4 decode steps per lane (0: skip)")
+    ap.add_argument("--long-prompt", type=int, default=28672, help="config 5a prompt tokens (0: skip)")
+    ap.add_argument("--job-segments", type=int, default=256, help="config 5b segments in the fixed job (0: skip)")
+    ap.add_argument("--job-steps", type=int, default=512, help="config 5b greedy tokens per segment")
     ap.add_argument("--kernel-case", default=None,
                     help="rows,K,M,mode: time one projection on the tcgen05 GEMM and the exact GEMM, then exit")
     args = ap.parse_args()
@@ -394,6 +529,7 @@ def main():
         dist.all_reduce(e2e_t, op=dist.ReduceOp.MAX)
     e2e_elapsed = float(e2e_t.item())
     bcast = rt.broadcast_seconds
+    rt_arena_bytes = rt.weight_bytes
     rt.close()
 
     # ---- aggregate segment throughput (BASELINE config 5b shape): independent 512-token segments
@@ -466,6 +602,10 @@ def main():
                        "last-row lm_head; tensor_frac against the measured bf16 burst peak")
         prt.close()
 
+    job = measure_segment_job(P, model, local, rank, world, dist, args, pk, wbytes) if args.job_segments > 0 else None
+    b4 = measure_batch4(P, model, local, dist, args, pk, wbytes) if args.batch4_steps > 0 else None
+    long_ctx = measure_long(P, model, local, dist, args, pk, wbytes) if args.long_prompt > 0 else None
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(model, prompt, args.cpu_budget, 64)
@@ -492,12 +632,20 @@ def main():
             line["cpu_baseline"] = cpu
         if world > 1:
             line["weight_broadcast_s"] = bcast
+            arena = rt_arena_bytes
+            line["weight_broadcast_gbs"] = arena / bcast / 1e9 if bcast > 0 else None
         if seg:
             line["segments"] = seg
         if seg_tc:
             line["segments_tensor"] = seg_tc
         if pre:
             line["prefill"] = pre
+        if job:
+            line["segments_job"] = job
+        if b4:
+            line["batch4"] = b4
+        if long_ctx:
+            line["long"] = long_ctx
         print(json.dumps(line), flush=True)
     if dist:
         dist.barrier()

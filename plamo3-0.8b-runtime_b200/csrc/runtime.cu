@@ -829,6 +829,13 @@ static int open_common(const char* model_dir, int context, int packed, int devic
             if (e) rc = fail(std::string("ncclCommInitRank failed: ") + (api.err ? api.err(e) : "?"));
         }
         if (!rc) {
+            // a first small broadcast sets up the communicator's channels (lazily, on first use),
+            // so the timed one measures the weight transfer alone
+            int e = api.bcast(rt->arena, rt->arena, 256, /*ncclUint8*/ 1, 0, comm, rt->stream);
+            if (e) rc = fail(std::string("ncclBroadcast failed: ") + (api.err ? api.err(e) : "?"));
+            if (!rc && cudaStreamSynchronize(rt->stream) != cudaSuccess) rc = fail("weight broadcast failed");
+        }
+        if (!rc) {
             auto t0 = std::chrono::steady_clock::now();
             int e = api.bcast(rt->arena, rt->arena, rt->arena_bytes, /*ncclUint8*/ 1, 0, comm, rt->stream);
             if (e) rc = fail(std::string("ncclBroadcast failed: ") + (api.err ? api.err(e) : "?"));

@@ -87,3 +87,13 @@ def micro_dir():
 def reference_dir(models_root):
     """Full reference-dims synthetic model (1.78 GB on disk, plus the .p12 archive)."""
     return _model_dir(models_root, "reference", load_package().synthetic.REFERENCE, packed=True)
+
+
+@pytest.fixture(scope="session")
+def example_dir(models_root):
+    """BASELINE.json's example dims per layer (d 2048, 16 q-heads over 4 KV heads, FFN 5632, vocab
+    80000) in 2 layers with a 32-key window, so grouped-query attention runs with rings that wrap."""
+    s = load_package().synthetic
+    cfg = s.ModelConfig(hidden_size=2048, num_hidden_layers=2, num_attention_heads=16, num_key_value_heads=4,
+                        intermediate_size=5632, vocab_size=80000, window_size=32, sliding_window_pattern=2)
+    return _model_dir(models_root, "example_gqa", cfg, packed=True)

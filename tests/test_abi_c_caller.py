@@ -26,3 +26,18 @@ def test_c_caller_compiles_and_runs(pkg, micro_dir, tmp_path, lang):
     r = subprocess.run([str(exe), str(micro_dir)], capture_output=True, text=True, timeout=120)
     assert r.returncode == 0, r.stderr + r.stdout
     assert "abi_caller: ok" in r.stdout
+
+
+def test_swift_module_shim_compiles_as_c(tmp_path):
+    """The SwiftPM C module (swift/Sources/CPlamo) imports the public headers through shim.h; with
+    no Swift toolchain here, the header set it exposes is compiled as C11."""
+    cc = shutil.which("gcc")
+    if not cc:
+        pytest.skip("no host compiler")
+    shim = REPO / "plamo3-0.8b-runtime_b200" / "swift" / "Sources" / "CPlamo" / "shim.h"
+    src = tmp_path / "use_shim.c"
+    src.write_text(f'#include "{shim}"\nint main(void) {{ return plamo_position(0); }}\n')
+    subprocess.run([cc, "-std=c11", "-pedantic", "-Wall", "-Werror", "-fsyntax-only", str(src)], check=True,
+                   capture_output=True, text=True)
+    modulemap = (shim.parent / "module.modulemap").read_text()
+    assert 'header "shim.h"' in modulemap and 'link "plamo_cuda"' in modulemap

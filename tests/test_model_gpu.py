@@ -103,6 +103,27 @@ def test_tiny_packed_equals_raw(cuda, pkg, tiny_dir):
     assert packed.weight_bytes < raw.weight_bytes
 
 
+def test_gqa_example_dims_match_oracle(cuda, pkg, oracle, example_dir):
+    """Grouped-query attention (4 KV heads, 4 query heads each) at BASELINE's example dims: the
+    multi-kernel path (hidden 2048 is outside the persistent kernel's plan) bit for bit against the
+    restatement through a prefill that crosses the window and decode steps that wrap the rings,
+    raw and .p12, with every KV cache compared at the end."""
+    rt = pkg.Runtime(example_dir, context=160)
+    assert not rt.persistent and rt.kv_heads == 4
+    ora = oracle.OracleRuntime(example_dir, context=160)
+    prompt = pkg.synthetic.seeded_tokens(45, rt.vocab, seed=8)
+    stats, ids = compare(rt, ora, prompt, 40)
+    check_bitwise(stats)
+    for layer in range(rt.layers):
+        gk, gv = rt.debug_kv(layer)
+        ok, ov = ora.kv(layer)
+        assert np.array_equal(gk, ok) and np.array_equal(gv, ov), layer
+    packed = pkg.Runtime(example_dir, context=160, packed=True)
+    got = [packed.prefill(prompt)] + [packed.forward([i]) for i in ids[:-1]]
+    assert got == ids
+    assert np.array_equal(packed.logits().view(np.uint32), rt.logits().view(np.uint32))
+
+
 def test_p12_bound_to_reference_digest_by_default(cuda, pkg, tiny_dir, monkeypatch):
     """Packed.swift:35-38: an archive whose source digest is not the reference checkpoint's is
     refused unless PLAMO_P12_LOCAL_SOURCE=1 accepts one bound to the safetensors file beside it."""

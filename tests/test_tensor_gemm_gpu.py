@@ -223,3 +223,44 @@ def test_tensor_mode_reference_dims_prefill(cuda, pkg, oracle, reference_dir):
     stats = compare_gap(rt, ora, prompt, 4)
     del ora
     check_noise(stats, floor_of(oracle, reference_dir, 1024, prompt, 4))
+
+
+@pytest.mark.slow
+def test_tensor_mode_layer0_cache_against_float64(cuda, pkg, oracle, reference_dir):
+    """The tcgen05 path's contract at the model level, element by element: after the 512-token
+    prompt prefilled on the tensor cores at the reference dims, layer 0's value cache holds
+    bf16(h . W_v) for every row, where h is the pre-mixer norm of the embedding rows (no earlier
+    tensor-core result feeds it). Against that product in float64 every cached value must lie
+    within one bf16 ulp and nearly all must be identical, so a wrong row, lane or tile mapping of
+    the qkv GEMM (or its epilogue) fails here, although the logits downstream are only held to the
+    accumulation-order drift. The key cache (QK-norm of the same GEMM's key rows, stored
+    unrotated) is held to the bound after its extra roundings (Kernels.metal:223-259)."""
+    prompt = np.array(pkg.synthetic.seeded_tokens(512, 107520, seed=1))
+    rt = pkg.Runtime(reference_dir, context=1024)
+    rt.set_tensor_gemm(True)
+    rt.prefill(list(prompt))
+    gk, gv = rt.debug_kv(0)
+    model = oracle.Model(reference_dir)
+    t = model.tensors
+    emb = oracle.bf16_to_f32(t["model.embed_tokens.weight"][prompt])
+    h, _ = oracle.norm(t["model.layers.layers.0.pre_mixer_norm.weight"], emb, 1.0)
+    w = oracle.bf16_to_f32(t["model.layers.layers.0.mixer.qkv_proj.weight"])
+    exact = h.astype(np.float64) @ w.astype(np.float64).T  # [512, 2304]
+    rounded = oracle.bf16_to_f32(oracle.f32_to_bf16(exact.astype(np.float32)))
+
+    def ulps(got_bits, ref):
+        got = oracle.bf16_to_f32(got_bits)
+        ulp = np.exp2(np.floor(np.log2(np.maximum(np.abs(ref), 1e-30))) - 7)
+        return np.abs(got.astype(np.float64) - ref) / ulp
+
+    v_ref = rounded[:, 2176:2304]
+    v_got = gv.reshape(-1, 128)[:512]
+    same_v = float(np.mean(oracle.bf16_to_f32(v_got) == v_ref))
+    assert ulps(v_got, exact[:, 2176:2304]).max() <= 1.0 + 1e-9, ulps(v_got, exact[:, 2176:2304]).max()
+    assert same_v >= 0.995, same_v
+    # keys: per-row RMSNorm with k_norm + 1 of the bf16 GEMM rows (layer 0 is local: unrotated)
+    k_ref, _ = oracle.norm(t["model.layers.layers.0.mixer.k_norm.weight"], rounded[:, 2048:2176].astype(np.float32), 1.0)
+    k_got = oracle.bf16_to_f32(gk.reshape(-1, 128)[:512])
+    same_k = float(np.mean(k_got == k_ref))
+    assert ulps(gk.reshape(-1, 128)[:512], k_ref.astype(np.float64)).max() <= 2.0 + 1e-9
+    assert same_k >= 0.99, same_k
