@@ -344,12 +344,15 @@ __global__ void __launch_bounds__(128) k_qkv(QkvArgs a) {
 // local softmax statistics and the unnormalised P.V partial; k_attn_merge combines the splits
 // (log-sum-exp) and rounds to bf16 (Kernels.metal:440-562).
 constexpr int QS = 132;
-constexpr int AT = 64;  // keys per staged K / V tile
+// Keys per staged K / V tile: 64 with one KV head; with grouped-query attention a tile holds every
+// KV head of its keys, so fewer keys keep the fp32 rotated tile and the bf16 staging in shared memory.
+__host__ __device__ constexpr int attn_tile_keys(int KV) { return KV == 1 ? 64 : KV == 2 ? 32 : 16; }
 
 int attention_per_max(int cap, int splits) { return ((cap + splits - 1) / splits + 31) & ~31; }
 size_t attention_smem(int H, int KV, int per_max) {
-    return sizeof(float) * (size_t(H) * QS + size_t(AT) * (KV * 128 + 1) + size_t(AT) * 64 + size_t(H) * per_max) +
-           2 * size_t(AT) * KV * 128 * 2;  // key / value staging, and the first value tile fetched early
+    const size_t AT = size_t(attn_tile_keys(KV));
+    return sizeof(float) * (size_t(H) * QS + AT * (KV * 128 + 1) + AT * 64 + size_t(H) * per_max) +
+           2 * AT * KV * 128 * 2;  // key / value staging, and the first value tile fetched early
 }
 
 // Stages rows [k0, k0 + tk) of the key (or value) cache window into shared memory as raw bf16 with
@@ -380,6 +383,7 @@ __device__ __forceinline__ void stage_rows_async(uint4* dst, const uint16_t* bas
     asm volatile("cp.async.commit_group;" ::: "memory");
 }
 
+template <int AT>
 __global__ void __launch_bounds__(256) k_attn_partial(AttnArgs a) {
     extern __shared__ __align__(16) float smem[];
     const int r = blockIdx.y, s = blockIdx.x, t = threadIdx.x;
@@ -433,7 +437,7 @@ __global__ void __launch_bounds__(256) k_attn_partial(AttnArgs a) {
         __syncthreads();
         const int j = t & (AT - 1);
         if (j < tk) {
-            for (int h = t >> 6; h < H; h += 4) {
+            for (int h = t / AT; h < H; h += 256 / AT) {
                 const float* qh = qs + h * QS;
                 const float* kj = kr + j * KS + (h / group) * 128;
                 float acc = 0.f;
@@ -665,7 +669,11 @@ cudaError_t configure_kernels() {
     PLAMO_ATTR(1) PLAMO_ATTR(2) PLAMO_ATTR(4) PLAMO_ATTR(8) PLAMO_ATTR(16)
 #undef PLAMO_ATTR
     if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(k_attn_partial, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        e = cudaFuncSetAttribute(k_attn_partial<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(k_attn_partial<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(k_attn_partial<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     if (e == cudaSuccess) e = configure_gemm();
     if (e == cudaSuccess) e = configure_gemm_tc();
     return e;
@@ -695,7 +703,12 @@ cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s) {
     if (a.H > 32 || a.H % a.KV) return cudaErrorInvalidValue;
     const size_t smem = attention_smem(a.H, a.KV, a.per_max);
     if (smem > 200 * 1024) return cudaErrorInvalidValue;
-    k_attn_partial<<<dim3(a.splits, a.rows), 256, smem, s>>>(a);
+    const dim3 grid(a.splits, a.rows);
+    switch (attn_tile_keys(a.KV)) {
+        case 64: k_attn_partial<64><<<grid, 256, smem, s>>>(a); break;
+        case 32: k_attn_partial<32><<<grid, 256, smem, s>>>(a); break;
+        default: k_attn_partial<16><<<grid, 256, smem, s>>>(a); break;
+    }
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     k_attn_merge<<<a.rows * a.H, 128, 0, s>>>(a);

@@ -42,6 +42,8 @@ struct MegaArgs {
     bool phases_packed;     // weights are .p12 tensors
     int attn_per_max;       // largest split width over the layers (shared-memory layout)
     int splits_max;         // largest split count over the layers
+    int direct;             // consumers poll the tagged data words themselves instead of the producers' hints first
+    int l2_prefetch;        // bit 0: gate/up rows, bit 1: down_proj rows, bulk-prefetched into L2 at the attention phase
     int xs_bytes;           // staged activations at the start of the work region
     int tbl_bytes;          // .p12: shared copy of one phase's block-table rows of a CTA
     int* ids;          // [1] input token (device-chained: written by the previous step)

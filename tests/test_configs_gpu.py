@@ -89,9 +89,8 @@ def test_c5a_long_context_32k(cuda, pkg, oracle, micro_dir, monkeypatch):
         assert np.array_equal(bits(mega.logits()), lo), step
         assert np.array_equal(bits(multi.logits()), lo), step
         assert a == o and b == o, step
-        if step < checked:
-            o = ora.forward([o])
-            a, b = mega.forward([o]), multi.forward([o])
+        if step < checked:  # every side consumes the restatement's id (teacher forcing)
+            a, b, o = mega.forward([o]), multi.forward([o]), ora.forward([o])
     del ora
     # to the end of the context: device-chained greedy decode on both paths
     rest = context - mega.position - 1

@@ -248,19 +248,25 @@ def test_tensor_mode_layer0_cache_against_float64(cuda, pkg, oracle, reference_d
     exact = h.astype(np.float64) @ w.astype(np.float64).T  # [512, 2304]
     rounded = oracle.bf16_to_f32(oracle.f32_to_bf16(exact.astype(np.float32)))
 
-    def ulps(got_bits, ref):
-        got = oracle.bf16_to_f32(got_bits)
+    def excess(got_bits, ref, n_ulps, slack):
+        """How far each cached value lies outside n_ulps bf16 ulps of `ref` plus an absolute
+        slack for results that cancel (their fp32 accumulation error is absolute, not relative);
+        > 0 flags an element. A mis-mapped row or lane is off by O(1)."""
+        got = oracle.bf16_to_f32(got_bits).astype(np.float64)
         ulp = np.exp2(np.floor(np.log2(np.maximum(np.abs(ref), 1e-30))) - 7)
-        return np.abs(got.astype(np.float64) - ref) / ulp
+        return np.abs(got - ref) - (n_ulps * ulp + slack)
 
     v_ref = rounded[:, 2176:2304]
     v_got = gv.reshape(-1, 128)[:512]
     same_v = float(np.mean(oracle.bf16_to_f32(v_got) == v_ref))
-    assert ulps(v_got, exact[:, 2176:2304]).max() <= 1.0 + 1e-9, ulps(v_got, exact[:, 2176:2304]).max()
+    ev = excess(v_got, exact[:, 2176:2304], 1.0, 1e-4)
+    assert ev.max() <= 0, (np.unravel_index(ev.argmax(), ev.shape), float(ev.max()))
     assert same_v >= 0.995, same_v
     # keys: per-row RMSNorm with k_norm + 1 of the bf16 GEMM rows (layer 0 is local: unrotated)
     k_ref, _ = oracle.norm(t["model.layers.layers.0.mixer.k_norm.weight"], rounded[:, 2048:2176].astype(np.float32), 1.0)
     k_got = oracle.bf16_to_f32(gk.reshape(-1, 128)[:512])
     same_k = float(np.mean(k_got == k_ref))
-    assert ulps(gk.reshape(-1, 128)[:512], k_ref.astype(np.float64)).max() <= 2.0 + 1e-9
+    ek = excess(gk.reshape(-1, 128)[:512], k_ref.astype(np.float64), 2.0, 1e-3)
+    assert ek.max() <= 0, (np.unravel_index(ek.argmax(), ek.shape), float(ek.max()))
     assert same_k >= 0.99, same_k
+    print(f"layer-0 cache: values identical {same_v:.5f}, keys identical {same_k:.5f}")
