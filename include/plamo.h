@@ -188,7 +188,9 @@ PLAMO_API int plamo_profile_decode(plamo_runtime*, int steps, double* class_ms, 
  * kernel with its device timeline recorded. shape = {CTAs, phases, 3, D}; out receives, per CTA, per
  * phase, the %globaltimer nanoseconds at [wait begin, work begin, work end], then one record per CTA
  * [step begin, head epilogue begin, step end] — CTAs x (phases + 1) x 3 entries — followed by D
- * stamps per CTA inside its first attention split of layer 0 (0 where unused); cap must hold
+ * stamps per CTA (0 where unused): [0, 5) inside its first attention split of layer 0, then for
+ * layer 1's QKV, o_proj, gate/up and down_proj phases (k = 0..3) six stamps at 8 + 6k: entry,
+ * producers' hints seen, input gathered, prologue done, chunk loop done, outputs stored; cap must hold
  * CTAs x ((phases + 1) x 3 + D) entries. Phases per layer: QKV, attention, o_proj, gate/up (SwiGLU),
  * down_proj; then the lm_head. */
 PLAMO_API int plamo_trace_decode(plamo_runtime*, uint64_t* out, size_t cap, int32_t* shape);

@@ -78,10 +78,6 @@ __device__ __forceinline__ void cp_async4(void* dst, const void* src) {
 }
 __device__ __forceinline__ void cp_async_wait_but_newest() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
-// bulk prefetch of [src, src + bytes) into L2 (no shared-memory destination, no completion)
-__device__ __forceinline__ void prefetch_l2(const void* src, uint32_t bytes) {
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
-}
 // orders this thread's earlier generic-proxy accesses before its next bulk copies (async proxy)
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async;" ::: "memory"); }
 
@@ -746,7 +742,7 @@ __device__ __forceinline__ bool attention_task(const MegaArgs& a, const MegaLaye
     }
     // every CTA's q/k/v rows are in (their hints); the group's query rows and, for the split that
     // holds this step's key, the key and value rows are read once into shared memory
-    bool ok = a.direct ? true : wait_hints(a.hints, gridDim.x, 1, tag, a.error);
+    bool ok = wait_hints(a.hints, gridDim.x, 1, tag, a.error);
     if (!ok) return false;
     ok = gather16<false>(sm.qkvs, a.qkv + h0 * 128, nq * 128, tag, a.error);
     if (owner && ok) ok = gather16<false>(sm.qkvs + MEGA_HG * 128, a.qkv + H * 128, 256, tag, a.error);
@@ -913,7 +909,7 @@ __device__ __forceinline__ bool attention_merge(const MegaArgs& a, int S, int h,
     const int t = threadIdx.x, H = a.H, d = t & 127;
     const int ngroups = (H + MEGA_HG - 1) / MEGA_HG;
     // the head's tasks (s, h / 4) for s < S
-    if (!a.direct && !wait_hints(a.hints + 4 * gridDim.x + H + h / MEGA_HG, S, ngroups, tag, a.error)) return false;
+    if (!wait_hints(a.hints + 4 * gridDim.x + H + h / MEGA_HG, S, ngroups, tag, a.error)) return false;
     float* pbuf = reinterpret_cast<float*>(sm.kraw);  // [MERGE_CHUNK][128] in kraw
     float* mxy = reinterpret_cast<float*>(sm.kr);      // [S][2] split (max, sum)
     float* mw = mxy + 2 * S;
@@ -1049,23 +1045,6 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_decode_mega(MegaArgs a) {
         const int l = ph.layer;
         if (trace) trace[p * MEGA_TRACE_STAMPS] = gtime();
         if (ph.kind == MK_ATT) {
-            // HBM is idle while attention and the o_proj exchange run (o_proj's weights are already
-            // in flight in registers): this CTA's gate/up and down_proj rows of the layer go into L2
-            // now, so those phases stream from L2 (raw weights; each CTA's rows are contiguous)
-            if (!PACKED && a.l2_prefetch && t == 32) {
-                for (int k = p + 1; k < a.nphases && k <= p + 3; k++) {
-                    const MegaPhase& q = phases[k];
-                    const bool want = (q.kind == MK_GU && (a.l2_prefetch & 1)) || (q.kind == MK_DOWN && (a.l2_prefetch & 2));
-                    if (!want) continue;
-                    const PhaseWork w = phase_work(q, cta, G);
-                    const size_t rb = size_t(w.K) * 2;
-                    for (int half = 0; half < (w.up ? 2 : 1); half++) {
-                        const uint8_t* base = w.w + size_t(w.u0 + half * w.up) * rb;
-                        const size_t n = size_t(w.nu) * rb;
-                        for (size_t o = 0; o < n; o += 32768) prefetch_l2(base + o, uint32_t(n - o < 32768 ? n - o : 32768));
-                    }
-                }
-            }
             const MegaLayer Ly = layers[l];
             const uint32_t tag = tag_of(l);
             const int S = active_splits(a, Ly, dsc0);
@@ -1131,7 +1110,7 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_decode_mega(MegaArgs a) {
                 // down_proj before the next layer and the head), as its tagged words land
                 const uint32_t* pin = ph.kind == MK_GU ? a.po : a.pd;
                 const uint32_t itag = tag_of(ph.kind == MK_HEAD ? a.L - 1 : (ph.kind == MK_GU ? l : l - 1));
-                if (!a.direct && !wait_hints(a.hints + (ph.kind == MK_GU ? 1 : 3) * G, G, 1, itag, a.error)) { ok = false; break; }
+                if (!wait_hints(a.hints + (ph.kind == MK_GU ? 1 : 3) * G, G, 1, itag, a.error)) { ok = false; break; }
                 if (wd) wd[1] = gtime();
                 load_norm<NPT>(nbuf, off1, d, w1);
                 load_norm<NPT>(nbuf + a.dpad, 1.0f, d, w2);
@@ -1170,9 +1149,8 @@ __global__ void __launch_bounds__(MEGA_THREADS, 1) k_decode_mega(MegaArgs a) {
         } else {
             // o_proj reads the merged attention rows, down_proj the SwiGLU activations
             if (pw.nchunk > 0) {
-                ok = a.direct ? true
-                     : ph.kind == MK_O ? wait_hints(a.hints + 4 * G, a.H, 1, tag, a.error)
-                                       : wait_hints(a.hints + 2 * G, G, 1, tag, a.error);
+                ok = ph.kind == MK_O ? wait_hints(a.hints + 4 * G, a.H, 1, tag, a.error)
+                                     : wait_hints(a.hints + 2 * G, G, 1, tag, a.error);
                 if (wd) wd[1] = gtime();
                 if (ok) ok = gather16<true>(xs, ph.kind == MK_O ? a.att : a.act, ph.lin.K, tag, a.error);
             }

@@ -42,8 +42,6 @@ struct MegaArgs {
     bool phases_packed;     // weights are .p12 tensors
     int attn_per_max;       // largest split width over the layers (shared-memory layout)
     int splits_max;         // largest split count over the layers
-    int direct;             // consumers poll the tagged data words themselves instead of the producers' hints first
-    int l2_prefetch;        // bit 0: gate/up rows, bit 1: down_proj rows, bulk-prefetched into L2 at the attention phase
     int xs_bytes;           // staged activations at the start of the work region
     int tbl_bytes;          // .p12: shared copy of one phase's block-table rows of a CTA
     int* ids;          // [1] input token (device-chained: written by the previous step)
@@ -69,7 +67,8 @@ struct MegaArgs {
     int* error;        // set to a non-zero code when a bounded wait times out
     // Optional timeline (null when off): per CTA, per phase, %globaltimer ns at [wait begin, work
     // begin, work end], then one record [step begin, head epilogue begin, step end], then
-    // after all CTAs' records, MEGA_TRACE_DETAIL stamps per CTA of its first attention task of layer 0.
+    // after all CTAs' records, MEGA_TRACE_DETAIL stamps per CTA: its first attention task of layer 0
+    // at [0, 5), layer 1's weight phases (QKV, o_proj, gate/up, down_proj) six each from index 8.
     unsigned long long* trace;
 };
 constexpr int MEGA_TRACE_STAMPS = 3;

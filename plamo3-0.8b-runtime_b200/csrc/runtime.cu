@@ -532,12 +532,6 @@ static int setup_mega(plamo_runtime& rt) {
     a.phases_packed = rt.packed;
     a.attn_per_max = per_max;
     a.splits_max = splits_max;
-    {
-        const char* pf = getenv("PLAMO_MEGA_L2");
-        a.l2_prefetch = pf ? atoi(pf) : 0;
-        const char* dr = getenv("PLAMO_MEGA_DIRECT");
-        a.direct = dr ? atoi(dr) : 0;
-    }
     a.xs_bytes = int(mega_xs_bytes(kmax));
     a.tbl_bytes = tbl_bytes;
     a.ids = rt.work.ids;
