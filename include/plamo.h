@@ -129,12 +129,14 @@ PLAMO_API int plamo_persistent_decode(const plamo_runtime*);
  * persistent kernel (plamo_persistent_decode). */
 PLAMO_API int plamo_debug_wait_timeout(plamo_runtime*, unsigned long long limit_ns);
 
-/* Dense contractions on the tensor cores: with enable != 0, every projection over 16 or more rows
- * of raw bf16 weights (prefill calls, batched steps and batched prefill of this runtime and its
- * batches) runs as a tcgen05 GEMM with fp32 accumulation. The results then match the default path
- * within the rounding of the accumulation order (next-token logits within RMSE 1e-2 and max |diff|
- * 5e-2, the tolerance of the reference's verify scripts), not bit for bit; batch-1 decode and
- * .p12 weights are unaffected. Off by default. Returns 0, or 1 for a null handle. */
+/* Dense contractions on the tensor cores ("tensor mode"), a bit mask. Bit 0: every projection over
+ * 16 or more rows of raw bf16 weights (prefill calls, batched steps and batched prefill of this
+ * runtime and its batches) runs as a tcgen05 GEMM with fp32 accumulation. Bit 1: the attention of
+ * every call over 16 or more rows (prefill chunks) runs its scores and P.V as tcgen05 MMAs (16
+ * query heads over one KV head; other shapes keep the CUDA-core kernel). 3 selects both. The
+ * results then match the default path within the rounding of the accumulation order (next-token
+ * logits within the drift the reference's own reordered sums show), not bit for bit; batch-1
+ * decode and .p12 weights are unaffected. Off (0) by default. Returns 0, or 1 for a null handle. */
 PLAMO_API int plamo_set_tensor_gemm(plamo_runtime*, int enable);
 
 /* Sampler.select (Sampler.swift:9-31) on the device, over the logits of slot 0 as

@@ -75,6 +75,20 @@ PLAMO_API int plamo_k_attention(const uint16_t* q, const uint16_t* keys, const u
                       int cap, int first, int count, int begin, int end, int full, const uint32_t* rope_local,
                       int splits, uint16_t* out, void* stream);
 
+/* Attention of `rows` query rows over one cache (the prefill form of the split-K attention above,
+ * Kernels.metal:301-562): q is [rows][heads*128] bf16 (already rotated); geo is a DEVICE array of
+ * [rows][4] int32 {first, count, begin, end} per row as in plamo_k_attention (keys r in [0,count)
+ * at slot (first + r) % cap, the row sees r in [begin, end)). tensor == 0: the CUDA-core kernels
+ * with `splits` key partitions (bit-identical to the runtime's default path); tensor != 0: the
+ * tcgen05 kernel of tensor mode (16 query heads over one KV head, splits chosen by the library),
+ * within rounding of the former. Rows of one 16-token chunk should be consecutive; rows with
+ * different windows are handled, at a lower rate. `workspace` (device, 256-byte aligned) holds the
+ * row descriptors and split partials; a call that finds it too small fails with the bytes needed. */
+PLAMO_API int plamo_k_attention_rows(const uint16_t* q, const uint16_t* keys, const uint16_t* values, int heads,
+                                     int kv_heads, int cap, const int32_t* geo, int rows, int full,
+                                     const uint32_t* rope_local, int splits, int tensor, uint16_t* out, void* workspace,
+                                     size_t workspace_bytes, void* stream);
+
 /* plamo_k_attention without any device allocation. No counterpart in the reference (whose Metal
  * encoder owns its buffers); for callers that must not allocate device memory during a call, such
  * as a serving loop that reserved its memory up front and can afford neither an out-of-memory

@@ -1,0 +1,341 @@
+// Prefill attention on the tensor cores (tensor mode): the split-K decomposition of
+// k_attn_partial + k_attn_merge (kernels.cu, Kernels.metal:301-562), with the scores and P.V of a
+// split as tcgen05 MMAs instead of one CUDA-core pass per query row.
+//
+// A CTA takes 8 query tokens of one forward call and one key split (up to ATC_SPAN keys of the
+// window). With one KV head (MQA) the 8 tokens x 16 heads are 128 MMA rows that share every key:
+// row r = token * 16 + head, one tensor-memory lane each. Per 256-key chunk of the split:
+//   - the chunk's keys are staged in shared memory (local layers re-rotated with the window-relative
+//     RoPE coordinates, Kernels.metal:277-285) and the values transposed, both in the K-major
+//     128-byte-swizzle layout that the MMA's shared-memory descriptors read;
+//   - S = Q.K^T for up to 4 tiles of 64 keys (M 128, N 64, K 128) lands in tensor memory;
+//   - each thread owns one row: it reads its scores (tcgen05.ld), applies the window / causal mask,
+//     updates the running max (rescaling its O row in tensor memory when the max grows) and writes
+//     P = exp(score - max) as a bf16 hi/lo pair, so P keeps 16 significant bits like the
+//     reference's fp32 softmax output (Kernels.metal:400-437), not bf16's 8;
+//   - O += P_hi.V + P_lo.V (M 128, N 128, K 64 per tile) accumulates in tensor memory.
+// At the end each row stores its split's (max, sum) and unnormalised O in the layout k_attn_merge
+// reads, and that merge runs unchanged.
+//
+// The results follow the tensor core's summation order and P's 16-bit split, so they match the
+// order-exact path within rounding, not bit for bit; the runtime uses this kernel only in tensor
+// mode. Every mbarrier wait is bounded (2 s) and reports through the tiled-GEMM error word.
+#include "common.cuh"
+#include "kernels.h"
+#include "mbarrier.cuh"
+#include "tcgen05.cuh"
+
+namespace plamo {
+
+namespace {
+
+constexpr int ATC_TOK = 8;        // query tokens per CTA (x 16 heads = 128 MMA rows)
+constexpr int ATC_H = 16;         // query heads (one KV head)
+constexpr int ATC_CH = 256;       // keys per staged chunk
+constexpr int ATC_KT = 64;        // keys per S tile (MMA N) and per P.V step (MMA K)
+constexpr int ATC_THREADS = 128;  // one thread per MMA row / tensor-memory lane
+constexpr int ATC_SPAN = 2048;    // keys of one split (one partial per row and split)
+
+// shared-memory layout (offsets from a 1024-byte aligned base)
+constexpr uint32_t OFF_Q = 0;                        // 2 k-blocks x [128 rows][64] bf16
+constexpr uint32_t OFF_K = OFF_Q + 2 * 16384;        // 2 k-blocks x [256 keys][64] bf16
+constexpr uint32_t OFF_VT = OFF_K + 2 * 32768;       // 4 key-blocks x [128 dims][64 keys] bf16
+constexpr uint32_t OFF_PH = OFF_VT + 4 * 16384;      // [128 rows][64 keys] bf16, P high part
+constexpr uint32_t OFF_PL = OFF_PH + 16384;          // P low part
+constexpr uint32_t OFF_CTL = OFF_PL + 16384;         // barriers, tensor-memory slot, token table
+constexpr uint32_t ATC_SMEM = OFF_CTL + 512 + 1024;  // + alignment slack
+constexpr uint32_t TMEM_COLS = 512;                  // S: columns [0, 256), O: [256, 384)
+constexpr uint32_t TM_O = 256;
+
+struct TokenInfo {
+    int first, count, begin, end, lane, pad;
+};
+
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+__global__ void __launch_bounds__(ATC_THREADS, 1) k_attn_tc(AttnArgs a, int* error) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
+    uint64_t* bar_s = reinterpret_cast<uint64_t*>(smem + OFF_CTL);
+    uint64_t* bar_pv = bar_s + 1;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_s + 2);
+    int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
+    TokenInfo* tok = reinterpret_cast<TokenInfo*>(smem + OFF_CTL + 64);
+
+    const int t = threadIdx.x, warp = t >> 5;
+    const int s = blockIdx.x, row0 = blockIdx.y * ATC_TOK;
+    const int ntok = min(ATC_TOK, a.rows - row0);
+    if (t < ntok) {
+        const RowGeo g = a.geo[row0 + t];
+        tok[t] = TokenInfo{g.first, g.count, g.begin, g.end, a.desc[row0 + t].lane, 0};
+    }
+    if (t == 0) {
+        bar_init(bar_s, 1);
+        bar_init(bar_pv, 1);
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncwarp();
+    if (warp == 0) tmem_alloc(tmem_slot, TMEM_COLS);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const uint32_t lane_base = uint32_t(warp * 32) << 16;
+    const uint32_t sbase = smem_addr(smem);
+    uint32_t ps = 0, ppv = 0;  // barrier parities
+
+    const int my_tok = t >> 4, my_head = t & 15;  // this thread's MMA row
+    unsigned done = 0;
+    const unsigned all = (1u << ntok) - 1u;
+    while (done != all) {
+        // the next run: the pending tokens that share the first one's lane slab and window
+        const TokenInfo L = tok[__ffs(~done & all) - 1];
+        unsigned run = 0;
+        for (int i = 0; i < ntok; i++) {
+            const TokenInfo& o = tok[i];
+            if (!((done >> i) & 1u) && o.lane == L.lane && o.first == L.first && o.count == L.count) run |= 1u << i;
+        }
+        done |= run;
+        const int k_lo = s * ATC_SPAN, k_hi = min(k_lo + ATC_SPAN, L.count);
+        int klo = 1 << 30, khi = 0;
+        for (int i = 0; i < ntok; i++)
+            if ((run >> i) & 1u) {
+                const int lo = max(tok[i].begin, k_lo), hi = min(tok[i].end, k_hi);
+                if (lo < hi) { klo = min(klo, lo); khi = max(khi, hi); }
+            }
+        const bool mine = (run >> my_tok) & 1u;
+        const int vis_lo = mine ? max(tok[my_tok].begin, k_lo) : 0;
+        const int vis_hi = mine ? min(tok[my_tok].end, k_hi) : 0;
+        float m_run = -INFINITY, l_run = 0.f;
+        if (klo < khi) {
+            // queries of the run's tokens (other rows zero)
+            for (int u = t; u < 128 * 16; u += ATC_THREADS) {
+                const int r = u >> 4, c = u & 15, i = r >> 4;
+                uint4 v = make_uint4(0u, 0u, 0u, 0u);
+                if ((run >> i) & 1u)
+                    v = __ldg(reinterpret_cast<const uint4*>(a.q + size_t(row0 + i) * ATC_H * 128 + (r & 15) * 128) + c);
+                *reinterpret_cast<uint4*>(smem + OFF_Q + (c >> 3) * 16384 + sw128_offset(uint32_t(r), uint32_t(c & 7) * 8)) = v;
+            }
+            const uint16_t* kbase = a.keys + size_t(L.lane) * a.lane_stride;
+            const uint16_t* vbase = a.values + size_t(L.lane) * a.lane_stride;
+            bool o_init = false;
+            for (int kc = klo; kc < khi; kc += ATC_CH) {
+                const int nk = min(ATC_CH, khi - kc), ntile = (nk + ATC_KT - 1) / ATC_KT, nrow = ntile * ATC_KT;
+                // keys: row j = key kc + j; dims d and d + 64 rotate together (local layers)
+                for (int u = t; u < nrow * 8; u += ATC_THREADS) {
+                    const int j = u >> 3, p = u & 7;
+                    uint4 o1 = make_uint4(0u, 0u, 0u, 0u), o2 = o1;
+                    if (j < nk) {
+                        const int kidx = kc + j, slot = (L.first + kidx) % a.cap;
+                        const uint4* src = reinterpret_cast<const uint4*>(kbase + size_t(slot) * 128);
+                        const uint4 x1 = __ldg(src + p), x2 = __ldg(src + 8 + p);
+                        if (a.full) {
+                            o1 = x1;
+                            o2 = x2;
+                        } else {
+                            const uint4* rp = reinterpret_cast<const uint4*>(a.rope_local + size_t(kidx) * 64 + p * 8);
+                            const uint4 c0 = __ldg(rp), c1 = __ldg(rp + 1);
+                            const uint32_t cs[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+                            const uint32_t a1[4] = {x1.x, x1.y, x1.z, x1.w}, a2[4] = {x2.x, x2.y, x2.z, x2.w};
+                            uint32_t r1[4], r2[4];
+#pragma unroll
+                            for (int e = 0; e < 4; e++) {
+                                const float l1 = lo_bf(a1[e]), h1 = hi_bf(a1[e]), l2 = lo_bf(a2[e]), h2 = hi_bf(a2[e]);
+                                const int d = p * 8 + 2 * e;
+                                const uint32_t q0 = f2bf(rope_rotate(l1, l2, d, cs[2 * e]));
+                                const uint32_t q1 = f2bf(rope_rotate(h1, h2, d + 1, cs[2 * e + 1]));
+                                const uint32_t q2 = f2bf(rope_rotate(l2, l1, d + 64, cs[2 * e]));
+                                const uint32_t q3 = f2bf(rope_rotate(h2, h1, d + 65, cs[2 * e + 1]));
+                                r1[e] = q0 | (q1 << 16);
+                                r2[e] = q2 | (q3 << 16);
+                            }
+                            o1 = make_uint4(r1[0], r1[1], r1[2], r1[3]);
+                            o2 = make_uint4(r2[0], r2[1], r2[2], r2[3]);
+                        }
+                    }
+                    *reinterpret_cast<uint4*>(smem + OFF_K + sw128_offset(uint32_t(j), uint32_t(p) * 8)) = o1;
+                    *reinterpret_cast<uint4*>(smem + OFF_K + 32768 + sw128_offset(uint32_t(j), uint32_t(p) * 8)) = o2;
+                }
+                // values, transposed: V^T[d][j] in blocks of 64 keys (consecutive threads take
+                // consecutive keys of one 8-dim group)
+                for (int u = t; u < nrow * 16; u += ATC_THREADS) {
+                    const int p = u / nrow, j = u - p * nrow;
+                    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+                    if (j < nk) {
+                        const int slot = (L.first + kc + j) % a.cap;
+                        v = __ldg(reinterpret_cast<const uint4*>(vbase + size_t(slot) * 128) + p);
+                    }
+                    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+                    uint8_t* blk = smem + OFF_VT + (j >> 6) * 16384;
+#pragma unroll
+                    for (int e = 0; e < 8; e++) {
+                        const uint16_t val = uint16_t((w[e >> 1] >> (16 * (e & 1))) & 0xffffu);
+                        *reinterpret_cast<uint16_t*>(blk + sw128_offset(uint32_t(p * 8 + e), uint32_t(j & 63))) = val;
+                    }
+                }
+                fence_async_smem();
+                __syncthreads();
+                // S = Q.K^T, one 64-key tile per 64 tensor-memory columns
+                if (t == 0) {
+                    tc_fence_after();
+                    const uint32_t idesc = tc_idesc(ATC_KT);
+                    for (int jt = 0; jt < ntile; jt++)
+#pragma unroll
+                        for (int kk = 0; kk < 8; kk++)
+                            umma_bf16(tmem + uint32_t(jt * ATC_KT), sw128_desc(sbase + OFF_Q + (kk >> 2) * 16384 + (kk & 3) * 32),
+                                      sw128_desc(sbase + OFF_K + (kk >> 2) * 32768 + jt * 8192 + (kk & 3) * 32), idesc,
+                                      uint32_t(kk));
+                    umma_commit(bar_s);
+                }
+                if (!__syncthreads_and(bar_wait(bar_s, ps))) {
+                    if (t == 0) { atomicCAS(error, 0, 21); *abort_flag = 1; }
+                    break;
+                }
+                ps ^= 1u;
+                tc_fence_after();
+                // running max over this row's visible keys of the chunk
+                const int lo_r = vis_lo - kc, hi_r = vis_hi - kc;
+                float mc = -INFINITY;
+                for (int jt = 0; jt < ntile; jt++)
+#pragma unroll
+                    for (int q = 0; q < 4; q++) {
+                        uint32_t v[16];
+                        tmem_ld16(tmem + lane_base + uint32_t(jt * ATC_KT + q * 16), v);
+#pragma unroll
+                        for (int e = 0; e < 16; e++) {
+                            const int col = jt * ATC_KT + q * 16 + e;
+                            if (col >= lo_r && col < hi_r) mc = fmaxf(mc, __uint_as_float(v[e]) * PLAMO_ATTN_SCALE);
+                        }
+                    }
+                const float m_new = fmaxf(m_run, mc);
+                const float factor = (m_run > -INFINITY && m_new > m_run) ? pexp(m_run - m_new) : 1.0f;
+                if (o_init && !__all_sync(FULL_MASK, factor == 1.0f)) {
+                    for (int q = 0; q < 8; q++) {
+                        uint32_t v[16];
+                        tmem_ld16(tmem + lane_base + TM_O + uint32_t(q * 16), v);
+#pragma unroll
+                        for (int e = 0; e < 16; e++) v[e] = __float_as_uint(__uint_as_float(v[e]) * factor);
+                        tmem_st16(tmem + lane_base + TM_O + uint32_t(q * 16), v);
+                    }
+                }
+                l_run *= factor;
+                m_run = m_new;
+                // P tile by tile, then O += P_hi.V + P_lo.V
+                bool ok = true;
+                for (int jt = 0; jt < ntile && ok; jt++) {
+                    uint32_t ph[32], pl[32];
+#pragma unroll
+                    for (int q = 0; q < 4; q++) {
+                        uint32_t v[16];
+                        tmem_ld16(tmem + lane_base + uint32_t(jt * ATC_KT + q * 16), v);
+#pragma unroll
+                        for (int e = 0; e < 16; e += 2) {
+                            float p2[2];
+#pragma unroll
+                            for (int h = 0; h < 2; h++) {
+                                const int col = jt * ATC_KT + q * 16 + e + h;
+                                float p = 0.f;
+                                if (col >= lo_r && col < hi_r) p = pexp(__uint_as_float(v[e + h]) * PLAMO_ATTN_SCALE - m_run);
+                                l_run += p;
+                                p2[h] = p;
+                            }
+                            const uint32_t h0 = f2bf(p2[0]), h1 = f2bf(p2[1]);
+                            const uint32_t l0 = f2bf(p2[0] - bf2f(h0)), l1 = f2bf(p2[1] - bf2f(h1));
+                            ph[(q * 16 + e) >> 1] = h0 | (h1 << 16);
+                            pl[(q * 16 + e) >> 1] = l0 | (l1 << 16);
+                        }
+                    }
+#pragma unroll
+                    for (int c = 0; c < 8; c++) {
+                        const uint32_t off = sw128_offset(uint32_t(t), uint32_t(c) * 8);
+                        *reinterpret_cast<uint4*>(smem + OFF_PH + off) = make_uint4(ph[4 * c], ph[4 * c + 1], ph[4 * c + 2], ph[4 * c + 3]);
+                        *reinterpret_cast<uint4*>(smem + OFF_PL + off) = make_uint4(pl[4 * c], pl[4 * c + 1], pl[4 * c + 2], pl[4 * c + 3]);
+                    }
+                    fence_async_smem();
+                    tc_fence_before();
+                    __syncthreads();
+                    if (t == 0) {
+                        tc_fence_after();
+                        const uint32_t idesc = tc_idesc(128);
+                        const uint32_t vt = sbase + OFF_VT + uint32_t(jt) * 16384;
+#pragma unroll
+                        for (int kk = 0; kk < 4; kk++)
+                            umma_bf16(tmem + TM_O, sw128_desc(sbase + OFF_PH + kk * 32), sw128_desc(vt + kk * 32), idesc,
+                                      uint32_t(o_init || kk > 0));
+#pragma unroll
+                        for (int kk = 0; kk < 4; kk++)
+                            umma_bf16(tmem + TM_O, sw128_desc(sbase + OFF_PL + kk * 32), sw128_desc(vt + kk * 32), idesc, 1u);
+                        umma_commit(bar_pv);
+                    }
+                    o_init = true;
+                    ok = __syncthreads_and(bar_wait(bar_pv, ppv)) != 0;
+                    ppv ^= 1u;
+                    tc_fence_after();
+                }
+                if (!ok) {
+                    if (t == 0) { atomicCAS(error, 0, 22); *abort_flag = 1; }
+                    break;
+                }
+                tc_fence_before();
+                __syncthreads();  // every MMA of the chunk is complete: the staging buffers are free
+            }
+        }
+        __syncthreads();
+        if (*abort_flag) break;
+        // this run's rows: the split's statistics and unnormalised output (k_attn_merge's layout)
+        const bool keys_seen = mine && l_run > 0.f;
+        if (klo < khi) {
+            for (int q = 0; q < 8; q++) {
+                uint32_t v[16];
+                tmem_ld16(tmem + lane_base + TM_O + uint32_t(q * 16), v);
+                if (keys_seen) {
+                    float* po = a.part_o + ((size_t(row0 + my_tok) * a.splits + s) * ATC_H + my_head) * 128 + q * 16;
+#pragma unroll
+                    for (int e = 0; e < 16; e += 4)
+                        *reinterpret_cast<float4*>(po + e) = make_float4(__uint_as_float(v[e]), __uint_as_float(v[e + 1]),
+                                                                          __uint_as_float(v[e + 2]), __uint_as_float(v[e + 3]));
+                }
+            }
+        }
+        if (mine)
+            a.part_ml[(size_t(row0 + my_tok) * a.splits + s) * ATC_H + my_head] =
+                keys_seen ? make_float2(m_run, l_run) : make_float2(-INFINITY, 0.f);
+        tc_fence_before();
+        __syncthreads();  // the O rows are read before the next run overwrites them
+        tc_fence_after();
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tmem, TMEM_COLS);
+    }
+}
+
+}  // namespace
+
+bool attention_tc_supported(const AttnArgs& a) {
+    return a.H == ATC_H && a.KV == 1 && a.rows >= 1 && (reinterpret_cast<uintptr_t>(a.q) & 15) == 0 &&
+           (reinterpret_cast<uintptr_t>(a.keys) & 15) == 0 && (reinterpret_cast<uintptr_t>(a.values) & 15) == 0 &&
+           (a.full || (reinterpret_cast<uintptr_t>(a.rope_local) & 15) == 0);
+}
+
+int attention_tc_splits(int cap) { return (cap + ATC_SPAN - 1) / ATC_SPAN; }
+
+cudaError_t configure_attention_tc() {
+    return cudaFuncSetAttribute(k_attn_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, int(ATC_SMEM));
+}
+
+// a.splits must be attention_tc_splits(a.cap) (the partial buffers hold that many splits per row).
+cudaError_t launch_attention_tc(const AttnArgs& a, cudaStream_t s) {
+    if (!attention_tc_supported(a) || a.splits != attention_tc_splits(a.cap)) return cudaErrorInvalidValue;
+    int* error = gemm_error_word(true);
+    if (!error) return cudaErrorInvalidDevice;
+    k_attn_tc<<<dim3(a.splits, (a.rows + ATC_TOK - 1) / ATC_TOK), ATC_THREADS, ATC_SMEM, s>>>(a, error);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    return launch_attention_merge(a, s);
+}
+
+}  // namespace plamo

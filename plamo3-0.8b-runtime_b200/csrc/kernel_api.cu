@@ -150,6 +150,43 @@ int plamo_k_packed_decode(const uint8_t* data, const uint32_t* entries, long lon
     return e == cudaSuccess ? 0 : kfail(e);
 }
 
+int plamo_k_attention_rows(const uint16_t* q, const uint16_t* keys, const uint16_t* values, int heads, int kv_heads,
+                           int cap, const int32_t* geo, int rows, int full, const uint32_t* rope_local, int splits,
+                           int tensor, uint16_t* out, void* workspace, size_t workspace_bytes, void* stream) {
+    if (!q || !keys || !values || !geo || !out || !workspace || rows < 1 || heads < 1 || heads > 32 || kv_heads < 1 ||
+        heads % kv_heads || cap < 1 || (!full && !rope_local) || (!tensor && (splits < 1 || splits > 4096))) {
+        g_error = "Invalid attention arguments";
+        return 1;
+    }
+    if (!configured()) { g_error = "Cannot configure kernels"; return 1; }
+    AttnArgs a;
+    a.q = q; a.keys = keys; a.values = values; a.geo = reinterpret_cast<const RowGeo*>(geo); a.rope_local = rope_local;
+    a.out = out; a.lane_stride = 0; a.rows = rows; a.H = heads; a.KV = kv_heads; a.cap = cap; a.full = full;
+    a.splits = tensor ? attention_tc_splits(cap) : splits;
+    a.per_max = attention_per_max(cap, a.splits);
+    if (tensor && !attention_tc_supported(a)) {
+        g_error = "The tensor-core attention takes 16 query heads over one KV head";
+        return 1;
+    }
+    if (!tensor && attention_smem(heads, kv_heads, a.per_max) > 200 * 1024) { g_error = "Too few attention splits"; return 1; }
+    const size_t desc_b = (size_t(rows) * sizeof(RowDesc) + 255) & ~size_t(255);
+    const size_t po_b = (size_t(rows) * a.splits * heads * 128 * sizeof(float) + 255) & ~size_t(255);
+    const size_t need = desc_b + po_b + size_t(rows) * a.splits * heads * sizeof(float2);
+    if (workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 255)) {
+        g_error = "Attention workspace too small or not 256-byte aligned: " + std::to_string(need) + " bytes needed";
+        return 1;
+    }
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaError_t e = cudaMemsetAsync(ws, 0, desc_b, s);  // every row in lane 0
+    if (e != cudaSuccess) return kfail(e);
+    a.desc = reinterpret_cast<const RowDesc*>(ws);
+    a.part_o = reinterpret_cast<float*>(ws + desc_b);
+    a.part_ml = reinterpret_cast<float2*>(ws + desc_b + po_b);
+    e = tensor ? launch_attention_tc(a, s) : launch_attention(a, s);
+    return e == cudaSuccess ? 0 : kfail(e);
+}
+
 // Library-owned scratch for plamo_k_attention (per device, grown on demand, freed at exit).
 struct AttnScratch {
     void* base = nullptr;

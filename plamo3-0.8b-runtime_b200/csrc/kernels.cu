@@ -676,6 +676,7 @@ cudaError_t configure_kernels() {
         e = cudaFuncSetAttribute(k_attn_partial<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     if (e == cudaSuccess) e = configure_gemm();
     if (e == cudaSuccess) e = configure_gemm_tc();
+    if (e == cudaSuccess) e = configure_attention_tc();
     return e;
 }
 
@@ -711,6 +712,10 @@ cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s) {
     }
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
+    return launch_attention_merge(a, s);
+}
+
+cudaError_t launch_attention_merge(const AttnArgs& a, cudaStream_t s) {
     k_attn_merge<<<a.rows * a.H, 128, 0, s>>>(a);
     return cudaGetLastError();
 }

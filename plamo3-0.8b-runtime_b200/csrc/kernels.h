@@ -106,6 +106,15 @@ int gemm_take_error();
 constexpr int TC_MIN_ROWS = 16;  // fewer rows stay on the order-exact GEMV
 cudaError_t launch_qkv(const QkvArgs& a, cudaStream_t s);
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s);
+// The split merge alone (k_attn_merge over a.splits partials per row).
+cudaError_t launch_attention_merge(const AttnArgs& a, cudaStream_t s);
+// Prefill attention on the tensor cores (attn_tc.cu): 16 query heads over one KV head, each row's
+// keys in attention_tc_splits(cap) splits; partials and merge as launch_attention, results within
+// rounding of it (tensor mode only).
+bool attention_tc_supported(const AttnArgs& a);
+int attention_tc_splits(int cap);
+cudaError_t launch_attention_tc(const AttnArgs& a, cudaStream_t s);
+cudaError_t configure_attention_tc();
 cudaError_t launch_finalize(unsigned long long* keys, const int* key_map, int rows, int* result,
                             int* chain_ids, RowDesc* advance, int* hist, int* hist_count, int hist_cap,
                             cudaStream_t s);

@@ -103,7 +103,8 @@ struct plamo_runtime {
     Config c;
     int context = 0, chunk = 16, local_cap = 0;
     bool packed = false;
-    bool tensor = false;  // projections over >= 16 rows on the tcgen05 GEMM (plamo_set_tensor_gemm)
+    bool tensor = false;       // projections over >= 16 rows on the tcgen05 GEMM (plamo_set_tensor_gemm bit 0)
+    bool tensor_attn = false;  // attention of calls over >= 16 rows on the tensor cores (bit 1)
     std::string name;
     uint8_t* arena = nullptr;
     size_t arena_bytes = 0, weight_bytes = 0;
@@ -362,12 +363,16 @@ static int enqueue_forward(plamo_runtime& rt, Work& w, int rows, const CacheView
         a.q = w.q; a.keys = cv.keys[l]; a.values = cv.values[l]; a.desc = w.desc; a.geo = w.geo; a.rope_local = rt.rope_local;
         a.part_o = w.part_o; a.part_ml = w.part_ml; a.out = w.att; a.lane_stride = cv.stride[l]; a.rows = rows;
         a.H = c.heads; a.KV = c.kv_heads; a.cap = L.cap; a.full = L.full; a.splits = L.splits; a.per_max = L.per_max;
+        // tensor mode: rows of a prefill-like call attend on the tensor cores (attn_tc.cu)
+        const bool attn_tc = rt.tensor_attn && rows >= TC_MIN_ROWS && attention_tc_supported(a);
+        if (attn_tc) a.splits = attention_tc_splits(L.cap);
         for (int r0 = 0; r0 < rows; r0 += w.att_rows) {
             AttnArgs b = a;
             b.rows = std::min(w.att_rows, rows - r0);
             b.q = w.q + size_t(r0) * c.q_dim(); b.out = w.att + size_t(r0) * c.q_dim();
             b.desc = w.desc + r0; b.geo = w.geo + r0;
-            LAUNCH(K_ATTN, launch_attention(b, s));
+            if (attn_tc) LAUNCH(K_ATTN, launch_attention_tc(b, s));
+            else LAUNCH(K_ATTN, launch_attention(b, s));
         }
         g = tc;
         g.lin = L.o; g.x = w.att; g.rows = rows; g.y = w.proj; g.ystride = c.d;
@@ -1228,7 +1233,8 @@ int plamo_repetition_period(const int32_t* tokens, int n, int repeats) {
 
 int plamo_set_tensor_gemm(plamo_runtime* rt, int enable) {
     if (!rt) return fail("Invalid runtime");
-    rt->tensor = enable != 0;
+    rt->tensor = (enable & 1) != 0;
+    rt->tensor_attn = (enable & 2) != 0;
     return 0;
 }
 

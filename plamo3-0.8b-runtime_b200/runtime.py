@@ -114,6 +114,9 @@ def library() -> ctypes.CDLL:
         "plamo_k_packed_decode": (ctypes.c_int, [_vp, _vp, ctypes.c_longlong, _vp, _vp]),
         "plamo_k_attention": (ctypes.c_int, [_vp, _vp, _vp] + [ctypes.c_int] * 8 + [_vp, ctypes.c_int, _vp, _vp]),
         "plamo_k_attention_static": (ctypes.c_int, [_vp, _vp, _vp] + [ctypes.c_int] * 8 + [_vp, ctypes.c_int, _vp, _vp]),
+        "plamo_k_attention_rows": (ctypes.c_int, [_vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp, ctypes.c_int,
+                                                  ctypes.c_int, _vp, ctypes.c_int, ctypes.c_int, _vp, _vp, ctypes.c_size_t,
+                                                  _vp]),
         "plamo_k_exp": (ctypes.c_int, [_vp, _vp, ctypes.c_longlong, _vp]),
     }
     for name, (res, args) in sig.items():
@@ -240,10 +243,13 @@ class Runtime:
                                       float(presence), ctypes.byref(out)))
         return out.value
 
-    def set_tensor_gemm(self, enable: bool = True):
-        """Projections over >= 16 rows on the tcgen05 tensor-core GEMM (prefill, batched steps):
-        results within the accumulation-order tolerance of the default path, not bit for bit."""
-        _check(library().plamo_set_tensor_gemm(self._h, int(bool(enable))))
+    def set_tensor_gemm(self, enable=True):
+        """Tensor mode: True (or 3) puts the projections over >= 16 rows (prefill, batched steps) on
+        the tcgen05 GEMM and the attention of calls over >= 16 rows on tcgen05 MMAs; 1 selects the
+        projections only, 2 the attention only. Results within the accumulation-order tolerance of
+        the default path, not bit for bit."""
+        mode = 3 if enable is True else int(enable)
+        _check(library().plamo_set_tensor_gemm(self._h, mode))
 
     @property
     def persistent(self) -> bool:
@@ -468,6 +474,14 @@ def k_attention_static(q, keys, values, heads, kv_heads, cap, first, count, begi
     """plamo_k_attention on a fixed device scratch array (no device allocation; asynchronous)."""
     _check(library().plamo_k_attention_static(q, keys, values, heads, kv_heads, cap, first, count, begin, end, int(full),
                                               rope_local or None, splits, out, stream or None))
+
+
+def k_attention_rows(q, keys, values, heads, kv_heads, cap, geo, rows, full, rope_local, splits, tensor, out,
+                     workspace, workspace_bytes, stream=0):
+    """plamo_k_attention_rows: multi-row (prefill) attention, CUDA-core or tensor-core kernel."""
+    _check(library().plamo_k_attention_rows(q, keys, values, heads, kv_heads, cap, geo, rows, int(full),
+                                            rope_local or None, splits, int(tensor), out, workspace,
+                                            int(workspace_bytes), stream or None))
 
 
 def k_exp(x, y, n, stream=0):
