@@ -9,11 +9,13 @@
 //     RoPE coordinates, Kernels.metal:277-285) and the values transposed, both in the K-major
 //     128-byte-swizzle layout that the MMA's shared-memory descriptors read;
 //   - S = Q.K^T for up to 4 tiles of 64 keys (M 128, N 64, K 128) lands in tensor memory;
-//   - each thread owns one row: it reads its scores (tcgen05.ld), applies the window / causal mask,
-//     updates the running max (rescaling its O row in tensor memory when the max grows) and writes
-//     P = exp(score - max) as a bf16 hi/lo pair, so P keeps 16 significant bits like the
-//     reference's fp32 softmax output (Kernels.metal:400-437), not bf16's 8;
-//   - O += P_hi.V + P_lo.V (M 128, N 128, K 64 per tile) accumulates in tensor memory.
+//   - two threads own a row, each half of its columns: they read the scores (tcgen05.ld), apply
+//     the window / causal mask, agree on the running max through shared memory (rescaling the O
+//     row in tensor memory when the max grows) and write P = 2^(score log2 e - max) as a bf16
+//     hi/lo pair, so P keeps 16 significant bits like the reference's fp32 softmax output
+//     (Kernels.metal:400-437), not bf16's 8;
+//   - O += P_hi.V + P_lo.V (M 128, N 128, K 64 per tile) accumulates in tensor memory, each tile's
+//     MMAs running while the next tile's P is computed.
 // At the end each row stores its split's (max, sum) and unnormalised O in the layout k_attn_merge
 // reads, and that merge runs unchanged.
 //
@@ -33,7 +35,7 @@ constexpr int ATC_TOK = 8;        // query tokens per CTA (x 16 heads = 128 MMA 
 constexpr int ATC_H = 16;         // query heads (one KV head)
 constexpr int ATC_CH = 256;       // keys per staged chunk
 constexpr int ATC_KT = 64;        // keys per S tile (MMA N) and per P.V step (MMA K)
-constexpr int ATC_THREADS = 128;  // one thread per MMA row / tensor-memory lane
+constexpr int ATC_THREADS = 256;  // two threads per MMA row / tensor-memory lane (column halves)
 constexpr int ATC_SPAN = 2048;    // keys of one split (one partial per row and split)
 
 // shared-memory layout (offsets from a 1024-byte aligned base)
@@ -43,7 +45,8 @@ constexpr uint32_t OFF_VT = OFF_K + 2 * 32768;       // 4 key-blocks x [128 dims
 constexpr uint32_t OFF_PH = OFF_VT + 4 * 16384;      // [128 rows][64 keys] bf16, P high part
 constexpr uint32_t OFF_PL = OFF_PH + 16384;          // P low part
 constexpr uint32_t OFF_CTL = OFF_PL + 16384;         // barriers, tensor-memory slot, token table
-constexpr uint32_t ATC_SMEM = OFF_CTL + 512 + 1024;  // + alignment slack
+constexpr uint32_t OFF_XCH = OFF_CTL + 512;          // [2][128] floats: the halves' row maxima / sums
+constexpr uint32_t ATC_SMEM = OFF_XCH + 1024 + 1024;  // + alignment slack
 constexpr uint32_t TMEM_COLS = 512;                  // S: columns [0, 256), O: [256, 384)
 constexpr uint32_t TM_O = 256;
 
@@ -52,6 +55,14 @@ struct TokenInfo {
 };
 
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+// 2^x on the multi-function unit (relative error about 2^-22, far below P's 16-bit hi/lo split)
+__device__ __forceinline__ float fast_exp2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+constexpr float ATC_LOG2E = 1.4426950408889634f;
+constexpr float ATC_LN2 = 0.6931471805599453f;
 
 __global__ void __launch_bounds__(ATC_THREADS, 1) k_attn_tc(AttnArgs a, int* error) {
     extern __shared__ uint8_t smem_raw[];
@@ -61,8 +72,12 @@ __global__ void __launch_bounds__(ATC_THREADS, 1) k_attn_tc(AttnArgs a, int* err
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_s + 2);
     int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
     TokenInfo* tok = reinterpret_cast<TokenInfo*>(smem + OFF_CTL + 64);
+    float* xchg = reinterpret_cast<float*>(smem + OFF_XCH);  // [2 halves][128 rows] row maxima / sums
 
-    const int t = threadIdx.x, warp = t >> 5;
+    const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+    // warps w and w + 4 share tensor-memory lanes 32 (w % 4) ..: the row is the lane, the two warps
+    // take the two halves of every tile's columns
+    const int quarter = warp & 3, half = warp >> 2, row = quarter * 32 + lane;
     const int s = blockIdx.x, row0 = blockIdx.y * ATC_TOK;
     const int ntok = min(ATC_TOK, a.rows - row0);
     if (t < ntok) {
@@ -81,11 +96,12 @@ __global__ void __launch_bounds__(ATC_THREADS, 1) k_attn_tc(AttnArgs a, int* err
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    const uint32_t lane_base = uint32_t(warp * 32) << 16;
+    const uint32_t lane_base = uint32_t(quarter * 32) << 16;
     const uint32_t sbase = smem_addr(smem);
+    const float qscale = PLAMO_ATTN_SCALE * ATC_LOG2E;  // scores in the log2 domain
     uint32_t ps = 0, ppv = 0;  // barrier parities
 
-    const int my_tok = t >> 4, my_head = t & 15;  // this thread's MMA row
+    const int my_tok = row >> 4, my_head = row & 15;
     unsigned done = 0;
     const unsigned all = (1u << ntok) - 1u;
     while (done != all) {
@@ -107,7 +123,7 @@ __global__ void __launch_bounds__(ATC_THREADS, 1) k_attn_tc(AttnArgs a, int* err
         const bool mine = (run >> my_tok) & 1u;
         const int vis_lo = mine ? max(tok[my_tok].begin, k_lo) : 0;
         const int vis_hi = mine ? min(tok[my_tok].end, k_hi) : 0;
-        float m_run = -INFINITY, l_run = 0.f;
+        float m_run = -INFINITY, l_run = 0.f;  // log2-domain max; this half's share of the sum
         if (klo < khi) {
             // queries of the run's tokens (other rows zero)
             for (int u = t; u < 128 * 16; u += ATC_THREADS) {
@@ -194,49 +210,53 @@ __global__ void __launch_bounds__(ATC_THREADS, 1) k_attn_tc(AttnArgs a, int* err
                 }
                 ps ^= 1u;
                 tc_fence_after();
-                // running max over this row's visible keys of the chunk
+                // the row's max over its visible keys of the chunk: each half over its columns,
+                // then the two halves meet in shared memory
                 const int lo_r = vis_lo - kc, hi_r = vis_hi - kc;
                 float mc = -INFINITY;
                 for (int jt = 0; jt < ntile; jt++)
 #pragma unroll
-                    for (int q = 0; q < 4; q++) {
+                    for (int q = 0; q < 2; q++) {
                         uint32_t v[16];
-                        tmem_ld16(tmem + lane_base + uint32_t(jt * ATC_KT + q * 16), v);
+                        const int c0 = jt * ATC_KT + half * 32 + q * 16;
+                        tmem_ld16(tmem + lane_base + uint32_t(c0), v);
 #pragma unroll
-                        for (int e = 0; e < 16; e++) {
-                            const int col = jt * ATC_KT + q * 16 + e;
-                            if (col >= lo_r && col < hi_r) mc = fmaxf(mc, __uint_as_float(v[e]) * PLAMO_ATTN_SCALE);
-                        }
+                        for (int e = 0; e < 16; e++)
+                            if (c0 + e >= lo_r && c0 + e < hi_r) mc = fmaxf(mc, __uint_as_float(v[e]) * qscale);
                     }
+                xchg[half * 128 + row] = mc;
+                __syncthreads();
+                mc = fmaxf(xchg[row], xchg[128 + row]);
                 const float m_new = fmaxf(m_run, mc);
-                const float factor = (m_run > -INFINITY && m_new > m_run) ? pexp(m_run - m_new) : 1.0f;
+                const float factor = (m_run > -INFINITY && m_new > m_run) ? fast_exp2(m_run - m_new) : 1.0f;
                 if (o_init && !__all_sync(FULL_MASK, factor == 1.0f)) {
-                    for (int q = 0; q < 8; q++) {
+                    for (int q = 0; q < 4; q++) {  // this half's 64 columns of O
                         uint32_t v[16];
-                        tmem_ld16(tmem + lane_base + TM_O + uint32_t(q * 16), v);
+                        const uint32_t col = TM_O + uint32_t(half * 64 + q * 16);
+                        tmem_ld16(tmem + lane_base + col, v);
 #pragma unroll
                         for (int e = 0; e < 16; e++) v[e] = __float_as_uint(__uint_as_float(v[e]) * factor);
-                        tmem_st16(tmem + lane_base + TM_O + uint32_t(q * 16), v);
+                        tmem_st16(tmem + lane_base + col, v);
                     }
                 }
                 l_run *= factor;
                 m_run = m_new;
-                // P tile by tile, then O += P_hi.V + P_lo.V
-                bool ok = true;
+                // P tile by tile: each tile's P is computed while the previous tile's P.V runs
+                bool pending = false, ok = true;
                 for (int jt = 0; jt < ntile && ok; jt++) {
-                    uint32_t ph[32], pl[32];
+                    uint32_t ph[16], pl[16];
 #pragma unroll
-                    for (int q = 0; q < 4; q++) {
+                    for (int q = 0; q < 2; q++) {
                         uint32_t v[16];
-                        tmem_ld16(tmem + lane_base + uint32_t(jt * ATC_KT + q * 16), v);
+                        const int c0 = jt * ATC_KT + half * 32 + q * 16;
+                        tmem_ld16(tmem + lane_base + uint32_t(c0), v);
 #pragma unroll
                         for (int e = 0; e < 16; e += 2) {
                             float p2[2];
 #pragma unroll
                             for (int h = 0; h < 2; h++) {
-                                const int col = jt * ATC_KT + q * 16 + e + h;
-                                float p = 0.f;
-                                if (col >= lo_r && col < hi_r) p = pexp(__uint_as_float(v[e + h]) * PLAMO_ATTN_SCALE - m_run);
+                                const int col = c0 + e + h;
+                                const float p = (col >= lo_r && col < hi_r) ? fast_exp2(__uint_as_float(v[e + h]) * qscale - m_run) : 0.f;
                                 l_run += p;
                                 p2[h] = p;
                             }
@@ -246,9 +266,14 @@ __global__ void __launch_bounds__(ATC_THREADS, 1) k_attn_tc(AttnArgs a, int* err
                             pl[(q * 16 + e) >> 1] = l0 | (l1 << 16);
                         }
                     }
+                    if (pending) {  // the previous tile's P.V has read the P buffer
+                        ok = __syncthreads_and(bar_wait(bar_pv, ppv)) != 0;
+                        ppv ^= 1u;
+                        if (!ok) break;
+                    }
 #pragma unroll
-                    for (int c = 0; c < 8; c++) {
-                        const uint32_t off = sw128_offset(uint32_t(t), uint32_t(c) * 8);
+                    for (int c = 0; c < 4; c++) {
+                        const uint32_t off = sw128_offset(uint32_t(row), uint32_t(half * 4 + c) * 8);
                         *reinterpret_cast<uint4*>(smem + OFF_PH + off) = make_uint4(ph[4 * c], ph[4 * c + 1], ph[4 * c + 2], ph[4 * c + 3]);
                         *reinterpret_cast<uint4*>(smem + OFF_PL + off) = make_uint4(pl[4 * c], pl[4 * c + 1], pl[4 * c + 2], pl[4 * c + 3]);
                     }
@@ -269,28 +294,35 @@ __global__ void __launch_bounds__(ATC_THREADS, 1) k_attn_tc(AttnArgs a, int* err
                         umma_commit(bar_pv);
                     }
                     o_init = true;
+                    pending = true;
+                }
+                if (ok && pending) {
                     ok = __syncthreads_and(bar_wait(bar_pv, ppv)) != 0;
                     ppv ^= 1u;
-                    tc_fence_after();
                 }
                 if (!ok) {
                     if (t == 0) { atomicCAS(error, 0, 22); *abort_flag = 1; }
                     break;
                 }
+                tc_fence_after();
                 tc_fence_before();
                 __syncthreads();  // every MMA of the chunk is complete: the staging buffers are free
             }
         }
         __syncthreads();
         if (*abort_flag) break;
-        // this run's rows: the split's statistics and unnormalised output (k_attn_merge's layout)
-        const bool keys_seen = mine && l_run > 0.f;
+        // this run's rows: the split's (max, sum) in the natural-log domain and unnormalised O
+        xchg[half * 128 + row] = l_run;
+        __syncthreads();
+        const float l_all = xchg[row] + xchg[128 + row];
+        const bool keys_seen = mine && l_all > 0.f;
         if (klo < khi) {
-            for (int q = 0; q < 8; q++) {
+            for (int q = 0; q < 4; q++) {
                 uint32_t v[16];
-                tmem_ld16(tmem + lane_base + TM_O + uint32_t(q * 16), v);
+                const int col = half * 64 + q * 16;
+                tmem_ld16(tmem + lane_base + TM_O + uint32_t(col), v);
                 if (keys_seen) {
-                    float* po = a.part_o + ((size_t(row0 + my_tok) * a.splits + s) * ATC_H + my_head) * 128 + q * 16;
+                    float* po = a.part_o + ((size_t(row0 + my_tok) * a.splits + s) * ATC_H + my_head) * 128 + col;
 #pragma unroll
                     for (int e = 0; e < 16; e += 4)
                         *reinterpret_cast<float4*>(po + e) = make_float4(__uint_as_float(v[e]), __uint_as_float(v[e + 1]),
@@ -298,11 +330,11 @@ __global__ void __launch_bounds__(ATC_THREADS, 1) k_attn_tc(AttnArgs a, int* err
                 }
             }
         }
-        if (mine)
+        if (mine && half == 0)
             a.part_ml[(size_t(row0 + my_tok) * a.splits + s) * ATC_H + my_head] =
-                keys_seen ? make_float2(m_run, l_run) : make_float2(-INFINITY, 0.f);
+                keys_seen ? make_float2(m_run * ATC_LN2, l_all) : make_float2(-INFINITY, 0.f);
         tc_fence_before();
-        __syncthreads();  // the O rows are read before the next run overwrites them
+        __syncthreads();  // the O rows and sums are read before the next run overwrites them
         tc_fence_after();
     }
     tc_fence_before();
