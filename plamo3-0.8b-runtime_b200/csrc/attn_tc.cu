@@ -61,6 +61,24 @@ __device__ __forceinline__ float fast_exp2(float x) {
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
     return y;
 }
+// Two floats to a bf16 pair (lo in the low half), round to nearest even in one instruction: the
+// same bits as f2bf for every finite value, which is all this kernel converts.
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+    uint32_t r;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+    return r;
+}
+__device__ __forceinline__ float round_bf16(float x) {
+    uint32_t r;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %1;" : "=r"(r) : "f"(x));
+    return __uint_as_float(r << 16);
+}
+// Rotate-half RoPE of one element as rope_rotate (Kernels.metal:261-274) with the hardware
+// rounding: rbf(rbf(x c) + rbf(+-other s)).
+__device__ __forceinline__ float rope_fast(float x, float other, bool low, uint32_t cs) {
+    const float c = lo_bf(cs), sn = hi_bf(cs);
+    return round_bf16(round_bf16(x * c) + round_bf16((low ? -other : other) * sn));
+}
 constexpr float ATC_LOG2E = 1.4426950408889634f;
 constexpr float ATC_LN2 = 0.6931471805599453f;
 
@@ -125,69 +143,96 @@ __global__ void __launch_bounds__(ATC_THREADS, 1) k_attn_tc(AttnArgs a, int* err
         const int vis_hi = mine ? min(tok[my_tok].end, k_hi) : 0;
         float m_run = -INFINITY, l_run = 0.f;  // log2-domain max; this half's share of the sum
         if (klo < khi) {
-            // queries of the run's tokens (other rows zero)
-            for (int u = t; u < 128 * 16; u += ATC_THREADS) {
-                const int r = u >> 4, c = u & 15, i = r >> 4;
-                uint4 v = make_uint4(0u, 0u, 0u, 0u);
-                if ((run >> i) & 1u)
-                    v = __ldg(reinterpret_cast<const uint4*>(a.q + size_t(row0 + i) * ATC_H * 128 + (r & 15) * 128) + c);
-                *reinterpret_cast<uint4*>(smem + OFF_Q + (c >> 3) * 16384 + sw128_offset(uint32_t(r), uint32_t(c & 7) * 8)) = v;
+            // queries of the run's tokens (other rows zero); every load of a thread in flight at once
+            {
+                uint4 v[8];
+#pragma unroll
+                for (int b = 0; b < 8; b++) {
+                    const int u = t + b * ATC_THREADS, r = u >> 4, c = u & 15, i = r >> 4;
+                    v[b] = (run >> i) & 1u
+                               ? __ldg(reinterpret_cast<const uint4*>(a.q + size_t(row0 + i) * ATC_H * 128 + (r & 15) * 128) + c)
+                               : make_uint4(0u, 0u, 0u, 0u);
+                }
+#pragma unroll
+                for (int b = 0; b < 8; b++) {
+                    const int u = t + b * ATC_THREADS, r = u >> 4, c = u & 15;
+                    *reinterpret_cast<uint4*>(smem + OFF_Q + (c >> 3) * 16384 + sw128_offset(uint32_t(r), uint32_t(c & 7) * 8)) = v[b];
+                }
             }
             const uint16_t* kbase = a.keys + size_t(L.lane) * a.lane_stride;
             const uint16_t* vbase = a.values + size_t(L.lane) * a.lane_stride;
             bool o_init = false;
             for (int kc = klo; kc < khi; kc += ATC_CH) {
                 const int nk = min(ATC_CH, khi - kc), ntile = (nk + ATC_KT - 1) / ATC_KT, nrow = ntile * ATC_KT;
-                // keys: row j = key kc + j; dims d and d + 64 rotate together (local layers)
-                for (int u = t; u < nrow * 8; u += ATC_THREADS) {
-                    const int j = u >> 3, p = u & 7;
-                    uint4 o1 = make_uint4(0u, 0u, 0u, 0u), o2 = o1;
-                    if (j < nk) {
-                        const int kidx = kc + j, slot = (L.first + kidx) % a.cap;
-                        const uint4* src = reinterpret_cast<const uint4*>(kbase + size_t(slot) * 128);
-                        const uint4 x1 = __ldg(src + p), x2 = __ldg(src + 8 + p);
-                        if (a.full) {
-                            o1 = x1;
-                            o2 = x2;
-                        } else {
-                            const uint4* rp = reinterpret_cast<const uint4*>(a.rope_local + size_t(kidx) * 64 + p * 8);
-                            const uint4 c0 = __ldg(rp), c1 = __ldg(rp + 1);
-                            const uint32_t cs[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-                            const uint32_t a1[4] = {x1.x, x1.y, x1.z, x1.w}, a2[4] = {x2.x, x2.y, x2.z, x2.w};
+                // keys: row j = key kc + j; dims d and d + 64 rotate together (local layers). Four
+                // units per thread at a time, their loads issued together.
+                for (int b0 = 0; b0 * ATC_THREADS < nrow * 8; b0 += 4) {
+                    uint4 x1[4], x2[4], c0[4], c1[4];
+#pragma unroll
+                    for (int b = 0; b < 4; b++) {
+                        const int u = t + (b0 + b) * ATC_THREADS, j = u >> 3, p = u & 7;
+                        x1[b] = x2[b] = c0[b] = c1[b] = make_uint4(0u, 0u, 0u, 0u);
+                        if (u < nrow * 8 && j < nk) {
+                            const int kidx = kc + j, slot = (L.first + kidx) % a.cap;
+                            const uint4* src = reinterpret_cast<const uint4*>(kbase + size_t(slot) * 128);
+                            x1[b] = __ldg(src + p);
+                            x2[b] = __ldg(src + 8 + p);
+                            if (!a.full) {
+                                const uint4* rp = reinterpret_cast<const uint4*>(a.rope_local + size_t(kidx) * 64 + p * 8);
+                                c0[b] = __ldg(rp);
+                                c1[b] = __ldg(rp + 1);
+                            }
+                        }
+                    }
+#pragma unroll
+                    for (int b = 0; b < 4; b++) {
+                        const int u = t + (b0 + b) * ATC_THREADS, j = u >> 3, p = u & 7;
+                        if (u >= nrow * 8) break;
+                        uint4 o1 = x1[b], o2 = x2[b];
+                        if (!a.full && j < nk) {
+                            const uint32_t cs[8] = {c0[b].x, c0[b].y, c0[b].z, c0[b].w, c1[b].x, c1[b].y, c1[b].z, c1[b].w};
+                            const uint32_t a1[4] = {x1[b].x, x1[b].y, x1[b].z, x1[b].w}, a2[4] = {x2[b].x, x2[b].y, x2[b].z, x2[b].w};
                             uint32_t r1[4], r2[4];
 #pragma unroll
                             for (int e = 0; e < 4; e++) {
                                 const float l1 = lo_bf(a1[e]), h1 = hi_bf(a1[e]), l2 = lo_bf(a2[e]), h2 = hi_bf(a2[e]);
                                 const int d = p * 8 + 2 * e;
-                                const uint32_t q0 = f2bf(rope_rotate(l1, l2, d, cs[2 * e]));
-                                const uint32_t q1 = f2bf(rope_rotate(h1, h2, d + 1, cs[2 * e + 1]));
-                                const uint32_t q2 = f2bf(rope_rotate(l2, l1, d + 64, cs[2 * e]));
-                                const uint32_t q3 = f2bf(rope_rotate(h2, h1, d + 65, cs[2 * e + 1]));
-                                r1[e] = q0 | (q1 << 16);
-                                r2[e] = q2 | (q3 << 16);
+                                (void)d;
+                                r1[e] = pack_bf16x2(rope_fast(l1, l2, true, cs[2 * e]), rope_fast(h1, h2, true, cs[2 * e + 1]));
+                                r2[e] = pack_bf16x2(rope_fast(l2, l1, false, cs[2 * e]), rope_fast(h2, h1, false, cs[2 * e + 1]));
                             }
                             o1 = make_uint4(r1[0], r1[1], r1[2], r1[3]);
                             o2 = make_uint4(r2[0], r2[1], r2[2], r2[3]);
                         }
+                        *reinterpret_cast<uint4*>(smem + OFF_K + sw128_offset(uint32_t(j), uint32_t(p) * 8)) = o1;
+                        *reinterpret_cast<uint4*>(smem + OFF_K + 32768 + sw128_offset(uint32_t(j), uint32_t(p) * 8)) = o2;
                     }
-                    *reinterpret_cast<uint4*>(smem + OFF_K + sw128_offset(uint32_t(j), uint32_t(p) * 8)) = o1;
-                    *reinterpret_cast<uint4*>(smem + OFF_K + 32768 + sw128_offset(uint32_t(j), uint32_t(p) * 8)) = o2;
                 }
                 // values, transposed: V^T[d][j] in blocks of 64 keys (consecutive threads take
-                // consecutive keys of one 8-dim group)
-                for (int u = t; u < nrow * 16; u += ATC_THREADS) {
-                    const int p = u / nrow, j = u - p * nrow;
-                    uint4 v = make_uint4(0u, 0u, 0u, 0u);
-                    if (j < nk) {
-                        const int slot = (L.first + kc + j) % a.cap;
-                        v = __ldg(reinterpret_cast<const uint4*>(vbase + size_t(slot) * 128) + p);
-                    }
-                    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-                    uint8_t* blk = smem + OFF_VT + (j >> 6) * 16384;
+                // consecutive keys of one 8-dim group); eight units per thread at a time
+                for (int b0 = 0; b0 * ATC_THREADS < nrow * 16; b0 += 8) {
+                    uint4 v[8];
 #pragma unroll
-                    for (int e = 0; e < 8; e++) {
-                        const uint16_t val = uint16_t((w[e >> 1] >> (16 * (e & 1))) & 0xffffu);
-                        *reinterpret_cast<uint16_t*>(blk + sw128_offset(uint32_t(p * 8 + e), uint32_t(j & 63))) = val;
+                    for (int b = 0; b < 8; b++) {
+                        const int u = t + (b0 + b) * ATC_THREADS, p = u / nrow, j = u - p * nrow;
+                        v[b] = make_uint4(0u, 0u, 0u, 0u);
+                        if (u < nrow * 16 && j < nk) {
+                            const int slot = (L.first + kc + j) % a.cap;
+                            v[b] = __ldg(reinterpret_cast<const uint4*>(vbase + size_t(slot) * 128) + p);
+                        }
+                    }
+#pragma unroll
+                    for (int b = 0; b < 8; b++) {
+                        const int u = t + (b0 + b) * ATC_THREADS, p = u / nrow, j = u - p * nrow;
+                        if (u >= nrow * 16) break;
+                        const uint32_t w[4] = {v[b].x, v[b].y, v[b].z, v[b].w};
+                        // element (dim 8p + e, key j): rows 8p..8p+7 are one 1024-byte swizzle group
+                        uint8_t* blk = smem + OFF_VT + (j >> 6) * 16384 + p * 1024 + (j & 7) * 2;
+                        const uint32_t jc = uint32_t(j & 63) >> 3;
+#pragma unroll
+                        for (int e = 0; e < 8; e++)
+                            *reinterpret_cast<uint16_t*>(blk + e * 128 + ((jc ^ uint32_t(e)) << 4)) =
+                                uint16_t(w[e >> 1] >> (16 * (e & 1)));
                     }
                 }
                 fence_async_smem();
@@ -214,30 +259,41 @@ __global__ void __launch_bounds__(ATC_THREADS, 1) k_attn_tc(AttnArgs a, int* err
                 // then the two halves meet in shared memory
                 const int lo_r = vis_lo - kc, hi_r = vis_hi - kc;
                 float mc = -INFINITY;
-                for (int jt = 0; jt < ntile; jt++)
+                for (int jt = 0; jt < ntile; jt += 2) {  // two tiles' loads in flight per wait
+                    uint32_t va[32], vb[32];
+                    const int ca = jt * ATC_KT + half * 32, cb = ca + ATC_KT;
+                    tmem_ld32_async(tmem + lane_base + uint32_t(ca), va);
+                    if (jt + 1 < ntile) tmem_ld32_async(tmem + lane_base + uint32_t(cb), vb);
+                    tmem_wait_ld(va);
+                    tmem_wait_ld(vb);
 #pragma unroll
-                    for (int q = 0; q < 2; q++) {
-                        uint32_t v[16];
-                        const int c0 = jt * ATC_KT + half * 32 + q * 16;
-                        tmem_ld16(tmem + lane_base + uint32_t(c0), v);
+                    for (int e = 0; e < 32; e++)
+                        if (ca + e >= lo_r && ca + e < hi_r) mc = fmaxf(mc, __uint_as_float(va[e]) * qscale);
+                    if (jt + 1 < ntile)
 #pragma unroll
-                        for (int e = 0; e < 16; e++)
-                            if (c0 + e >= lo_r && c0 + e < hi_r) mc = fmaxf(mc, __uint_as_float(v[e]) * qscale);
-                    }
+                        for (int e = 0; e < 32; e++)
+                            if (cb + e >= lo_r && cb + e < hi_r) mc = fmaxf(mc, __uint_as_float(vb[e]) * qscale);
+                }
                 xchg[half * 128 + row] = mc;
                 __syncthreads();
                 mc = fmaxf(xchg[row], xchg[128 + row]);
                 const float m_new = fmaxf(m_run, mc);
                 const float factor = (m_run > -INFINITY && m_new > m_run) ? fast_exp2(m_run - m_new) : 1.0f;
-                if (o_init && !__all_sync(FULL_MASK, factor == 1.0f)) {
-                    for (int q = 0; q < 4; q++) {  // this half's 64 columns of O
-                        uint32_t v[16];
-                        const uint32_t col = TM_O + uint32_t(half * 64 + q * 16);
-                        tmem_ld16(tmem + lane_base + col, v);
+                if (o_init && !__all_sync(FULL_MASK, factor == 1.0f)) {  // this half's 64 columns of O
+                    uint32_t va[32], vb[32];
+                    const uint32_t col = lane_base + TM_O + uint32_t(half * 64);
+                    tmem_ld32_async(tmem + col, va);
+                    tmem_ld32_async(tmem + col + 32, vb);
+                    tmem_wait_ld(va);
+                    tmem_wait_ld(vb);
 #pragma unroll
-                        for (int e = 0; e < 16; e++) v[e] = __float_as_uint(__uint_as_float(v[e]) * factor);
-                        tmem_st16(tmem + lane_base + col, v);
+                    for (int e = 0; e < 32; e++) {
+                        va[e] = __float_as_uint(__uint_as_float(va[e]) * factor);
+                        vb[e] = __float_as_uint(__uint_as_float(vb[e]) * factor);
                     }
+                    tmem_st32_async(tmem + col, va);
+                    tmem_st32_async(tmem + col + 32, vb);
+                    tmem_wait_st();
                 }
                 l_run *= factor;
                 m_run = m_new;
@@ -245,25 +301,27 @@ __global__ void __launch_bounds__(ATC_THREADS, 1) k_attn_tc(AttnArgs a, int* err
                 bool pending = false, ok = true;
                 for (int jt = 0; jt < ntile && ok; jt++) {
                     uint32_t ph[16], pl[16];
+                    {
+                        uint32_t v[32];
+                        const int c0 = jt * ATC_KT + half * 32;
+                        tmem_ld32_async(tmem + lane_base + uint32_t(c0), v);
+                        tmem_wait_ld(v);
+                        // columns outside [lo_r, hi_r) get P = 0; the tile is wholly visible for most rows
+                        const bool whole = c0 >= lo_r && c0 + 32 <= hi_r;
+                        const float nm = -m_run;
 #pragma unroll
-                    for (int q = 0; q < 2; q++) {
-                        uint32_t v[16];
-                        const int c0 = jt * ATC_KT + half * 32 + q * 16;
-                        tmem_ld16(tmem + lane_base + uint32_t(c0), v);
-#pragma unroll
-                        for (int e = 0; e < 16; e += 2) {
-                            float p2[2];
-#pragma unroll
-                            for (int h = 0; h < 2; h++) {
-                                const int col = c0 + e + h;
-                                const float p = (col >= lo_r && col < hi_r) ? fast_exp2(__uint_as_float(v[e + h]) * qscale - m_run) : 0.f;
-                                l_run += p;
-                                p2[h] = p;
+                        for (int e = 0; e < 32; e += 2) {
+                            float p0 = fast_exp2(fmaf(__uint_as_float(v[e]), qscale, nm));
+                            float p1 = fast_exp2(fmaf(__uint_as_float(v[e + 1]), qscale, nm));
+                            if (!whole) {
+                                p0 = (c0 + e >= lo_r && c0 + e < hi_r) ? p0 : 0.f;
+                                p1 = (c0 + e + 1 >= lo_r && c0 + e + 1 < hi_r) ? p1 : 0.f;
                             }
-                            const uint32_t h0 = f2bf(p2[0]), h1 = f2bf(p2[1]);
-                            const uint32_t l0 = f2bf(p2[0] - bf2f(h0)), l1 = f2bf(p2[1] - bf2f(h1));
-                            ph[(q * 16 + e) >> 1] = h0 | (h1 << 16);
-                            pl[(q * 16 + e) >> 1] = l0 | (l1 << 16);
+                            l_run += p0;
+                            l_run += p1;
+                            const uint32_t hp = pack_bf16x2(p0, p1);
+                            ph[e >> 1] = hp;
+                            pl[e >> 1] = pack_bf16x2(p0 - lo_bf(hp), p1 - hi_bf(hp));
                         }
                     }
                     if (pending) {  // the previous tile's P.V has read the P buffer
@@ -317,16 +375,20 @@ __global__ void __launch_bounds__(ATC_THREADS, 1) k_attn_tc(AttnArgs a, int* err
         const float l_all = xchg[row] + xchg[128 + row];
         const bool keys_seen = mine && l_all > 0.f;
         if (klo < khi) {
-            for (int q = 0; q < 4; q++) {
-                uint32_t v[16];
-                const int col = half * 64 + q * 16;
-                tmem_ld16(tmem + lane_base + TM_O + uint32_t(col), v);
-                if (keys_seen) {
-                    float* po = a.part_o + ((size_t(row0 + my_tok) * a.splits + s) * ATC_H + my_head) * 128 + col;
+            uint32_t va[32], vb[32];
+            const int col = half * 64;
+            tmem_ld32_async(tmem + lane_base + TM_O + uint32_t(col), va);
+            tmem_ld32_async(tmem + lane_base + TM_O + uint32_t(col + 32), vb);
+            tmem_wait_ld(va);
+            tmem_wait_ld(vb);
+            if (keys_seen) {
+                float* po = a.part_o + ((size_t(row0 + my_tok) * a.splits + s) * ATC_H + my_head) * 128 + col;
 #pragma unroll
-                    for (int e = 0; e < 16; e += 4)
-                        *reinterpret_cast<float4*>(po + e) = make_float4(__uint_as_float(v[e]), __uint_as_float(v[e + 1]),
-                                                                          __uint_as_float(v[e + 2]), __uint_as_float(v[e + 3]));
+                for (int e = 0; e < 32; e += 4) {
+                    *reinterpret_cast<float4*>(po + e) = make_float4(__uint_as_float(va[e]), __uint_as_float(va[e + 1]),
+                                                                      __uint_as_float(va[e + 2]), __uint_as_float(va[e + 3]));
+                    *reinterpret_cast<float4*>(po + 32 + e) = make_float4(__uint_as_float(vb[e]), __uint_as_float(vb[e + 1]),
+                                                                           __uint_as_float(vb[e + 2]), __uint_as_float(vb[e + 3]));
                 }
             }
         }

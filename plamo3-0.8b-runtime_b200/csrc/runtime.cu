@@ -70,6 +70,7 @@ struct CacheView {
 struct Work {
     int rows_cap = 0;
     int att_rows = 0;  // rows per attention launch (its split partials hold that many)
+    long long att_row_splits = 0;  // (row, split) partial slots the buffers hold
     uint16_t *x, *h, *qkv, *q, *att, *proj, *act;
     RowGeo* geo;
     RowDesc* desc;
@@ -239,6 +240,7 @@ static int alloc_work(Owner& o, plamo_runtime& rt, Work& w, int rows) {
     for (const Layer& L : rt.layers) max_splits = std::max(max_splits, L.splits);
     const size_t row_part = size_t(max_splits) * c.heads * (128 * sizeof(float) + sizeof(float2));
     w.att_rows = int(std::min<size_t>(rows, std::max<size_t>(ATT_ROWS, ATT_PART_BYTES / row_part)));
+    w.att_row_splits = (long long)w.att_rows * max_splits;
     const size_t R = size_t(rows), RA = size_t(w.att_rows);
     w.rows_cap = rows;
     w.part_tc_cap = TC_PART_FLOATS;
@@ -365,10 +367,13 @@ static int enqueue_forward(plamo_runtime& rt, Work& w, int rows, const CacheView
         a.H = c.heads; a.KV = c.kv_heads; a.cap = L.cap; a.full = L.full; a.splits = L.splits; a.per_max = L.per_max;
         // tensor mode: rows of a prefill-like call attend on the tensor cores (attn_tc.cu)
         const bool attn_tc = rt.tensor_attn && rows >= TC_MIN_ROWS && attention_tc_supported(a);
+        // the tensor-core kernel splits each row's keys into fewer, wider splits: a launch takes as
+        // many rows as the partial buffers hold at that split count
         if (attn_tc) a.splits = attention_tc_splits(L.cap);
-        for (int r0 = 0; r0 < rows; r0 += w.att_rows) {
+        const int per_launch = attn_tc ? int(std::max<long long>(1, w.att_row_splits / a.splits)) : w.att_rows;
+        for (int r0 = 0; r0 < rows; r0 += per_launch) {
             AttnArgs b = a;
-            b.rows = std::min(w.att_rows, rows - r0);
+            b.rows = std::min(per_launch, rows - r0);
             b.q = w.q + size_t(r0) * c.q_dim(); b.out = w.att + size_t(r0) * c.q_dim();
             b.desc = w.desc + r0; b.geo = w.geo + r0;
             if (attn_tc) LAUNCH(K_ATTN, launch_attention_tc(b, s));
