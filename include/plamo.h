@@ -103,7 +103,11 @@ PLAMO_API int plamo_batch_generate(plamo_batch*, const int32_t* const* prompts, 
                          int32_t* reasons, int32_t* out_count);
 
 /* Debug/state access used by the parity tests: copies one layer's KV cache (scalar runtime, or one
- * lane of a batch) as bf16 bits, capacity*kv_heads*128 values each. */
+ * lane of a batch) as bf16 bits in the reference's ring layout, capacity*kv_heads*128 values each:
+ * global layers hold every position (capacity = context); local layers show the reference's ring of
+ * min(context, window + 16) slots (Runtime.swift:240), the key of position k of the last
+ * `capacity` positions at slot k % capacity (the library's own ring is longer, so a prefill call
+ * can take a long prompt's chunks in one pass). */
 PLAMO_API int plamo_debug_kv(plamo_runtime*, int layer, uint16_t* keys, uint16_t* values);
 PLAMO_API int plamo_batch_debug_kv(plamo_batch*, int layer, int lane, uint16_t* keys, uint16_t* values);
 

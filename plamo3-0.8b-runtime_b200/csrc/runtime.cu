@@ -102,7 +102,13 @@ struct plamo_runtime {
     int device = 0;
     cudaStream_t stream = nullptr;
     Config c;
-    int context = 0, chunk = 16, local_cap = 0;
+    int context = 0, chunk = 16;
+    // Local layers keep a ring of the last keys. The reference's ring holds window + 16 keys
+    // (Runtime.swift:240), enough for one 16-token chunk per command buffer; that capacity
+    // (local_ref_cap) sets the split-K partitions and the debug view. The physical ring here
+    // (local_cap) holds window + PREFILL_CALL_ROWS keys, so one forward call can take up to that
+    // many rows of a long prompt without overwriting a key an earlier row of the call still sees.
+    int local_cap = 0, local_ref_cap = 0;
     bool packed = false;
     bool tensor = false;       // projections over >= 16 rows on the tcgen05 GEMM (plamo_set_tensor_gemm bit 0)
     bool tensor_attn = false;  // attention of calls over >= 16 rows on the tensor cores (bit 1)
@@ -228,6 +234,9 @@ static int pin_alloc(Owner& o, T*& p, size_t count) {
 // them (a wide prefill would otherwise need rows x splits x heads x 128 floats at once): as many
 // rows as ATT_PART_BYTES of partials hold, and at least ATT_ROWS.
 constexpr int ATT_ROWS = 64;
+// Rows of one prompt a prefill call may take once the prompt overruns the local ring (the slack
+// of the physical ring beyond the window).
+constexpr int PREFILL_CALL_ROWS = 512;
 constexpr size_t ATT_PART_BYTES = size_t(64) << 20;
 // Split-K partials of the tcgen05 GEMM (8 MiB): splits of the small projections at up to a few
 // dozen rows; larger calls have tiles enough for every SM and do not split.
@@ -339,8 +348,10 @@ static int prof_end(cudaStream_t s, int cls) {
 // out_map[k]: 1 for the scalar runtime (Runtime.swift:453-458), every row for a batched step
 // (Batch.swift:163-165), the lanes' last prompt rows for a batched prefill. chain: also feed the
 // argmax back as the next step's input id and advance the row descriptors (device-chained decode).
+// chunked: the rows are prompt chunks (consecutive rows share a chunk and a lane), the shape the
+// tensor-core attention takes; batched decode steps (one row per lane) are not.
 static int enqueue_forward(plamo_runtime& rt, Work& w, int rows, const CacheView& cv, int nout, Outputs& o,
-                           bool chain) {
+                           bool chain, bool chunked = false) {
     const Config& c = rt.c;
     cudaStream_t s = rt.stream;
     LAUNCH(K_NORM, launch_embed_norm(w.ids, rows, c.vocab, rt.embed, rt.layers[0].pre_mixer, c.d, w.x, w.h, nout ? o.keys : nullptr,
@@ -366,7 +377,7 @@ static int enqueue_forward(plamo_runtime& rt, Work& w, int rows, const CacheView
         a.part_o = w.part_o; a.part_ml = w.part_ml; a.out = w.att; a.lane_stride = cv.stride[l]; a.rows = rows;
         a.H = c.heads; a.KV = c.kv_heads; a.cap = L.cap; a.full = L.full; a.splits = L.splits; a.per_max = L.per_max;
         // tensor mode: rows of a prefill-like call attend on the tensor cores (attn_tc.cu)
-        const bool attn_tc = rt.tensor_attn && rows >= TC_MIN_ROWS && attention_tc_supported(a);
+        const bool attn_tc = rt.tensor_attn && chunked && rows >= TC_MIN_ROWS && attention_tc_supported(a);
         // the tensor-core kernel splits each row's keys into fewer, wider splits: a launch takes as
         // many rows as the partial buffers hold at that split count
         if (attn_tc) a.splits = attention_tc_splits(L.cap);
@@ -662,7 +673,7 @@ static int prefill_rows(plamo_runtime& rt, Work& w, const CacheView& cv, Outputs
     for (int c = 0; c < max_chunks; c++)
         for (int i = 0; i < int(lanes.size()); i++)
             if (c * chunk < lanes[i].len) units.push_back({i, c * chunk});
-    std::vector<char> in_call(lanes.size());
+    std::vector<int> in_call(lanes.size());  // rows of each lane in the call being built
     std::vector<std::pair<int, int>> call;
     size_t u = 0;
     while (u < units.size()) {
@@ -672,8 +683,10 @@ static int prefill_rows(plamo_runtime& rt, Work& w, const CacheView& cv, Outputs
         while (u < units.size()) {
             const int i = units[u].first, cn = std::min(chunk, lanes[i].len - units[u].second);
             if (rows + cn > w.rows_cap) break;
-            if (in_call[i] && lanes[i].pos0 + lanes[i].len > rt.local_cap) break;
-            in_call[i] = 1;
+            // a lane whose prompt overruns the local ring takes at most ring - window rows per call
+            if (in_call[i] && lanes[i].pos0 + lanes[i].len > rt.local_cap && in_call[i] + cn > rt.local_cap - rt.c.window)
+                break;
+            in_call[i] += cn;
             call.push_back(units[u++]);
             rows += cn;
         }
@@ -693,7 +706,7 @@ static int prefill_rows(plamo_runtime& rt, Work& w, const CacheView& cv, Outputs
             }
         if (upload_inputs(rt, w, rows)) return 1;
         CK(cudaEventRecord(rt.e0, rt.stream));
-        if (enqueue_forward(rt, w, rows, cv, nout, o, false)) return 1;
+        if (enqueue_forward(rt, w, rows, cv, nout, o, false, true)) return 1;
         if (finish(rt, seconds)) return 1;
         if (rows > 1 && check_gemm()) return 1;
     }
@@ -718,7 +731,7 @@ static int forward_impl(plamo_runtime& rt, const int32_t* ids, int n, bool outpu
         if (decode_step(rt)) return 1;
         if (rt.mega) CK(cudaMemcpyAsync(rt.h_error, rt.margs.error, sizeof(int), cudaMemcpyDeviceToHost, rt.stream));
     } else {
-        if (enqueue_forward(rt, w, n, rt.cache, output ? 1 : 0, rt.out, false)) return 1;
+        if (enqueue_forward(rt, w, n, rt.cache, output ? 1 : 0, rt.out, false, true)) return 1;
     }
     if (output) CK(cudaMemcpyAsync(rt.out.h_result, rt.out.result, sizeof(int), cudaMemcpyDeviceToHost, rt.stream));
     if (finish(rt, &rt.gpu_seconds)) return 1;
@@ -821,7 +834,8 @@ static int open_common(const char* model_dir, int context, int packed, int devic
     rt->context = context;
     rt->packed = packed != 0;
     rt->chunk = std::min(context, 16);                                   // Runtime.swift:173
-    rt->local_cap = std::min(context, rt->c.window + rt->chunk);         // Runtime.swift:240
+    rt->local_ref_cap = std::min(context, rt->c.window + rt->chunk);     // Runtime.swift:240
+    rt->local_cap = std::min(context, rt->c.window + PREFILL_CALL_ROWS);
     int rc = configure_kernels() == cudaSuccess ? 0 : fail("Cannot configure kernels");
     if (!rc && (cudaStreamCreateWithFlags(&rt->stream, cudaStreamNonBlocking) != cudaSuccess ||
                 cudaEventCreate(&rt->e0) != cudaSuccess || cudaEventCreate(&rt->e1) != cudaSuccess))
@@ -956,10 +970,12 @@ static int setup_runtime(plamo_runtime* rt, const ModelFiles* mf, bool upload, s
         L.gate_up = lin(items[k++], 2 * c.ffn, c.d);
         L.down = lin(items[k++], c.d, c.ffn);
         L.full = c.is_global(i);
-        L.cap = L.full ? rt->context : rt->local_cap;  // Runtime.swift:240
-        // split-K width: ~64 keys per split for the local window, <= 256 keys for global history
-        L.splits = L.full ? std::max(32, (L.cap + 255) / 256) : std::max(1, (L.cap + 63) / 64);
-        L.per_max = attention_per_max(L.cap, L.splits);
+        L.cap = L.full ? rt->context : rt->local_cap;
+        // split-K width: ~64 keys per split for the local window, <= 256 keys for global history,
+        // from the reference's capacities (the partitions set the summation order)
+        const int ref_cap = L.full ? rt->context : rt->local_ref_cap;
+        L.splits = L.full ? std::max(32, (ref_cap + 255) / 256) : std::max(1, (ref_cap + 63) / 64);
+        L.per_max = attention_per_max(ref_cap, L.splits);
         max_splits = std::max(max_splits, L.splits);
         const size_t n = size_t(L.cap) * c.kv_heads * 128;
         if (rt->dalloc(L.keys, n) || rt->dalloc(L.values, n)) return 1;
@@ -970,7 +986,7 @@ static int setup_runtime(plamo_runtime* rt, const ModelFiles* mf, bool upload, s
         rt->cache.stride.push_back(0);
     }
     std::vector<uint32_t> lo, gl;
-    const int local_rows = std::min(rt->context, c.window + 16);  // Runtime.swift:266
+    const int local_rows = std::min(rt->context, c.window + 16);  // Runtime.swift:266 (window-relative rows)
     build_rope(c, mf->inv_local, mf->inv_full, local_rows, rt->context, lo, gl);
     if (rt->dalloc(rt->rope_local, lo.size()) || rt->dalloc(rt->rope_global, gl.size())) return 1;
     CK(cudaMemcpy(rt->rope_local, lo.data(), lo.size() * 4, cudaMemcpyHostToDevice));
@@ -1251,14 +1267,35 @@ int plamo_dims(const plamo_runtime* rt, int32_t out[10]) {
     return 0;
 }
 
+// Copies one layer's cache of one lane in the reference's ring layout: a local layer's physical
+// ring (local_cap slots) is shown as the reference's ring of local_ref_cap slots, key position k of
+// the last local_ref_cap positions before `position` at slot k % local_ref_cap (zeros elsewhere).
+static int copy_kv_view(const plamo_runtime& rt, const Layer& L, const uint16_t* dk, const uint16_t* dv, int position,
+                        uint16_t* keys, uint16_t* values) {
+    const size_t row = size_t(rt.c.kv_heads) * 128;
+    const int phys = L.cap, ref = L.full ? L.cap : rt.local_ref_cap;
+    if (phys == ref) {
+        CK(cudaMemcpy(keys, dk, size_t(phys) * row * 2, cudaMemcpyDeviceToHost));
+        CK(cudaMemcpy(values, dv, size_t(phys) * row * 2, cudaMemcpyDeviceToHost));
+        return 0;
+    }
+    std::vector<uint16_t> hk(size_t(phys) * row), hv(size_t(phys) * row);
+    CK(cudaMemcpy(hk.data(), dk, hk.size() * 2, cudaMemcpyDeviceToHost));
+    CK(cudaMemcpy(hv.data(), dv, hv.size() * 2, cudaMemcpyDeviceToHost));
+    std::fill(keys, keys + size_t(ref) * row, uint16_t(0));
+    std::fill(values, values + size_t(ref) * row, uint16_t(0));
+    for (int k = std::max(0, position - ref); k < position; k++) {
+        std::copy_n(hk.data() + size_t(k % phys) * row, row, keys + size_t(k % ref) * row);
+        std::copy_n(hv.data() + size_t(k % phys) * row, row, values + size_t(k % ref) * row);
+    }
+    return 0;
+}
+
 int plamo_debug_kv(plamo_runtime* rt, int layer, uint16_t* keys, uint16_t* values) {
     if (!rt || layer < 0 || layer >= rt->c.layers) return fail("Invalid layer");
     CK(cudaSetDevice(rt->device));
     const Layer& L = rt->layers[layer];
-    const size_t n = size_t(L.cap) * rt->c.kv_heads * 128 * 2;
-    CK(cudaMemcpy(keys, L.keys, n, cudaMemcpyDeviceToHost));
-    CK(cudaMemcpy(values, L.values, n, cudaMemcpyDeviceToHost));
-    return 0;
+    return copy_kv_view(*rt, L, L.keys, L.values, rt->position, keys, values);
 }
 
 // ---- Batch ---------------------------------------------------------------------------------------
@@ -1390,9 +1427,9 @@ int plamo_batch_debug_kv(plamo_batch* b, int layer, int lane, uint16_t* keys, ui
     if (!b || layer < 0 || layer >= b->rt->c.layers || lane < 0 || lane >= b->lanes) return fail("Invalid layer or lane");
     CK(cudaSetDevice(b->rt->device));
     const long long stride = b->cache.stride[layer];
-    CK(cudaMemcpy(keys, b->cache.keys[layer] + size_t(lane) * stride, size_t(stride) * 2, cudaMemcpyDeviceToHost));
-    CK(cudaMemcpy(values, b->cache.values[layer] + size_t(lane) * stride, size_t(stride) * 2, cudaMemcpyDeviceToHost));
-    return 0;
+    const int position = lane < int(b->positions.size()) ? b->positions[lane] : 0;
+    return copy_kv_view(*b->rt, b->rt->layers[layer], b->cache.keys[layer] + size_t(lane) * stride,
+                        b->cache.values[layer] + size_t(lane) * stride, position, keys, values);
 }
 
 // decodeBatch + Batch.generate (BatchDecode.swift:8-47)

@@ -1,8 +1,9 @@
 """BASELINE configs 4 and 5a under parity: the batch4 ring wrap at the reference dims, and the
 32k-context long-sequence path (global layers over the full history, split-K flash-decode).
 
-C4 (Batch.swift:40,116-128; Runtime.swift:239-247): four lanes whose prompts nearly fill the
-2,064-slot local ring, so every lane's ring wraps within the first decoded steps. Every lane's
+C4 (Batch.swift:40,116-128; Runtime.swift:239-247): four lanes whose prompts overrun the
+2,064-slot local ring and nearly fill the library's longer physical ring, so both wrap within the
+first decoded steps. Every lane's
 logits after every batched step must equal the scalar runtime's bit for bit (the scalar path is
 itself bit-identical to the CPU restatement), and lane 0 is also checked against the restatement
 directly across the wrap.
@@ -32,9 +33,11 @@ def bits(a):
 
 
 def test_c4_batch4_rings_wrap_at_reference_dims(cuda, pkg, oracle, reference_dir):
-    lens = [2040, 2046, 2052, 2058]
-    steps = 40  # positions reach 2080-2098: every local ring (2,064 slots) wraps
-    context = 2200
+    lens = [2550, 2556, 2562, 2568]
+    # positions reach 2590-2608: past the reference's 2,064-slot local ring and past the library's
+    # own ring of window + 512 = 2,560 slots, so both wrap during the batched steps
+    steps = 40
+    context = 2624
     prompts = [pkg.synthetic.seeded_tokens(n, 107520, seed=40 + i) for i, n in enumerate(lens)]
     rt = pkg.Runtime(reference_dir, context=context)
     # the scalar runtime, lane by lane: greedy ids and every step's logits
