@@ -2,7 +2,7 @@
 // k_attn_partial + k_attn_merge (kernels.cu, Kernels.metal:301-562), with the scores and P.V of a
 // split as tcgen05 MMAs instead of one CUDA-core pass per query row.
 //
-// A CTA takes 8 query tokens of one forward call and one key split (up to ATC_SPAN keys of the
+// A CTA takes 8 query tokens of one forward call and one key split (up to `span` keys of the
 // window). With one KV head (MQA) the 8 tokens x 16 heads are 128 MMA rows that share every key:
 // row r = token * 16 + head, one tensor-memory lane each. Per 256-key chunk of the split:
 //   - the chunk's keys are staged in shared memory (local layers re-rotated with the window-relative
@@ -36,7 +36,7 @@ constexpr int ATC_H = 16;         // query heads (one KV head)
 constexpr int ATC_CH = 256;       // keys per staged chunk
 constexpr int ATC_KT = 64;        // keys per S tile (MMA N) and per P.V step (MMA K)
 constexpr int ATC_THREADS = 256;  // two threads per MMA row / tensor-memory lane (column halves)
-constexpr int ATC_SPAN = 2048;    // keys of one split (one partial per row and split)
+constexpr int ATC_SPLITS = 8;     // target key splits per row (span = cache / 8, >= one chunk)
 
 // shared-memory layout (offsets from a 1024-byte aligned base)
 constexpr uint32_t OFF_Q = 0;                        // 2 k-blocks x [128 rows][64] bf16
@@ -82,7 +82,7 @@ __device__ __forceinline__ float rope_fast(float x, float other, bool low, uint3
 constexpr float ATC_LOG2E = 1.4426950408889634f;
 constexpr float ATC_LN2 = 0.6931471805599453f;
 
-__global__ void __launch_bounds__(ATC_THREADS, 1) k_attn_tc(AttnArgs a, int* error) {
+__global__ void __launch_bounds__(ATC_THREADS, 1) k_attn_tc(AttnArgs a, int span, int* error) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
     uint64_t* bar_s = reinterpret_cast<uint64_t*>(smem + OFF_CTL);
@@ -131,7 +131,7 @@ __global__ void __launch_bounds__(ATC_THREADS, 1) k_attn_tc(AttnArgs a, int* err
             if (!((done >> i) & 1u) && o.lane == L.lane && o.first == L.first && o.count == L.count) run |= 1u << i;
         }
         done |= run;
-        const int k_lo = s * ATC_SPAN, k_hi = min(k_lo + ATC_SPAN, L.count);
+        const int k_lo = s * span, k_hi = min(k_lo + span, L.count);
         int klo = 1 << 30, khi = 0;
         for (int i = 0; i < ntok; i++)
             if ((run >> i) & 1u) {
@@ -415,18 +415,30 @@ bool attention_tc_supported(const AttnArgs& a) {
            (a.full || (reinterpret_cast<uintptr_t>(a.rope_local) & 15) == 0);
 }
 
-int attention_tc_splits(int cap) { return (cap + ATC_SPAN - 1) / ATC_SPAN; }
+// Keys per split: about an eighth of the cache, in whole 256-key chunks, so short prompts spread
+// over more CTAs and long ones keep the partials (and the merge's reads) few.
+static int attention_tc_span(int cap) {
+    const int span = ((cap + ATC_SPLITS - 1) / ATC_SPLITS + ATC_CH - 1) / ATC_CH * ATC_CH;
+    return span < ATC_CH ? ATC_CH : span;
+}
+
+int attention_tc_splits(int cap) {
+    const int span = attention_tc_span(cap);
+    return (cap + span - 1) / span;
+}
 
 cudaError_t configure_attention_tc() {
     return cudaFuncSetAttribute(k_attn_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, int(ATC_SMEM));
 }
 
-// a.splits must be attention_tc_splits(a.cap) (the partial buffers hold that many splits per row).
+// a.splits must be attention_tc_splits(keys), keys = a.key_bound (or a.cap when 0): the partial
+// buffers hold that many splits per row.
 cudaError_t launch_attention_tc(const AttnArgs& a, cudaStream_t s) {
-    if (!attention_tc_supported(a) || a.splits != attention_tc_splits(a.cap)) return cudaErrorInvalidValue;
+    const int keys = a.key_bound > 0 && a.key_bound < a.cap ? a.key_bound : a.cap;
+    if (!attention_tc_supported(a) || a.splits != attention_tc_splits(keys)) return cudaErrorInvalidValue;
     int* error = gemm_error_word(true);
     if (!error) return cudaErrorInvalidDevice;
-    k_attn_tc<<<dim3(a.splits, (a.rows + ATC_TOK - 1) / ATC_TOK), ATC_THREADS, ATC_SMEM, s>>>(a, error);
+    k_attn_tc<<<dim3(a.splits, (a.rows + ATC_TOK - 1) / ATC_TOK), ATC_THREADS, ATC_SMEM, s>>>(a, attention_tc_span(keys), error);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     return launch_attention_merge(a, s);

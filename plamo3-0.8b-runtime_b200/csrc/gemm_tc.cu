@@ -28,6 +28,8 @@
 #include "mbarrier.cuh"
 #include "tcgen05.cuh"
 
+#include <cstdlib>
+
 namespace plamo {
 
 namespace {
@@ -229,6 +231,205 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     }
 }
 
+// Persistent form for calls with a tile for every SM and no K split (prefill): one CTA per SM walks
+// the tiles (tile = m-tile * n-tiles + n-tile, so the CTAs running together share weight tiles in
+// L2) with its roles in separate warps: warp 0 issues the TMA copies into a ring of stages that
+// runs on across tiles, warp 1 issues the MMAs into one of two tensor-memory accumulators, and
+// warps 2-5 drain the other accumulator (the previous tile) meanwhile, so a tile's epilogue no
+// longer sits between two tiles' main loops. Same epilogues and results as k_gemm_tc.
+constexpr int TCP_THREADS = 192;
+
+template <int BN, int MODE>
+__global__ void __launch_bounds__(TCP_THREADS, 1)
+    k_gemm_tcp(GemvArgs a, const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmw, int* error) {
+    using T = TcTile<BN>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + T::STAGES * T::STAGE);
+    uint64_t* empty = full + T::STAGES;
+    uint64_t* tfull = empty + T::STAGES;  // [2] accumulator b holds a finished tile
+    uint64_t* tempty = tfull + 2;         // [2] accumulator b was drained by the epilogue warps
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+    volatile int* stop = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    volatile int* ep_abort = reinterpret_cast<volatile int*>(smem + T::STAGES * T::STAGE + 192);  // [2]
+    float* xg = reinterpret_cast<float*>(smem + T::STAGES * T::STAGE + 256);  // SwiGLU exchange
+    float* xu = xg + 64 * 9;
+
+    const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+    const int M = a.lin.M, Mout = MODE == GEMV_SWIGLU ? M / 2 : M;
+    const int per = MODE == GEMV_SWIGLU ? TC_BM / 2 : TC_BM;
+    const int nn = (a.rows + BN - 1) / BN, nkb = a.lin.K / TC_BK;
+    const int ntiles = ((Mout + per - 1) / per) * nn;
+
+    if (t == 0) {
+        for (int i = 0; i < T::STAGES; i++) {
+            bar_init(&full[i], 1);
+            bar_init(&empty[i], 1);
+        }
+        for (int b = 0; b < 2; b++) {
+            bar_init(&tfull[b], 1);
+            bar_init(&tempty[b], 4);
+        }
+        *stop = 0;
+        ep_abort[0] = ep_abort[1] = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncwarp();
+    if (warp == 1) tmem_alloc(tmem_slot, 2 * BN);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        int issued = 0;
+        if (lane == 0) {
+            int g = 0;
+            for (int tile = blockIdx.x; tile < ntiles && !*stop; tile += gridDim.x) {
+                const int m0 = (tile / nn) * per, n0 = (tile % nn) * BN;
+                for (int i = 0; i < nkb; i++, g++) {
+                    const int s = g % T::STAGES;
+                    if (g >= T::STAGES && !bar_wait(&empty[s], uint32_t((g / T::STAGES) & 1) ^ 1u)) {
+                        atomicCAS(error, 0, 4);
+                        *stop = 1;
+                        break;
+                    }
+                    uint8_t* st = smem + s * T::STAGE;
+                    const int kx = i * TC_BK;
+                    bar_expect(&full[s], T::STAGE);
+                    if (MODE == GEMV_SWIGLU) {
+                        tma2(st, &tmw, kx, m0, &full[s]);
+                        tma2(st + T::A_BYTES / 2, &tmw, kx, Mout + m0, &full[s]);
+                    } else {
+                        tma2(st, &tmw, kx, m0, &full[s]);
+                    }
+                    tma2(st + T::A_BYTES, &tmx, kx, n0, &full[s]);
+                    issued = g + 1;
+                }
+            }
+            // copies issued into this CTA's shared memory land before it exits (only an aborted
+            // step leaves some unconsumed)
+            for (int i = issued - T::STAGES < 0 ? 0 : issued - T::STAGES; i < issued; i++)
+                bar_wait(&full[i % T::STAGES], uint32_t(i / T::STAGES) & 1u);
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        if (lane == 0) {
+            const uint32_t idesc = tc_idesc(BN);
+            int g = 0, local = 0;
+            for (int tile = blockIdx.x; tile < ntiles && !*stop; tile += gridDim.x, local++) {
+                const int b = local & 1;
+                if (local >= 2 && !bar_wait(&tempty[b], uint32_t(((local >> 1) - 1) & 1))) {
+                    atomicCAS(error, 0, 5);
+                    *stop = 1;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t acc = tmem + uint32_t(b * BN);
+                bool ok = true;
+                for (int i = 0; i < nkb; i++, g++) {
+                    const int s = g % T::STAGES;
+                    if (!bar_wait(&full[s], uint32_t(g / T::STAGES) & 1u)) {
+                        atomicCAS(error, 0, 6);
+                        *stop = 1;
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t sa = smem_addr(smem + s * T::STAGE), sb = sa + T::A_BYTES;
+#pragma unroll
+                    for (int kk = 0; kk < TC_BK / TC_UK; kk++)
+                        umma_bf16(acc, sw128_desc(sa + kk * 32), sw128_desc(sb + kk * 32), idesc, uint32_t(i | kk));
+                    umma_commit(&empty[s]);
+                }
+                umma_commit(&tfull[b]);  // also after an abort: the epilogue waits on it, bounded
+                if (!ok) break;
+            }
+        }
+        __syncwarp();
+    } else {
+        // epilogue warps 2-5: tensor-memory lane quarter warp % 4, one weight row per thread
+        const int q = warp & 3, row = q * 32 + lane;
+        const uint32_t lane_base = uint32_t(q * 32) << 16;
+        int local = 0;
+        for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, local++) {
+            const int b = local & 1;
+            const bool ok = bar_wait(&tfull[b], uint32_t(local >> 1) & 1u);
+            if (!ok) {
+                atomicCAS(error, 0, 7);
+                ep_abort[local & 1] = 1;
+            }
+            // the four epilogue warps take the same decision (they meet at named barriers): a slot
+            // per tile parity, only ever set, read by all after the barrier below; a slot is
+            // written again two tiles later, after every warp passed the next tile's barrier
+            asm volatile("bar.sync 1, 128;" ::: "memory");
+            if (ep_abort[local & 1]) break;
+            tc_fence_after();
+            const int m0 = (tile / nn) * per, n0 = (tile % nn) * BN;
+            const uint32_t acc = tmem + uint32_t(b * BN);
+            for (int c0 = 0; c0 < BN && n0 + c0 < a.rows; c0 += 16) {
+                uint32_t v[16];
+                tmem_ld16(acc + lane_base + uint32_t(c0), v);
+                if (MODE == GEMV_SWIGLU) {
+                    // gate rows in lanes 0-63, up rows in 64-127: quarters 0-1 finish columns
+                    // 0..7 of the 16, quarters 2-3 columns 8..15, each passing the other half
+                    const bool gate = q < 2;
+                    const int i = row & 63;
+#pragma unroll
+                    for (int j = 0; j < 8; j++) {
+                        if (gate) xg[i * 9 + j] = __uint_as_float(v[8 + j]);
+                        else xu[i * 9 + j] = __uint_as_float(v[j]);
+                    }
+                    asm volatile("bar.sync 1, 128;" ::: "memory");
+                    if (m0 + i < Mout) {
+#pragma unroll
+                        for (int j = 0; j < 8; j++) {
+                            const int col = gate ? j : 8 + j;
+                            const int r = n0 + c0 + col;
+                            if (r < a.rows) {
+                                const int orow = a.out_map ? a.out_map[r] : r;
+                                const float gv = gate ? __uint_as_float(v[j]) : xg[i * 9 + j];
+                                const float uv = gate ? xu[i * 9 + j] : __uint_as_float(v[8 + j]);
+                                a.y[size_t(orow) * a.ystride + m0 + i] = uint16_t(f2bf(swiglu(gv, uv)));
+                            }
+                        }
+                    }
+                    asm volatile("bar.sync 1, 128;" ::: "memory");
+                } else {
+                    const int m = m0 + row;
+#pragma unroll
+                    for (int j = 0; j < 16; j++) {
+                        const int r = n0 + c0 + j;
+                        const bool rok = r < a.rows, okm = rok && m < Mout;
+                        const int orow = rok ? (a.out_map ? a.out_map[r] : r) : 0;
+                        const uint32_t bits = f2bf(__uint_as_float(v[j]));
+                        if (okm) a.y[size_t(orow) * a.ystride + m] = uint16_t(bits);
+                        if (MODE == GEMV_LOGITS) {
+                            unsigned long long key = okm ? argmax_key(bf2f(bits), uint32_t(m)) : 0ull;
+#pragma unroll
+                            for (int o = 16; o > 0; o >>= 1) {
+                                const unsigned long long other = __shfl_xor_sync(FULL_MASK, key, o);
+                                key = other > key ? other : key;
+                            }
+                            if (lane == 0 && rok && key) atomicMax(a.keys + orow, key);
+                        }
+                    }
+                }
+            }
+            // this accumulator is drained: the MMA warp may reuse it (one arrival per warp)
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(&tempty[b])) : "memory");
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 2 * BN);
+    }
+}
+
 // Adds the split partials of one output in split order and applies the mode's epilogue.
 template <int MODE>
 __global__ void __launch_bounds__(256) k_gemm_tc_finish(GemvArgs a, int splits) {
@@ -295,12 +496,25 @@ TcDevice* tc_device() {
     return &t;
 }
 
+// PLAMO_TC_PERSISTENT=0 in the environment keeps every call on the one-tile-per-CTA kernel (A/B runs).
+bool tcp_enabled() {
+    static const bool on = [] {
+        const char* e = getenv("PLAMO_TC_PERSISTENT");
+        return !(e && e[0] == '0');
+    }();
+    return on;
+}
+
 template <int BN, int MODE>
 cudaError_t tc_launch(const GemvArgs& a, int splits, int tiles, TcDevice& dev, cudaStream_t s) {
     CUtensorMap tmx, tmw;
     if (!encode_kmajor(&tmx, a.x, a.rows, a.lin.K, BN) ||
         !encode_kmajor(&tmw, a.lin.w, a.lin.M, a.lin.K, MODE == GEMV_SWIGLU ? TC_BM / 2 : TC_BM))
         return cudaErrorInvalidValue;
+    if (splits == 1 && tiles > dev.sms && BN == 128 && tcp_enabled()) {  // persistent: more tiles than SMs
+        k_gemm_tcp<BN, MODE><<<dev.sms, TCP_THREADS, TcTile<BN>::SMEM + 5120, s>>>(a, tmx, tmw, dev.error);
+        return cudaGetLastError();
+    }
     k_gemm_tc<BN, MODE><<<tiles * splits, TC_THREADS, TcTile<BN>::SMEM, s>>>(a, tmx, tmw, splits, dev.error);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess || splits == 1) return e;
@@ -321,6 +535,14 @@ cudaError_t tc_mode(const GemvArgs& a, GemvMode mode, int splits, int tiles, TcD
 template <int BN>
 cudaError_t tc_attr() {
     cudaError_t e = cudaFuncSetAttribute(k_gemm_tc<BN, GEMV_PLAIN>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcTile<BN>::SMEM);
+    if (BN == 128) {
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(k_gemm_tcp<BN, GEMV_PLAIN>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcTile<BN>::SMEM + 5120);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(k_gemm_tcp<BN, GEMV_SWIGLU>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcTile<BN>::SMEM + 5120);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(k_gemm_tcp<BN, GEMV_LOGITS>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcTile<BN>::SMEM + 5120);
+    }
     if (e == cudaSuccess)
         e = cudaFuncSetAttribute(k_gemm_tc<BN, GEMV_SWIGLU>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcTile<BN>::SMEM);
     if (e == cudaSuccess)

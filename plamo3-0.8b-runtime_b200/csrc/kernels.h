@@ -51,6 +51,7 @@ struct AttnArgs {
     uint16_t* out = nullptr;           // [rows][H*128]
     long long lane_stride = 0;
     int rows = 1, H = 16, KV = 1, cap = 0, full = 0, splits = 1, per_max = 0;
+    int key_bound = 0;  // tensor-core attention: no row sees key index >= key_bound (0: cap)
 };
 
 struct QkvArgs {
@@ -112,7 +113,7 @@ cudaError_t launch_attention_merge(const AttnArgs& a, cudaStream_t s);
 // keys in attention_tc_splits(cap) splits; partials and merge as launch_attention, results within
 // rounding of it (tensor mode only).
 bool attention_tc_supported(const AttnArgs& a);
-int attention_tc_splits(int cap);
+int attention_tc_splits(int keys);  // keys: the cache capacity or a smaller bound on the rows' key counts
 cudaError_t launch_attention_tc(const AttnArgs& a, cudaStream_t s);
 cudaError_t configure_attention_tc();
 cudaError_t launch_finalize(unsigned long long* keys, const int* key_map, int rows, int* result,

@@ -357,6 +357,10 @@ static int enqueue_forward(plamo_runtime& rt, Work& w, int rows, const CacheView
     LAUNCH(K_NORM, launch_embed_norm(w.ids, rows, c.vocab, rt.embed, rt.layers[0].pre_mixer, c.d, w.x, w.h, nout ? o.keys : nullptr,
                                      w.out_map, nout, s));
     const float post_mlp_offset = float(1.0 / std::pow(5.0, 1.5));  // Runtime.swift:450
+    // chunked calls: no row's window counts more keys than its chunk's end (host descriptors)
+    int key_bound = 1;
+    if (chunked)
+        for (int r = 0; r < rows; r++) key_bound = std::max(key_bound, w.h_desc[r].cstart + w.h_desc[r].crows);
     GemvArgs tc;  // path selection shared by every projection of the pass
     tc.tensor = rt.tensor ? 1 : 0;
     tc.part = w.part_tc;
@@ -380,7 +384,10 @@ static int enqueue_forward(plamo_runtime& rt, Work& w, int rows, const CacheView
         const bool attn_tc = rt.tensor_attn && chunked && rows >= TC_MIN_ROWS && attention_tc_supported(a);
         // the tensor-core kernel splits each row's keys into fewer, wider splits: a launch takes as
         // many rows as the partial buffers hold at that split count
-        if (attn_tc) a.splits = attention_tc_splits(L.cap);
+        if (attn_tc) {
+            a.key_bound = std::min(L.cap, key_bound);
+            a.splits = attention_tc_splits(a.key_bound);
+        }
         const int per_launch = attn_tc ? int(std::max<long long>(1, w.att_row_splits / a.splits)) : w.att_rows;
         for (int r0 = 0; r0 < rows; r0 += per_launch) {
             AttnArgs b = a;
