@@ -45,13 +45,16 @@ struct TcTile {
     static constexpr int A_BYTES = TC_BM * 128;
     static constexpr int B_BYTES = BN * 128;
     static constexpr int STAGE = A_BYTES + B_BYTES;  // a multiple of 1024 (swizzle atoms stay aligned)
-    static constexpr int STAGES = BN == 128 ? 6 : (BN == 64 ? 4 : 5);
+    static constexpr int STAGES = BN == 256 ? 4 : BN == 128 ? 6 : (BN == 64 ? 4 : 5);
     static constexpr int SMEM = 1024 + STAGES * STAGE + 256;
 };
 
+// SwiGLU of the tensor-core epilogues (Kernels.metal:202-210 rounding points): the accumulation
+// order already differs from the exact path here, so the sigmoid takes the multi-function unit's
+// exponential and reciprocal (a few ulps of fp32, far below the bf16 roundings that follow).
 __device__ __forceinline__ float swiglu(float g, float u) {
     const float gq = rbf(g), uq = rbf(u);
-    return rbf(rbf(gq / (1.0f + pexp(-gq))) * uq);
+    return rbf(rbf(__fdividef(gq, 1.0f + __expf(-gq))) * uq);
 }
 
 template <int BN, int MODE>
@@ -505,13 +508,22 @@ bool tcp_enabled() {
     return on;
 }
 
+// PLAMO_TC_BN256=0 in the environment keeps the persistent kernel at 128-row tiles (A/B runs).
+bool bn256_enabled() {
+    static const bool on = [] {
+        const char* e = getenv("PLAMO_TC_BN256");
+        return !(e && e[0] == '0');
+    }();
+    return on;
+}
+
 template <int BN, int MODE>
 cudaError_t tc_launch(const GemvArgs& a, int splits, int tiles, TcDevice& dev, cudaStream_t s) {
     CUtensorMap tmx, tmw;
     if (!encode_kmajor(&tmx, a.x, a.rows, a.lin.K, BN) ||
         !encode_kmajor(&tmw, a.lin.w, a.lin.M, a.lin.K, MODE == GEMV_SWIGLU ? TC_BM / 2 : TC_BM))
         return cudaErrorInvalidValue;
-    if (splits == 1 && tiles > dev.sms && BN == 128 && tcp_enabled()) {  // persistent: more tiles than SMs
+    if (splits == 1 && tiles > dev.sms && BN >= 128 && tcp_enabled()) {  // persistent: more tiles than SMs
         k_gemm_tcp<BN, MODE><<<dev.sms, TCP_THREADS, TcTile<BN>::SMEM + 5120, s>>>(a, tmx, tmw, dev.error);
         return cudaGetLastError();
     }
@@ -535,7 +547,7 @@ cudaError_t tc_mode(const GemvArgs& a, GemvMode mode, int splits, int tiles, TcD
 template <int BN>
 cudaError_t tc_attr() {
     cudaError_t e = cudaFuncSetAttribute(k_gemm_tc<BN, GEMV_PLAIN>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcTile<BN>::SMEM);
-    if (BN == 128) {
+    if (BN >= 128) {
         if (e == cudaSuccess)
             e = cudaFuncSetAttribute(k_gemm_tcp<BN, GEMV_PLAIN>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcTile<BN>::SMEM + 5120);
         if (e == cudaSuccess)
@@ -556,6 +568,7 @@ cudaError_t configure_gemm_tc() {
     cudaError_t e = tc_attr<32>();
     if (e == cudaSuccess) e = tc_attr<64>();
     if (e == cudaSuccess) e = tc_attr<128>();
+    if (e == cudaSuccess) e = tc_attr<256>();
     return e;
 }
 
@@ -572,6 +585,11 @@ int gemm_tc_plan(const GemvArgs& a, GemvMode mode, int sms, int* bn_out, int* ti
     const int mtiles = (Mout + per - 1) / per, nkb = a.lin.K / TC_BK;
     int bn = a.rows <= 32 ? 32 : 64;
     if (a.rows > 64 && mtiles * ((a.rows + 127) / 128) >= sms) bn = 128;
+    // 256-row activation tiles (the persistent kernel) once they too leave no SM idle: each
+    // weight tile staged in shared memory then serves twice the rows (measured: down_proj over
+    // 4096 rows 105 -> 83 us, qkv 45 -> 36 us)
+    if (mode != GEMV_SWIGLU && a.rows >= 256 && mtiles * ((a.rows + 255) / 256) > sms && tcp_enabled() && bn256_enabled())
+        bn = 256;  // (SwiGLU tiles stay at 128 rows: their epilogue, not the loads, bounds them)
     const int tiles = mtiles * ((a.rows + bn - 1) / bn);
     // split K while the tiles leave SMs idle, each split keeps >= 4 stages of k, and the
     // partials fit the caller's workspace
@@ -600,7 +618,8 @@ cudaError_t launch_gemm_tc(const GemvArgs& a, GemvMode mode, cudaStream_t s, int
     switch (bn) {
         case 32: return tc_mode<32>(a, mode, splits, tiles, *dev, s);
         case 64: return tc_mode<64>(a, mode, splits, tiles, *dev, s);
-        default: return tc_mode<128>(a, mode, splits, tiles, *dev, s);
+        case 128: return tc_mode<128>(a, mode, splits, tiles, *dev, s);
+        default: return tc_mode<256>(a, mode, splits, tiles, *dev, s);
     }
 }
 
