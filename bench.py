@@ -314,6 +314,105 @@ def kernel_case(args):
     return 0
 
 
+def prefill_case(args):
+    """One 512-token prefill of BASELINE config 2 on one path (exact or tensor), after a warm-up
+    prefill: device time of the second. A short case for kernel profiles and launch lists."""
+    import torch
+    P = pkg()
+    model = ensure_model(Path(args.model_root), False, 0, None)
+    rt = P.Runtime(model, context=PROMPT + 16)
+    rt.set_tensor_gemm(args.prefill_case == "tensor")
+    prompt = P.synthetic.seeded_tokens(PROMPT, rt.vocab, seed=1)
+    rt.prefill(prompt)
+    rt.reset()
+    torch.cuda.synchronize()
+    g0 = rt.gpu_seconds
+    rt.prefill(prompt)
+    torch.cuda.synchronize()
+    print(json.dumps(dict(case="prefill", path=args.prefill_case, tokens=PROMPT, ms=1e3 * (rt.gpu_seconds - g0))), flush=True)
+    return 0
+
+
+def attention_case(args):
+    """plamo_k_attention_rows on chunked-prefill geometry (full,cap,p0,rows: rows consecutive
+    positions from p0 in 16-token chunks, a global layer when full else a local one with the
+    2,048-key window): CUDA-event time per call of the CUDA-core and the tensor-core kernels over
+    --steps calls after --warmup, on seeded random queries, keys and values."""
+    import numpy as np
+    import torch
+    R = pkg().runtime
+    full, cap, p0, rows = (int(v) for v in args.attention_case.split(","))
+    H, W = 16, 2048
+    geo, pos = [], p0
+    while len(geo) < rows:
+        cstart, n = pos, min(16, rows - len(geo))
+        for j in range(n):
+            p = cstart + j
+            if full:
+                geo.append((0, cstart + n, 0, p + 1))
+            else:
+                first = max(0, cstart - (W - 1))
+                end = p - first + 1
+                geo.append((first, cstart + n - first, max(0, end - W), end))
+        pos += n
+    g = torch.Generator().manual_seed(0)
+    keys = torch.randn(cap * 128, generator=g).bfloat16().cuda()
+    values = torch.randn(cap * 128, generator=g).bfloat16().cuda()
+    q = torch.randn(rows * H * 128, generator=g).bfloat16().cuda()
+    inv = torch.tensor([1e4 ** (-2 * i / 128) for i in range(64)], dtype=torch.float64)
+    ang = (torch.arange(2064, dtype=torch.float64)[:, None] * inv[None, :]).float().double()
+    cs = torch.cos(ang).float().bfloat16().view(torch.int16).int() & 0xFFFF
+    sn = torch.sin(ang).float().bfloat16().view(torch.int16).int() & 0xFFFF
+    table = (cs | (sn << 16)).cuda()
+    tgeo = torch.tensor(np.array(geo, dtype=np.int32)).cuda()
+    out = torch.zeros(rows * H * 128, dtype=torch.bfloat16, device="cuda")
+    splits = max(32, (cap + 255) // 256) if full else (min(cap, 2064) + 63) // 64
+    ws = torch.zeros(rows * max(splits, 16) * H * (128 * 4 + 8) + rows * 16 + (1 << 20), dtype=torch.uint8, device="cuda")
+    res = dict(case=dict(full=full, cap=cap, p0=p0, rows=rows, exact_splits=splits))
+    for name, tensor in (("exact", 0), ("tensor", 1)):
+        fn = lambda: R.k_attention_rows(q.data_ptr(), keys.data_ptr(), values.data_ptr(), H, 1, cap, tgeo.data_ptr(), rows,
+                                        full, table.data_ptr(), splits, tensor, out.data_ptr(), ws.data_ptr(), ws.numel())
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        res[name] = dict(us=e0.elapsed_time(e1) * 1e3 / args.steps)
+    print(json.dumps(res), flush=True)
+    return 0
+
+
+def select_case(args):
+    """plamo_k_select (Sampler.select on the device) over a reference-size vocabulary of seeded
+    random logits with a 256-token history: CUDA-event time per call."""
+    import torch
+    R = pkg().runtime
+    V = 107520
+    g = torch.Generator().manual_seed(0)
+    logits = torch.randn(V, generator=g).bfloat16().cuda()
+    hist = torch.randint(0, V, (256,), generator=g, dtype=torch.int32).cuda()
+    counts = torch.zeros(V, dtype=torch.int32, device="cuda")
+    flags = torch.zeros(V, dtype=torch.uint8, device="cuda")
+    key = torch.zeros(1, dtype=torch.int64, device="cuda")
+    fn = lambda: R.k_select(logits.data_ptr(), V, hist.data_ptr(), 256, 1.3, 3, 0.2, 0.1, counts.data_ptr(),
+                            flags.data_ptr(), key.data_ptr())
+    for _ in range(args.warmup):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    print(json.dumps(dict(case="select", vocab=V, history=256, us=e0.elapsed_time(e1) * 1e3 / args.steps)), flush=True)
+    return 0
+
+
 def measure_batch4(P, model, local, dist, args, pk, wbytes):
     """four independent 512-token segments (seeds 2000 + lane) prefilled
     together, then 2,048 batched greedy steps each, so every lane's 2,064-slot local ring wraps
@@ -445,6 +544,11 @@ def main():
     ap.add_argument("--job-steps", type=int, default=512, help="config 5b greedy tokens per segment")
     ap.add_argument("--kernel-case", default=None,
                     help="rows,K,M,mode: time one projection on the tcgen05 GEMM and the exact GEMM, then exit")
+    ap.add_argument("--prefill-case", default=None, choices=["exact", "tensor"],
+                    help="one 512-token prefill on that path after a warm-up, then exit (profiles)")
+    ap.add_argument("--attention-case", default=None,
+                    help="full,cap,p0,rows: time the multi-row attention kernels, then exit")
+    ap.add_argument("--select-case", action="store_true", help="time the device sampler, then exit")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -452,6 +556,12 @@ def main():
         return run_reference(args)
     if args.kernel_case:
         return kernel_case(args)
+    if args.prefill_case:
+        return prefill_case(args)
+    if args.attention_case:
+        return attention_case(args)
+    if args.select_case:
+        return select_case(args)
 
     import torch
     world = int(os.environ.get("WORLD_SIZE", "1"))
