@@ -135,7 +135,7 @@ def ensure_model(root: Path, packed: bool, rank: int, dist) -> Path:
             P.synthetic.write_model(d, P.synthetic.REFERENCE, seed=0)
             (d / ".ready").write_text("ok")
         if packed:
-            P.packing.write_p12(d)
+            P.runtime.pack_p12(d)  # the library's C++ writer: pack_weights.py's archive bytes
             marker.write_text("ok")
     if dist is not None:
         dist.barrier()
@@ -446,6 +446,43 @@ def measure_batch4(P, model, local, dist, args, pk, wbytes):
                 path="order-exact CUDA-core projections (bit-identical to the restatement); one weight pass per step")
 
 
+def measure_packed(P, root, local, rank, dist, args, pk, prompt):
+    """the C2 decode from the lossless .p12 archive (the library's C++ packer
+    writes it from the same weights; Packed.swift:12-91, Kernels.metal:23-44). Device-chained
+    greedy steps after the 512-token prefill, CUDA events, max over ranks; roofline of the
+    persistent kernel against the archive's streamed bytes (data regions + block tables)."""
+    import torch
+    d = ensure_model(root, True, rank, dist)
+    steps = args.packed_steps
+    rt = P.Runtime(d, context=PROMPT + args.warmup + steps + args.profile_steps + 16, packed=True, device=local)
+    rt.prefill(prompt)
+    rt.decode_chain(args.warmup)
+    if dist: dist.barrier()
+    torch.cuda.synchronize()
+    g0 = rt.gpu_seconds
+    rt.decode_chain(steps)
+    torch.cuda.synchronize()
+    t = torch.tensor([rt.gpu_seconds - g0], device="cuda", dtype=torch.float64)
+    if dist: dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    elapsed = float(t.item())
+    prof = rt.profile_decode(args.profile_steps)
+    rt.close()
+    key = "persistent" if "persistent" in prof else "gemv"
+    pbytes = linear_bytes(d, True)
+    per_launch_bytes = pbytes * args.profile_steps / max(1, prof[key]["launches"])
+    per_launch_s = prof[key]["ms"] * 1e-3 / max(1, prof[key]["launches"])
+    achieved = per_launch_bytes / per_launch_s / 1e9
+    tf = REPO / "profiles" / f"{key}_decode_traffic_p12.json"
+    traffic = json.loads(tf.read_text()).get("dram_bytes_per_launch") if tf.exists() else None
+    world = dist.get_world_size() if dist else 1
+    return dict(steps=steps, tok_s=aggregate_rate(steps, world, elapsed), ms_per_step=1e3 * elapsed / steps,
+                bytes_per_token=pbytes,
+                roofline=dict(bound="hbm", kernel="k_decode_mega<packed>" if key == "persistent" else "k_gemv<packed>",
+                              achieved=achieved, peak=pk["hbm"], unit="GB/s", frac=achieved / pk["hbm"],
+                              traffic=traffic, bytes_per_launch=per_launch_bytes, launch_us=per_launch_s * 1e6),
+                path="persistent decode from the .p12 archive, decoded in registers (ids identical to bf16)")
+
+
 def measure_long(P, model, local, dist, args, pk, wbytes):
     """BASELINE config 5a: one 28,672-token prompt in a 32,768-token context (global layers keep
     the full history; split-K flash-decode), prefilled on the order-exact path and on the tcgen05
@@ -538,6 +575,7 @@ def main():
     ap.add_argument("--segment-lanes", type=int, default=32)
     ap.add_argument("--segment-steps", type=int, default=32)
     ap.add_argument("--prefill-reps", type=int, default=5)
+    ap.add_argument("--packed-steps", type=int, default=1024, help="config 3 (.p12) decode steps (0: skip)")
     ap.add_argument("--batch4-steps", type=int, default=2048, help="config 4 decode steps per lane (0: skip)")
     ap.add_argument("--long-prompt", type=int, default=28672, help="config 5a prompt tokens (0: skip)")
     ap.add_argument("--job-segments", type=int, default=256, help="config 5b segments in the fixed job (0: skip)")
@@ -712,6 +750,8 @@ def main():
                        "last-row lm_head; tensor_frac against the measured bf16 burst peak")
         prt.close()
 
+    packed = (measure_packed(P, Path(args.model_root), local, rank, dist, args, pk, prompt)
+              if args.packed_steps > 0 and not args.packed else None)
     job = measure_segment_job(P, model, local, rank, world, dist, args, pk, wbytes) if args.job_segments > 0 else None
     b4 = measure_batch4(P, model, local, dist, args, pk, wbytes) if args.batch4_steps > 0 else None
     long_ctx = measure_long(P, model, local, dist, args, pk, wbytes) if args.long_prompt > 0 else None
@@ -750,6 +790,8 @@ def main():
             line["segments_tensor"] = seg_tc
         if pre:
             line["prefill"] = pre
+        if packed:
+            line["packed"] = packed
         if job:
             line["segments_job"] = job
         if b4:
