@@ -199,7 +199,17 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
     return red[8];
 }
 
-__device__ __forceinline__ void norm_row(const float (&v)[NPT], int n, const uint16_t* w, float offset, float* red,
+// The factors bf16(w + offset) of a norm row, read before the row's reduction so their load
+// latency overlaps it.
+__device__ __forceinline__ void norm_factors(const uint16_t* w, int n, float offset, float (&f)[NPT]) {
+#pragma unroll
+    for (int j = 0; j < NPT; j++) {
+        const int i = threadIdx.x + j * 256;
+        f[j] = i < n ? rbf(bf2f(w[i]) + offset) : 0.f;
+    }
+}
+
+__device__ __forceinline__ void norm_row(const float (&v)[NPT], int n, const float (&f)[NPT], float* red,
                                          float (&z)[NPT]) {
     float ss = 0.f;
 #pragma unroll
@@ -209,20 +219,27 @@ __device__ __forceinline__ void norm_row(const float (&v)[NPT], int n, const uin
 #pragma unroll
     for (int j = 0; j < NPT; j++) {
         const int i = threadIdx.x + j * 256;
-        z[j] = i < n ? rbf(rbf(v[j] * scale) * rbf(bf2f(w[i]) + offset)) : 0.f;
+        z[j] = i < n ? rbf(rbf(v[j] * scale) * f[j]) : 0.f;
     }
 }
 
+// Every global read of the row (source, norm weights, residual row, next norm weights) is issued
+// before the first reduction, so a row pays one memory latency instead of one per stage; the
+// arithmetic and its order are unchanged.
 __global__ void __launch_bounds__(256) k_norm(NormArgs a) {
     __shared__ float red[9];
     const int r = blockIdx.x;
-    float v[NPT], z[NPT];
+    const size_t row = size_t(r) * a.n;
+    float v[NPT], z[NPT], f[NPT], xr[NPT], g[NPT];
 #pragma unroll
     for (int j = 0; j < NPT; j++) {
         const int i = threadIdx.x + j * 256;
-        v[j] = i < a.n ? bf2f(a.src[size_t(r) * a.n + i]) : 0.f;
+        v[j] = i < a.n ? bf2f(a.src[row + i]) : 0.f;
+        xr[j] = a.residual && i < a.n ? bf2f(a.x[row + i]) : 0.f;
     }
-    norm_row(v, a.n, a.w, a.offset, red, z);
+    norm_factors(a.w, a.n, a.offset, f);
+    if (a.next_w) norm_factors(a.next_w, a.n, 1.0f, g);
+    norm_row(v, a.n, f, red, z);
     if (!a.residual) {
         const int orow = a.out_map ? a.out_map[r] : r;
 #pragma unroll
@@ -230,7 +247,7 @@ __global__ void __launch_bounds__(256) k_norm(NormArgs a) {
             const int i = threadIdx.x + j * 256;
             if (i < a.n) {
                 const uint16_t b = uint16_t(f2bf(z[j]));
-                a.x[size_t(r) * a.n + i] = b;
+                a.x[row + i] = b;
                 if (a.y2) a.y2[size_t(orow) * a.n + i] = b;
             }
         }
@@ -240,19 +257,19 @@ __global__ void __launch_bounds__(256) k_norm(NormArgs a) {
     for (int j = 0; j < NPT; j++) {
         const int i = threadIdx.x + j * 256;
         if (i < a.n) {
-            const float val = rbf(bf2f(a.x[size_t(r) * a.n + i]) + z[j]);
-            a.x[size_t(r) * a.n + i] = uint16_t(f2bf(val));
+            const float val = rbf(xr[j] + z[j]);
+            a.x[row + i] = uint16_t(f2bf(val));
             v[j] = val;
         } else {
             v[j] = 0.f;
         }
     }
     if (!a.next_w) return;
-    norm_row(v, a.n, a.next_w, 1.0f, red, z);
+    norm_row(v, a.n, g, red, z);
 #pragma unroll
     for (int j = 0; j < NPT; j++) {
         const int i = threadIdx.x + j * 256;
-        if (i < a.n) a.next[size_t(r) * a.n + i] = uint16_t(f2bf(z[j]));
+        if (i < a.n) a.next[row + i] = uint16_t(f2bf(z[j]));
     }
 }
 
@@ -269,7 +286,7 @@ __global__ void __launch_bounds__(256) k_embed_norm(const int* ids, int vocab, c
     // range unless every logit was NaN, in which case row 0 is read instead of faulting.
     const int id = ids[r];
     const size_t row = size_t(id >= 0 && id < vocab ? id : 0) * d;
-    float v[NPT], z[NPT];
+    float v[NPT], z[NPT], f[NPT];
 #pragma unroll
     for (int j = 0; j < NPT; j++) {
         const int i = threadIdx.x + j * 256;
@@ -277,7 +294,8 @@ __global__ void __launch_bounds__(256) k_embed_norm(const int* ids, int vocab, c
         if (i < d) { b = embed[row + i]; x[size_t(r) * d + i] = b; }
         v[j] = bf2f(b);
     }
-    norm_row(v, d, w, 1.0f, red, z);
+    norm_factors(w, d, 1.0f, f);
+    norm_row(v, d, f, red, z);
 #pragma unroll
     for (int j = 0; j < NPT; j++) {
         const int i = threadIdx.x + j * 256;
@@ -498,40 +516,83 @@ __global__ void __launch_bounds__(256) k_attn_partial(AttnArgs a) {
     }
 }
 
-// Splits are taken in order, eight at a time: their statistics and partials are loaded together
-// before the dependent max / fma chains run over them.
-__global__ void __launch_bounds__(128) k_attn_merge(AttnArgs a) {
-    const int r = blockIdx.x / a.H, h = blockIdx.x - r * a.H, d = threadIdx.x;
-    const float2* ml = a.part_ml + size_t(r) * a.splits * a.H;
-    const float* po = a.part_o + size_t(r) * a.splits * a.H * 128 + h * 128 + d;
-    const size_t po_split = size_t(a.H) * 128;
-    float M = -INFINITY;
-    for (int s0 = 0; s0 < a.splits; s0 += 8) {
-        float m[8];
+// One thread per 8 consecutive outputs of one (row, head): split statistics and 16-byte partial
+// loads. Up to eight splits are loaded in one round trip and then folded; more splits are taken
+// eight at a time (their maxima first, then the sums). Either way the max runs over the splits in
+// order and the sum and P.V chains add the splits in order, as the single-pass form did.
+constexpr int MERGE_DIMS = 8;
+
+__device__ __forceinline__ void merge_fold(const float2 (&st)[8], const float4 (&pa)[8], const float4 (&pb)[8], int n,
+                                           float M, float& L, float (&o)[MERGE_DIMS]) {
 #pragma unroll
-        for (int j = 0; j < 8; j++) m[j] = s0 + j < a.splits ? ml[(s0 + j) * a.H + h].x : -INFINITY;
+    for (int j = 0; j < 8; j++) {
+        if (j < n && st[j].y > 0.f) {
+            const float w = pexp(st[j].x - M);
+            L = fmaf(w, st[j].y, L);
+            const float pv[MERGE_DIMS] = {pa[j].x, pa[j].y, pa[j].z, pa[j].w, pb[j].x, pb[j].y, pb[j].z, pb[j].w};
 #pragma unroll
-        for (int j = 0; j < 8; j++) M = fmaxf(M, m[j]);
-    }
-    float L = 0.f, o = 0.f;
-    for (int s0 = 0; s0 < a.splits; s0 += 8) {
-        float2 st[8];
-        float pv[8];
-#pragma unroll
-        for (int j = 0; j < 8; j++) {
-            st[j] = s0 + j < a.splits ? ml[(s0 + j) * a.H + h] : make_float2(-INFINITY, 0.f);
-            pv[j] = s0 + j < a.splits ? po[(s0 + j) * po_split] : 0.f;  // used only when the split had keys
+            for (int k = 0; k < MERGE_DIMS; k++) o[k] = fmaf(pv[k], w, o[k]);
         }
+    }
+}
+
+__global__ void __launch_bounds__(256) k_attn_merge(AttnArgs a) {
+    const int per_row = (a.H * (128 / MERGE_DIMS) + 255) / 256;
+    const int r = blockIdx.x / per_row;
+    const int idx = (blockIdx.x - r * per_row) * 256 + threadIdx.x;
+    if (idx >= a.H * (128 / MERGE_DIMS)) return;
+    const int h = idx / (128 / MERGE_DIMS), d0 = (idx % (128 / MERGE_DIMS)) * MERGE_DIMS;
+    const float2* ml = a.part_ml + size_t(r) * a.splits * a.H + h;  // split s at ml[s * H]
+    const float* po = a.part_o + size_t(r) * a.splits * a.H * 128 + h * 128 + d0;
+    const size_t po_split = size_t(a.H) * 128;
+    float M = -INFINITY, L = 0.f, o[MERGE_DIMS];
+#pragma unroll
+    for (int k = 0; k < MERGE_DIMS; k++) o[k] = 0.f;
+    float2 st[8];
+    float4 pa[8], pb[8];
+    auto load = [&](int s0) {
 #pragma unroll
         for (int j = 0; j < 8; j++) {
-            if (st[j].y > 0.f) {
-                const float w = pexp(st[j].x - M);
-                L = fmaf(w, st[j].y, L);
-                o = fmaf(pv[j], w, o);
+            if (s0 + j < a.splits) {
+                st[j] = ml[size_t(s0 + j) * a.H];
+                // partials are read whether or not the split had keys; only splits with keys use them
+                const float4* q = reinterpret_cast<const float4*>(po + (s0 + j) * po_split);
+                pa[j] = q[0];
+                pb[j] = q[1];
+            } else {
+                st[j] = make_float2(-INFINITY, 0.f);
             }
         }
+    };
+    if (a.splits <= 8) {
+        load(0);
+#pragma unroll
+        for (int j = 0; j < 8; j++) M = fmaxf(M, st[j].x);
+        merge_fold(st, pa, pb, a.splits, M, L, o);
+    } else {
+        for (int s0 = 0; s0 < a.splits; s0 += 8) {
+            float m[8];
+#pragma unroll
+            for (int j = 0; j < 8; j++) m[j] = s0 + j < a.splits ? ml[size_t(s0 + j) * a.H].x : -INFINITY;
+#pragma unroll
+            for (int j = 0; j < 8; j++) M = fmaxf(M, m[j]);
+        }
+        for (int s0 = 0; s0 < a.splits; s0 += 8) {
+            load(s0);
+            merge_fold(st, pa, pb, a.splits - s0, M, L, o);
+        }
     }
-    a.out[size_t(r) * a.H * 128 + h * 128 + d] = uint16_t(f2bf(o / L));
+    uint16_t* out = a.out + size_t(r) * a.H * 128 + h * 128 + d0;
+    uint32_t packed[MERGE_DIMS / 2];
+#pragma unroll
+    for (int k = 0; k < MERGE_DIMS / 2; k++)
+        packed[k] = f2bf(o[2 * k] / L) | (f2bf(o[2 * k + 1] / L) << 16);
+    if ((reinterpret_cast<uintptr_t>(out) & 15) == 0) {
+        *reinterpret_cast<uint4*>(out) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+    } else {
+#pragma unroll
+        for (int k = 0; k < MERGE_DIMS; k++) out[k] = uint16_t(packed[k >> 1] >> (16 * (k & 1)));
+    }
 }
 
 // --------------------------------------------------------------------------------------------
@@ -716,7 +777,7 @@ cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s) {
 }
 
 cudaError_t launch_attention_merge(const AttnArgs& a, cudaStream_t s) {
-    k_attn_merge<<<a.rows * a.H, 128, 0, s>>>(a);
+    k_attn_merge<<<a.rows * ((a.H * (128 / MERGE_DIMS) + 255) / 256), 256, 0, s>>>(a);
     return cudaGetLastError();
 }
 
