@@ -42,6 +42,13 @@ PLAMO_API int plamo_open(const char* model_dir, int context, int packed, int dev
 PLAMO_API int plamo_open_broadcast(const char* model_dir, int context, int packed, int device,
                          const void* nccl_id, int rank, int world, plamo_runtime** out);
 PLAMO_API int plamo_nccl_unique_id(void* out_128_bytes);
+/* The communicator setup of plamo_open_broadcast alone (no model, no device memory), for failure
+ * tests of the data-parallel open: creates the NCCL communicator non-blocking and polls it until it
+ * is ready, fails, or limit_ms passes (plamo_open_broadcast uses PLAMO_NCCL_TIMEOUT_MS, default
+ * 120000), aborting it on failure or timeout, then destroys it. A rank whose peers never join gets
+ * "NCCL communicator setup timed out ..." instead of waiting forever. PLAMO_NCCL_LIBRARY in the
+ * environment names the NCCL library to load first. Returns 0, or 1 with plamo_last_error set. */
+PLAMO_API int plamo_debug_nccl_init(const void* nccl_id, int rank, int world, long long limit_ms);
 /* Seconds spent in the load-time weight broadcast (0 when loaded from disk). */
 PLAMO_API double plamo_broadcast_seconds(const plamo_runtime*);
 

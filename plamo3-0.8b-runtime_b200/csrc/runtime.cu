@@ -16,6 +16,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <dlfcn.h>
+#include <nccl.h>  // types and constants only: the library is loaded with dlopen
 
 #include <algorithm>
 #include <chrono>
@@ -23,6 +24,7 @@
 #include <cmath>
 #include <cstring>
 #include <mutex>
+#include <thread>
 #include <set>
 #include <string>
 #include <utility>
@@ -472,6 +474,22 @@ static int capture_decode_graph(plamo_runtime& rt) {
 // buffers and the step counter. Leaves rt.mega false when the model shape is outside the kernel's
 // plan (hidden size <= 1536, one KV head, <= 16 query heads) or cooperative launch is unavailable
 // (the multi-kernel path remains).
+// The persistent kernel's copy of every norm vector, from the weight arena: [4l + k] = pre-mixer,
+// post-mixer, pre-MLP, post-MLP of layer l; [4L] final. Taken again after a broadcast open has
+// received the arena (the copy at setup saw the arena before the weights arrived).
+static int copy_mega_norms(plamo_runtime& rt, const MegaArgs& a) {
+    const Config& c = rt.c;
+    uint16_t* tab = const_cast<uint16_t*>(a.norms);
+    for (int l = 0; l < c.layers; l++) {
+        const Layer& L = rt.layers[l];
+        const uint16_t* src[4] = {L.pre_mixer, L.post_mixer, L.pre_mlp, L.post_mlp};
+        for (int k = 0; k < 4; k++)
+            CK(cudaMemcpy(tab + size_t(4 * l + k) * a.dpad, src[k], size_t(c.d) * 2, cudaMemcpyDeviceToDevice));
+    }
+    CK(cudaMemcpy(tab + size_t(4 * c.layers) * a.dpad, rt.final_norm, size_t(c.d) * 2, cudaMemcpyDeviceToDevice));
+    return 0;
+}
+
 static int setup_mega(plamo_runtime& rt) {
     const char* env = getenv("PLAMO_PERSISTENT");
     if (env && env[0] == '0') return 0;
@@ -543,18 +561,12 @@ static int setup_mega(plamo_runtime& rt) {
     a.rope_local = rt.rope_local;
     a.rope_global = rt.rope_global;
     a.d = c.d; a.H = c.heads; a.F = c.ffn; a.V = c.vocab; a.W = c.window;
-    {  // the norm table: [4l + k] = pre-mixer, post-mixer, pre-MLP, post-MLP of layer l; [4L] final
+    {  // the norm table (filled from the weight arena by copy_mega_norms)
         a.dpad = (c.d + 7) / 8 * 8;
         uint16_t* tab = nullptr;
         if (rt.dalloc(tab, size_t(4 * c.layers + 1) * a.dpad)) return 1;
-        for (int l = 0; l < c.layers; l++) {
-            const Layer& L = rt.layers[l];
-            const uint16_t* src[4] = {L.pre_mixer, L.post_mixer, L.pre_mlp, L.post_mlp};
-            for (int k = 0; k < 4; k++)
-                CK(cudaMemcpy(tab + size_t(4 * l + k) * a.dpad, src[k], size_t(c.d) * 2, cudaMemcpyDeviceToDevice));
-        }
-        CK(cudaMemcpy(tab + size_t(4 * c.layers) * a.dpad, rt.final_norm, size_t(c.d) * 2, cudaMemcpyDeviceToDevice));
         a.norms = tab;
+        if (copy_mega_norms(rt, a)) return 1;
     }
     a.post_mlp_offset = float(1.0 / std::pow(5.0, 1.5));
     a.phases_packed = rt.packed;
@@ -776,33 +788,49 @@ int plamo_open_broadcast(const char* model_dir, int context, int packed, int dev
 }
 
 // --- NCCL loaded on demand (no link-time dependency; reuses an already loaded libnccl) --------
-typedef struct { char internal[128]; } nccl_uid;
-typedef int (*nccl_get_uid_fn)(nccl_uid*);
-typedef int (*nccl_init_rank_fn)(void**, int, nccl_uid, int);
+// PLAMO_NCCL_LIBRARY names the library to load first (a deployment's own NCCL build). The
+// communicator is created non-blocking (ncclCommInitRankConfig, blocking = 0) and every NCCL step
+// is polled with a limit (PLAMO_NCCL_TIMEOUT_MS, default 120 s): a rank that never joins, or dies
+// mid-broadcast, ends the other ranks' calls with an error after the limit, and the communicator
+// is aborted (which also ends its kernels in flight) instead of waiting forever.
+typedef int (*nccl_get_uid_fn)(ncclUniqueId*);
+typedef int (*nccl_init_rank_fn)(void**, int, ncclUniqueId, int);
+typedef int (*nccl_init_config_fn)(void**, int, ncclUniqueId, int, ncclConfig_t*);
 typedef int (*nccl_bcast_fn)(const void*, void*, size_t, int, int, void*, cudaStream_t);
-typedef int (*nccl_destroy_fn)(void*);
+typedef int (*nccl_comm_fn)(void*);
+typedef int (*nccl_async_fn)(void*, int*);
 typedef const char* (*nccl_err_fn)(int);
 struct NcclApi {
     void* h = nullptr;
     nccl_get_uid_fn get_uid = nullptr;
     nccl_init_rank_fn init_rank = nullptr;
+    nccl_init_config_fn init_config = nullptr;
     nccl_bcast_fn bcast = nullptr;
-    nccl_destroy_fn destroy = nullptr;
+    nccl_comm_fn destroy = nullptr;
+    nccl_comm_fn abort = nullptr;
+    nccl_async_fn async_error = nullptr;
     nccl_err_fn err = nullptr;
 };
 static bool nccl_api(NcclApi& api) {
     static NcclApi cached;
     static bool tried = false;
+    static std::mutex mu;
+    std::lock_guard<std::mutex> lock(mu);
     if (!tried) {
         tried = true;
-        void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+        void* h = nullptr;
+        if (const char* path = std::getenv("PLAMO_NCCL_LIBRARY")) h = dlopen(path, RTLD_NOW | RTLD_GLOBAL);
+        if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
         if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
         if (h) {
             cached.h = h;
             cached.get_uid = (nccl_get_uid_fn)dlsym(h, "ncclGetUniqueId");
             cached.init_rank = (nccl_init_rank_fn)dlsym(h, "ncclCommInitRank");
+            cached.init_config = (nccl_init_config_fn)dlsym(h, "ncclCommInitRankConfig");
             cached.bcast = (nccl_bcast_fn)dlsym(h, "ncclBroadcast");
-            cached.destroy = (nccl_destroy_fn)dlsym(h, "ncclCommDestroy");
+            cached.destroy = (nccl_comm_fn)dlsym(h, "ncclCommDestroy");
+            cached.abort = (nccl_comm_fn)dlsym(h, "ncclCommAbort");
+            cached.async_error = (nccl_async_fn)dlsym(h, "ncclCommGetAsyncError");
             cached.err = (nccl_err_fn)dlsym(h, "ncclGetErrorString");
         }
     }
@@ -810,13 +838,100 @@ static bool nccl_api(NcclApi& api) {
     return api.h && api.get_uid && api.init_rank && api.bcast && api.destroy;
 }
 
+static std::string nccl_message(const NcclApi& api, const char* what, int e) {
+    return std::string(what) + " failed: " + (api.err ? api.err(e) : "?");
+}
+
+static long long nccl_limit_ms() {
+    const char* v = std::getenv("PLAMO_NCCL_TIMEOUT_MS");
+    const long long ms = v ? std::atoll(v) : 0;
+    return ms > 0 ? ms : 120000;
+}
+
+// Polls the communicator (and, when given, the stream its work was enqueued on) until the step
+// completes, fails, or the limit passes; aborts the communicator on failure or timeout. Returns 0,
+// or 1 with the error set; *comm is null after an abort.
+static int nccl_finish(const NcclApi& api, void** comm, cudaStream_t stream, long long limit_ms, const char* what) {
+    const auto t0 = std::chrono::steady_clock::now();
+    auto elapsed_ms = [&] {
+        return std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+    };
+    std::string err;
+    if (api.async_error) {
+        for (;;) {
+            int state = ncclSuccess;
+            const int e = api.async_error(*comm, &state);
+            if (e != ncclSuccess) { err = nccl_message(api, what, e); break; }
+            if (state == ncclSuccess) break;
+            if (state != ncclInProgress) { err = nccl_message(api, what, state); break; }
+            if (elapsed_ms() > limit_ms) { err = std::string(what) + " timed out after " + std::to_string(limit_ms) + " ms (a rank did not join)"; break; }
+            std::this_thread::sleep_for(std::chrono::microseconds(200));
+        }
+    }
+    while (err.empty() && stream) {
+        const cudaError_t q = cudaStreamQuery(stream);
+        if (q == cudaSuccess) break;
+        if (q != cudaErrorNotReady) { err = std::string(what) + ": " + cudaGetErrorString(q); break; }
+        if (elapsed_ms() > limit_ms) { err = std::string(what) + " timed out after " + std::to_string(limit_ms) + " ms (a rank stopped)"; break; }
+        std::this_thread::sleep_for(std::chrono::microseconds(200));
+    }
+    if (err.empty()) return 0;
+    if (*comm) (api.abort ? api.abort : api.destroy)(*comm);
+    *comm = nullptr;
+    return fail(err);
+}
+
+// Creates the broadcast communicator: non-blocking when the library has ncclCommInitRankConfig
+// (bounded by the limit), else the blocking ncclCommInitRank.
+static int nccl_comm_init(const NcclApi& api, const void* nccl_id, int rank, int world, long long limit_ms, void** comm) {
+    ncclUniqueId id;
+    memcpy(&id, nccl_id, sizeof(id));
+    *comm = nullptr;
+    if (!api.init_config || !api.async_error) {
+        const int e = api.init_rank(comm, world, id, rank);
+        if (e) { *comm = nullptr; return fail(nccl_message(api, "ncclCommInitRank", e)); }
+        return 0;
+    }
+    ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+    cfg.blocking = 0;
+    const int e = api.init_config(comm, world, id, rank, &cfg);
+    if (e != ncclSuccess && e != ncclInProgress) {
+        if (*comm) (api.abort ? api.abort : api.destroy)(*comm);
+        *comm = nullptr;
+        return fail(nccl_message(api, "ncclCommInitRankConfig", e));
+    }
+    if (!*comm) return fail("ncclCommInitRankConfig returned no communicator");
+    return nccl_finish(api, comm, nullptr, limit_ms, "NCCL communicator setup");
+}
+
+// One broadcast from rank 0 on `stream`, completed (or failed) within the limit.
+static int nccl_broadcast(const NcclApi& api, void** comm, void* buf, size_t bytes, cudaStream_t stream, long long limit_ms) {
+    const int e = api.bcast(buf, buf, bytes, /*ncclUint8*/ 1, 0, *comm, stream);
+    if (e != ncclSuccess && e != ncclInProgress) {
+        (api.abort ? api.abort : api.destroy)(*comm);
+        *comm = nullptr;
+        return fail(nccl_message(api, "ncclBroadcast", e));
+    }
+    return nccl_finish(api, comm, stream, limit_ms, "ncclBroadcast");
+}
+
 int plamo_nccl_unique_id(void* out) {
     NcclApi api;
     if (!out || !nccl_api(api)) return fail("NCCL is not available");
-    nccl_uid id;
+    ncclUniqueId id;
     int e = api.get_uid(&id);
-    if (e) return fail(std::string("ncclGetUniqueId failed: ") + (api.err ? api.err(e) : "?"));
+    if (e) return fail(nccl_message(api, "ncclGetUniqueId", e));
     memcpy(out, &id, sizeof(id));
+    return 0;
+}
+
+int plamo_debug_nccl_init(const void* nccl_id, int rank, int world, long long limit_ms) {
+    NcclApi api;
+    if (!nccl_id || world < 1 || rank < 0 || rank >= world || limit_ms < 1) return fail("Invalid broadcast arguments");
+    if (!nccl_api(api)) return fail("NCCL is not available");
+    void* comm = nullptr;
+    if (nccl_comm_init(api, nccl_id, rank, world, limit_ms, &comm)) return 1;
+    api.destroy(comm);
     return 0;
 }
 
@@ -851,29 +966,21 @@ static int open_common(const char* model_dir, int context, int packed, int devic
     if (!rc) rc = setup_runtime(rt, mf, nccl_id == nullptr || rank == 0, &arena);
     if (!rc && nccl_id) {
         NcclApi api;
+        const long long limit = nccl_limit_ms();
         if (!nccl_api(api)) rc = fail("NCCL is not available");
         void* comm = nullptr;
-        if (!rc) {
-            nccl_uid id;
-            memcpy(&id, nccl_id, sizeof(id));
-            int e = api.init_rank(&comm, world, id, rank);
-            if (e) rc = fail(std::string("ncclCommInitRank failed: ") + (api.err ? api.err(e) : "?"));
-        }
-        if (!rc) {
-            // a first small broadcast sets up the communicator's channels (lazily, on first use),
-            // so the timed one measures the weight transfer alone
-            int e = api.bcast(rt->arena, rt->arena, 256, /*ncclUint8*/ 1, 0, comm, rt->stream);
-            if (e) rc = fail(std::string("ncclBroadcast failed: ") + (api.err ? api.err(e) : "?"));
-            if (!rc && cudaStreamSynchronize(rt->stream) != cudaSuccess) rc = fail("weight broadcast failed");
-        }
+        if (!rc) rc = nccl_comm_init(api, nccl_id, rank, world, limit, &comm);
+        // a first small broadcast sets up the communicator's channels (lazily, on first use), so
+        // the timed one measures the weight transfer alone
+        if (!rc) rc = nccl_broadcast(api, &comm, rt->arena, 256, rt->stream, limit);
         if (!rc) {
             auto t0 = std::chrono::steady_clock::now();
-            int e = api.bcast(rt->arena, rt->arena, rt->arena_bytes, /*ncclUint8*/ 1, 0, comm, rt->stream);
-            if (e) rc = fail(std::string("ncclBroadcast failed: ") + (api.err ? api.err(e) : "?"));
-            if (!rc && cudaStreamSynchronize(rt->stream) != cudaSuccess) rc = fail("weight broadcast failed");
+            rc = nccl_broadcast(api, &comm, rt->arena, rt->arena_bytes, rt->stream, limit);
             rt->bcast_seconds = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
         }
         if (comm) api.destroy(comm);
+        // state derived from the arena's contents at setup is taken again from the received weights
+        if (!rc && rank > 0 && rt->mega) rc = copy_mega_norms(*rt, rt->margs);
     }
     delete mf;  // weights are resident; the mappings are no longer needed
     if (rc) { delete rt; return rc; }

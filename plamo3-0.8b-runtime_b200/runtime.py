@@ -92,6 +92,7 @@ def library() -> ctypes.CDLL:
         "plamo_profile_decode": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.POINTER(ctypes.c_double), _i32p]),
         "plamo_persistent_decode": (ctypes.c_int, [_vp]),
         "plamo_debug_wait_timeout": (ctypes.c_int, [_vp, ctypes.c_ulonglong]),
+        "plamo_debug_nccl_init": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int, ctypes.c_longlong]),
         "plamo_trace_decode": (ctypes.c_int, [_vp, _vp, ctypes.c_size_t, _i32p]),
         "plamo_set_tensor_gemm": (ctypes.c_int, [_vp, ctypes.c_int]),
         "plamo_select": (ctypes.c_int, [_vp, _i32p, ctypes.c_int, ctypes.c_float, ctypes.c_int, ctypes.c_float,
@@ -392,6 +393,12 @@ def repetition_period(tokens, repeats: int):
     arr, ptr = _ids(tokens)
     p = library().plamo_repetition_period(ptr, len(arr), int(repeats))
     return p or None
+
+
+def debug_nccl_init(nccl_id: bytes, rank: int, world: int, limit_ms: int) -> None:
+    """The communicator setup of Runtime.broadcast alone, bounded by limit_ms (failure tests)."""
+    buf = ctypes.create_string_buffer(bytes(nccl_id), 128)
+    _check(library().plamo_debug_nccl_init(buf, int(rank), int(world), int(limit_ms)))
 
 
 def pack_p12(model_dir, source_sha256: str | None = None) -> dict:
