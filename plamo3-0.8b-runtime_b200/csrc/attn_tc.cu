@@ -83,6 +83,7 @@ constexpr float ATC_LOG2E = 1.4426950408889634f;
 constexpr float ATC_LN2 = 0.6931471805599453f;
 
 __global__ void __launch_bounds__(ATC_THREADS, 1) k_attn_tc(AttnArgs a, int span, int* error) {
+    pdl_enter();
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
     uint64_t* bar_s = reinterpret_cast<uint64_t*>(smem + OFF_CTL);
@@ -438,8 +439,8 @@ cudaError_t launch_attention_tc(const AttnArgs& a, cudaStream_t s) {
     if (!attention_tc_supported(a) || a.splits != attention_tc_splits(keys)) return cudaErrorInvalidValue;
     int* error = gemm_error_word(true);
     if (!error) return cudaErrorInvalidDevice;
-    k_attn_tc<<<dim3(a.splits, (a.rows + ATC_TOK - 1) / ATC_TOK), ATC_THREADS, ATC_SMEM, s>>>(a, attention_tc_span(keys), error);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e = pdl_launch(k_attn_tc, dim3(a.splits, (a.rows + ATC_TOK - 1) / ATC_TOK), dim3(ATC_THREADS), ATC_SMEM, s,
+                               a, attention_tc_span(keys), error);
     if (e != cudaSuccess) return e;
     return launch_attention_merge(a, s);
 }

@@ -1,6 +1,8 @@
 // Shared device helpers for the sm_100a kernels.
 #pragma once
 #include <cstdint>
+#include <cstdlib>
+#include <utility>
 #include <cuda_runtime.h>
 
 #define PLAMO_HD 128        // head_dim
@@ -10,6 +12,43 @@
 namespace plamo {
 
 constexpr unsigned FULL_MASK = 0xffffffffu;
+
+// Programmatic dependent launch. The kernels of a forward call are launched with programmatic
+// stream serialization, so a kernel's launch and CTA rasterisation overlap the tail of the kernel
+// before it in the stream. Each such kernel calls pdl_enter() before it touches global memory:
+// the wait returns once the previous kernel has completed and its writes are visible, so the data
+// dependencies are those of a plain launch; the trigger then lets the next kernel launch while
+// this one runs. Without the launch attribute both instructions are no-ops.
+__device__ __forceinline__ void pdl_enter() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// PLAMO_PDL=0 in the environment launches plainly (for comparison); on by default.
+inline bool pdl_enabled() {
+    static const bool on = [] {
+        const char* v = std::getenv("PLAMO_PDL");
+        return !(v && v[0] == '0');
+    }();
+    return on;
+}
+
+// kernel<<<grid, block, smem, s>>>(args...) with the programmatic-serialization attribute.
+template <typename... KArgs, typename... Args>
+inline cudaError_t pdl_launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                              Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 // bf16 widening and the reference's round-to-nearest-even narrowing (Kernels.metal:5-10); the
 // integer form reproduces its behaviour bit for bit, NaN payloads included.

@@ -111,6 +111,7 @@ __device__ __forceinline__ void read16(const uint8_t* base, int r, int lines, in
 template <int MODE>
 __global__ void __launch_bounds__(256, 1)
     k_gemm(GemvArgs a, const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmw, int* error) {
+    pdl_enter();
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + NSTAGE * STAGE_BYTES + RED_BYTES);
@@ -269,8 +270,7 @@ cudaError_t gemm_launch(const GemvArgs& a, cudaStream_t s) {
     int* err = gemm_error_word(true);
     if (!err) return cudaErrorMemoryAllocation;
     const int grid = tiles < sms[dev & 63] ? tiles : sms[dev & 63];  // persistent: one CTA per SM
-    k_gemm<MODE><<<grid, 256, GEMM_SMEM, s>>>(a, tmx, tmw, err);
-    return cudaGetLastError();
+    return pdl_launch(k_gemm<MODE>, dim3(grid), dim3(256), GEMM_SMEM, s, a, tmx, tmw, err);
 }
 
 }  // namespace

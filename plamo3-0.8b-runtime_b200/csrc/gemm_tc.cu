@@ -61,6 +61,7 @@ template <int BN, int MODE>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     k_gemm_tc(GemvArgs a, const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmw, int splits,
               int* error) {
+    pdl_enter();
     using T = TcTile<BN>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
@@ -245,6 +246,7 @@ constexpr int TCP_THREADS = 192;
 template <int BN, int MODE>
 __global__ void __launch_bounds__(TCP_THREADS, 1)
     k_gemm_tcp(GemvArgs a, const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmw, int* error) {
+    pdl_enter();
     using T = TcTile<BN>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
@@ -433,9 +435,11 @@ __global__ void __launch_bounds__(TCP_THREADS, 1)
     }
 }
 
-// Adds the split partials of one output in split order and applies the mode's epilogue.
+// Adds the split partials of one output in split order and applies the mode's epilogue. Every
+// split's partial is loaded before the first add, so the sum costs one memory round trip.
 template <int MODE>
 __global__ void __launch_bounds__(256) k_gemm_tc_finish(GemvArgs a, int splits) {
+    pdl_enter();
     const int r = int(blockIdx.y), m = int(blockIdx.x) * 256 + int(threadIdx.x);
     const int M = a.lin.M, Mout = MODE == GEMV_SWIGLU ? M / 2 : M;
     const size_t sstride = size_t(a.rows) * M;
@@ -443,11 +447,23 @@ __global__ void __launch_bounds__(256) k_gemm_tc_finish(GemvArgs a, int splits) 
     const int orow = a.out_map ? a.out_map[r] : r;
     unsigned long long key = 0ull;
     if (m < Mout) {
-        float v = p[m];
-        for (int s = 1; s < splits; s++) v = v + p[s * sstride + m];
+        float pv[TC_SPLITS_MAX], pu[TC_SPLITS_MAX];
+#pragma unroll
+        for (int s = 0; s < TC_SPLITS_MAX; s++) {
+            if (s < splits) {
+                pv[s] = p[s * sstride + m];
+                if (MODE == GEMV_SWIGLU) pu[s] = p[s * sstride + Mout + m];
+            }
+        }
+        float v = pv[0];
+#pragma unroll
+        for (int s = 1; s < TC_SPLITS_MAX; s++)
+            if (s < splits) v = v + pv[s];
         if (MODE == GEMV_SWIGLU) {
-            float u = p[Mout + m];
-            for (int s = 1; s < splits; s++) u = u + p[s * sstride + Mout + m];
+            float u = pu[0];
+#pragma unroll
+            for (int s = 1; s < TC_SPLITS_MAX; s++)
+                if (s < splits) u = u + pu[s];
             a.y[size_t(orow) * a.ystride + m] = uint16_t(f2bf(swiglu(v, u)));
         } else {
             const uint32_t b = f2bf(v);
@@ -524,15 +540,14 @@ cudaError_t tc_launch(const GemvArgs& a, int splits, int tiles, TcDevice& dev, c
         !encode_kmajor(&tmw, a.lin.w, a.lin.M, a.lin.K, MODE == GEMV_SWIGLU ? TC_BM / 2 : TC_BM))
         return cudaErrorInvalidValue;
     if (splits == 1 && tiles > dev.sms && BN >= 128 && tcp_enabled()) {  // persistent: more tiles than SMs
-        k_gemm_tcp<BN, MODE><<<dev.sms, TCP_THREADS, TcTile<BN>::SMEM + 5120, s>>>(a, tmx, tmw, dev.error);
-        return cudaGetLastError();
+        return pdl_launch(k_gemm_tcp<BN, MODE>, dim3(dev.sms), dim3(TCP_THREADS), TcTile<BN>::SMEM + 5120, s, a, tmx,
+                          tmw, dev.error);
     }
-    k_gemm_tc<BN, MODE><<<tiles * splits, TC_THREADS, TcTile<BN>::SMEM, s>>>(a, tmx, tmw, splits, dev.error);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e = pdl_launch(k_gemm_tc<BN, MODE>, dim3(tiles * splits), dim3(TC_THREADS), TcTile<BN>::SMEM, s, a, tmx,
+                               tmw, splits, dev.error);
     if (e != cudaSuccess || splits == 1) return e;
     const int Mout = MODE == GEMV_SWIGLU ? a.lin.M / 2 : a.lin.M;
-    k_gemm_tc_finish<MODE><<<dim3((Mout + 255) / 256, a.rows), 256, 0, s>>>(a, splits);
-    return cudaGetLastError();
+    return pdl_launch(k_gemm_tc_finish<MODE>, dim3((Mout + 255) / 256, a.rows), dim3(256), 0, s, a, splits);
 }
 
 template <int BN>

@@ -63,6 +63,7 @@ __device__ __forceinline__ void load16(const Linear& lin, size_t el, uint32_t (&
 // shared load of a warp is conflict-free.
 template <int R, bool PACKED, int MODE>
 __global__ void __launch_bounds__(256) k_gemv(GemvArgs a) {
+    pdl_enter();
     extern __shared__ uint4 xs[];
     constexpr int NW = MODE == GEMV_SWIGLU ? 2 : 1;
     // Two interleaved accumulators per (weight row, activation row): the per-row summation order
@@ -227,6 +228,7 @@ __device__ __forceinline__ void norm_row(const float (&v)[NPT], int n, const flo
 // before the first reduction, so a row pays one memory latency instead of one per stage; the
 // arithmetic and its order are unchanged.
 __global__ void __launch_bounds__(256) k_norm(NormArgs a) {
+    pdl_enter();
     __shared__ float red[9];
     const int r = blockIdx.x;
     const size_t row = size_t(r) * a.n;
@@ -278,6 +280,7 @@ __global__ void __launch_bounds__(256) k_norm(NormArgs a) {
 __global__ void __launch_bounds__(256) k_embed_norm(const int* ids, int vocab, const uint16_t* embed, const uint16_t* w,
                                                     int d, uint16_t* x, uint16_t* h, unsigned long long* keys,
                                                     const int* key_map, int nkeys) {
+    pdl_enter();
     __shared__ float red[9];
     const int r = blockIdx.x;
     if (r == 0 && keys)
@@ -308,6 +311,7 @@ __global__ void __launch_bounds__(256) k_embed_norm(const int* ids, int vocab, c
 // Per (row, head) warp: QK RMSNorm (w + 1), RoPE of queries, KV append into the ring slot
 // pos % cap of the row's lane slab (global layers store rotated keys, local layers raw keys).
 __global__ void __launch_bounds__(128) k_qkv(QkvArgs a) {
+    pdl_enter();
     const int gw = blockIdx.x * 4 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     const int heads = a.H + a.KV;
     if (gw >= a.rows * heads) return;
@@ -403,6 +407,7 @@ __device__ __forceinline__ void stage_rows_async(uint4* dst, const uint16_t* bas
 
 template <int AT>
 __global__ void __launch_bounds__(256) k_attn_partial(AttnArgs a) {
+    pdl_enter();
     extern __shared__ __align__(16) float smem[];
     const int r = blockIdx.y, s = blockIdx.x, t = threadIdx.x;
     const RowGeo g = a.geo[r];
@@ -537,6 +542,7 @@ __device__ __forceinline__ void merge_fold(const float2 (&st)[8], const float4 (
 }
 
 __global__ void __launch_bounds__(256) k_attn_merge(AttnArgs a) {
+    pdl_enter();
     const int per_row = (a.H * (128 / MERGE_DIMS) + 255) / 256;
     const int r = blockIdx.x / per_row;
     const int idx = (blockIdx.x - r * per_row) * 256 + threadIdx.x;
@@ -601,6 +607,7 @@ __global__ void __launch_bounds__(256) k_attn_merge(AttnArgs a) {
 // next input, advances the row descriptor and appends the id to a bounded history.
 __global__ void k_finalize(unsigned long long* keys, const int* key_map, int rows, int* result,
                            int* chain_ids, RowDesc* advance, int* hist, int* hist_count, int hist_cap) {
+    pdl_enter();
     const int r = threadIdx.x;
     if (r >= rows) return;
     const int k = key_map ? key_map[r] : r;
@@ -620,6 +627,7 @@ __global__ void k_finalize(unsigned long long* keys, const int* key_map, int row
 
 // Standalone first-index argmax over bf16 rows (Kernels.metal:704-729).
 __global__ void __launch_bounds__(256) k_argmax(const uint16_t* logits, int n, unsigned long long* keys) {
+    pdl_enter();
     const int r = blockIdx.y;
     unsigned long long best = 0ull;
     for (int i = blockIdx.x * 256 + threadIdx.x; i < n; i += gridDim.x * 256) {
@@ -656,8 +664,7 @@ static cudaError_t gemv_launch(const GemvArgs& a, cudaStream_t s) {
     const int Mout = M == GEMV_SWIGLU ? a.lin.M / 2 : a.lin.M;
     int grid = (Mout + 7) / 8;
     if (M == GEMV_LOGITS) grid = grid < 148 * 4 ? grid : 148 * 4;
-    k_gemv<R, P, M><<<grid, 256, smem, s>>>(a);
-    return cudaGetLastError();
+    return pdl_launch(k_gemv<R, P, M>, dim3(grid), dim3(256), smem, s, a);
 }
 
 template <int R, bool P>
@@ -745,20 +752,18 @@ cudaError_t launch_embed_norm(const int* ids, int rows, int vocab, const uint16_
                               uint16_t* x, uint16_t* h, unsigned long long* keys, const int* key_map, int nkeys,
                               cudaStream_t s) {
     if (d > 256 * NPT) return cudaErrorInvalidValue;
-    k_embed_norm<<<rows, 256, 0, s>>>(ids, vocab, embed, w, d, x, h, keys, key_map, nkeys);
-    return cudaGetLastError();
+    return pdl_launch(k_embed_norm, dim3(rows), dim3(256), 0, s, ids, vocab, embed, w, d, x, h, keys, key_map,
+                      nkeys);
 }
 
 cudaError_t launch_norm(const NormArgs& a, cudaStream_t s) {
     if (a.n > 256 * NPT) return cudaErrorInvalidValue;
-    k_norm<<<a.rows, 256, 0, s>>>(a);
-    return cudaGetLastError();
+    return pdl_launch(k_norm, dim3(a.rows), dim3(256), 0, s, a);
 }
 
 cudaError_t launch_qkv(const QkvArgs& a, cudaStream_t s) {
     const int warps = a.rows * (a.H + a.KV);
-    k_qkv<<<(warps + 3) / 4, 128, 0, s>>>(a);
-    return cudaGetLastError();
+    return pdl_launch(k_qkv, dim3((warps + 3) / 4), dim3(128), 0, s, a);
 }
 
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s) {
@@ -766,26 +771,24 @@ cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s) {
     const size_t smem = attention_smem(a.H, a.KV, a.per_max);
     if (smem > 200 * 1024) return cudaErrorInvalidValue;
     const dim3 grid(a.splits, a.rows);
+    cudaError_t e;
     switch (attn_tile_keys(a.KV)) {
-        case 64: k_attn_partial<64><<<grid, 256, smem, s>>>(a); break;
-        case 32: k_attn_partial<32><<<grid, 256, smem, s>>>(a); break;
-        default: k_attn_partial<16><<<grid, 256, smem, s>>>(a); break;
+        case 64: e = pdl_launch(k_attn_partial<64>, grid, dim3(256), smem, s, a); break;
+        case 32: e = pdl_launch(k_attn_partial<32>, grid, dim3(256), smem, s, a); break;
+        default: e = pdl_launch(k_attn_partial<16>, grid, dim3(256), smem, s, a); break;
     }
-    cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     return launch_attention_merge(a, s);
 }
 
 cudaError_t launch_attention_merge(const AttnArgs& a, cudaStream_t s) {
-    k_attn_merge<<<a.rows * ((a.H * (128 / MERGE_DIMS) + 255) / 256), 256, 0, s>>>(a);
-    return cudaGetLastError();
+    return pdl_launch(k_attn_merge, dim3(a.rows * ((a.H * (128 / MERGE_DIMS) + 255) / 256)), dim3(256), 0, s, a);
 }
 
 cudaError_t launch_finalize(unsigned long long* keys, const int* key_map, int rows, int* result, int* chain_ids,
                             RowDesc* advance, int* hist, int* hist_count, int hist_cap, cudaStream_t s) {
-    k_finalize<<<1, 64 * ((rows + 63) / 64), 0, s>>>(keys, key_map, rows, result, chain_ids, advance, hist, hist_count,
-                                                      hist_cap);
-    return cudaGetLastError();
+    return pdl_launch(k_finalize, dim3(1), dim3(64 * ((rows + 63) / 64)), 0, s, keys, key_map, rows, result, chain_ids,
+                      advance, hist, hist_count, hist_cap);
 }
 
 cudaError_t launch_argmax(const uint16_t* logits, int rows, int n, unsigned long long* keys, uint32_t* out,
@@ -794,8 +797,7 @@ cudaError_t launch_argmax(const uint16_t* logits, int rows, int n, unsigned long
     if (e != cudaSuccess) return e;
     int blocks = (n + 255) / 256;
     blocks = blocks < 64 ? blocks : 64;
-    k_argmax<<<dim3(blocks, rows), 256, 0, s>>>(logits, n, keys);
-    e = cudaGetLastError();
+    e = pdl_launch(k_argmax, dim3(blocks, rows), dim3(256), 0, s, logits, n, keys);
     if (e != cudaSuccess) return e;
     return launch_finalize(keys, nullptr, rows, reinterpret_cast<int*>(out), nullptr, nullptr, nullptr, nullptr, 0, s);
 }
