@@ -373,7 +373,7 @@ __host__ __device__ constexpr int attn_tile_keys(int KV) { return KV == 1 ? 64 :
 int attention_per_max(int cap, int splits) { return ((cap + splits - 1) / splits + 31) & ~31; }
 size_t attention_smem(int H, int KV, int per_max) {
     const size_t AT = size_t(attn_tile_keys(KV));
-    return sizeof(float) * (size_t(H) * QS + AT * (KV * 128 + 1) + AT * 64 + size_t(H) * per_max) +
+    return sizeof(float) * (size_t(H) * QS + AT * (KV * 128 + 4) + AT * 64 + size_t(H) * per_max) +
            2 * AT * KV * 128 * 2;  // key / value staging, and the first value tile fetched early
 }
 
@@ -412,7 +412,7 @@ __global__ void __launch_bounds__(256) k_attn_partial(AttnArgs a) {
     const int r = blockIdx.y, s = blockIdx.x, t = threadIdx.x;
     const RowGeo g = a.geo[r];
     const int lane_id = a.desc[r].lane;
-    const int H = a.H, KV = a.KV, group = H / KV, KS = KV * 128 + 1;
+    const int H = a.H, KV = a.KV, group = H / KV, KS = KV * 128 + 4;  // 16-byte rows, rows 4 banks apart
     int per = (g.count + a.splits - 1) / a.splits;
     per = (per + 31) & ~31;
     const int k0 = s * per, k1 = min(k0 + per, g.count);
@@ -461,11 +461,18 @@ __global__ void __launch_bounds__(256) k_attn_partial(AttnArgs a) {
         const int j = t & (AT - 1);
         if (j < tk) {
             for (int h = t / AT; h < H; h += 256 / AT) {
-                const float* qh = qs + h * QS;
-                const float* kj = kr + j * KS + (h / group) * 128;
+                // 16-byte shared-memory reads; the products are still added in d order
+                const float4* qh = reinterpret_cast<const float4*>(qs + h * QS);
+                const float4* kj = reinterpret_cast<const float4*>(kr + j * KS + (h / group) * 128);
                 float acc = 0.f;
-#pragma unroll 16
-                for (int d = 0; d < 128; d++) acc = fmaf(qh[d], kj[d], acc);
+#pragma unroll 8
+                for (int d4 = 0; d4 < 32; d4++) {
+                    const float4 q = qh[d4], k = kj[d4];
+                    acc = fmaf(q.x, k.x, acc);
+                    acc = fmaf(q.y, k.y, acc);
+                    acc = fmaf(q.z, k.z, acc);
+                    acc = fmaf(q.w, k.w, acc);
+                }
                 sc[h * a.per_max + t0 + j] = acc * PLAMO_ATTN_SCALE;
             }
         }
@@ -495,7 +502,28 @@ __global__ void __launch_bounds__(256) k_attn_partial(AttnArgs a) {
         else stage_rows(raw, vbase, g.first, lo + t0, tk, a.cap, KV);
         __syncthreads();
         const uint16_t* vtile = t0 == 0 ? reinterpret_cast<const uint16_t*>(vfirst) : raw16;
-        for (int i = 0; i < tk; i++) {
+        int i = 0;
+        if (KV == 1) {
+            // four keys at a time: one 16-byte read of each head's scores; every output still adds
+            // the keys in order
+            for (; i + 4 <= tk; i += 4) {
+                float v[4];
+#pragma unroll
+                for (int u = 0; u < 4; u++) v[u] = bf2f(vtile[(i + u) * 128 + d]);
+#pragma unroll
+                for (int q = 0; q < 16; q++) {
+                    const int h = hh + 2 * q;
+                    if (h < H) {
+                        const float4 pr = *reinterpret_cast<const float4*>(sc + h * a.per_max + t0 + i);
+                        acc[q] = fmaf(pr.x, v[0], acc[q]);
+                        acc[q] = fmaf(pr.y, v[1], acc[q]);
+                        acc[q] = fmaf(pr.z, v[2], acc[q]);
+                        acc[q] = fmaf(pr.w, v[3], acc[q]);
+                    }
+                }
+            }
+        }
+        for (; i < tk; i++) {
             const uint16_t* vr = vtile + i * KV * 128;
             if (KV == 1) {
                 const float v = bf2f(vr[d]);
