@@ -434,7 +434,17 @@ __global__ void __launch_bounds__(256) k_attn_partial(AttnArgs a) {
     const int n = hi - lo;
     // the first value tile streams in while the keys are staged, rotated and scored
     stage_rows_async(vfirst, vbase, g.first, lo, min(AT, n), a.cap, KV);
-    for (int i = t; i < H * 128; i += 256) qs[(i >> 7) * QS + (i & 127)] = bf2f(a.q[size_t(r) * H * 128 + i]);
+    const uint16_t* qrow = a.q + size_t(r) * H * 128;
+    if ((reinterpret_cast<uintptr_t>(qrow) & 15) == 0) {  // eight values per 16-byte read
+        for (int i8 = t; i8 < H * 16; i8 += 256) {
+            const uint4 w = reinterpret_cast<const uint4*>(qrow)[i8];
+            float* dst = qs + (i8 >> 4) * QS + (i8 & 15) * 8;
+            reinterpret_cast<float4*>(dst)[0] = make_float4(bf2f(w.x & 0xffffu), bf2f(w.x >> 16), bf2f(w.y & 0xffffu), bf2f(w.y >> 16));
+            reinterpret_cast<float4*>(dst)[1] = make_float4(bf2f(w.z & 0xffffu), bf2f(w.z >> 16), bf2f(w.w & 0xffffu), bf2f(w.w >> 16));
+        }
+    } else {
+        for (int i = t; i < H * 128; i += 256) qs[(i >> 7) * QS + (i & 127)] = bf2f(qrow[i]);
+    }
     // pass 1: scores of every visible key of this split
     for (int t0 = 0; t0 < n; t0 += AT) {
         const int tk = min(AT, n - t0);
@@ -445,17 +455,31 @@ __global__ void __launch_bounds__(256) k_attn_partial(AttnArgs a) {
                 reinterpret_cast<uint4*>(rope)[i] =
                     __ldg(reinterpret_cast<const uint4*>(a.rope_local + size_t(lo + t0 + (i >> 4)) * 64) + (i & 15));
         __syncthreads();
-        for (int i = t; i < tk * KV * 128; i += 256) {
-            const int j = i / (KV * 128), e = i - j * (KV * 128);
+        // eight consecutive elements per thread and pass (16-byte shared-memory reads and writes)
+        for (int i8 = t; i8 < tk * KV * 16; i8 += 256) {
+            const int j = i8 / (KV * 16), e0 = (i8 - j * (KV * 16)) * 8;
             const uint16_t* kr16 = raw16 + j * KV * 128;
-            float val;
+            const uint4 w = *reinterpret_cast<const uint4*>(kr16 + e0);
+            const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
+            float val[8];
             if (a.full) {
-                val = bf2f(kr16[e]);
+#pragma unroll
+                for (int k = 0; k < 8; k++) val[k] = bf2f((wv[k >> 1] >> (16 * (k & 1))) & 0xffffu);
             } else {  // window-relative re-rotation of raw local keys (Kernels.metal:277-285)
-                const int d = e & 127, kvoff = e - d, partner = d < 64 ? d + 64 : d - 64;
-                val = rope_rotate(bf2f(kr16[kvoff + d]), bf2f(kr16[kvoff + partner]), d, rope[j * 64 + (d & 63)]);
+                const int d0 = e0 & 127, kvoff = e0 - d0, p0 = d0 < 64 ? d0 + 64 : d0 - 64;
+                const uint4 o = *reinterpret_cast<const uint4*>(kr16 + kvoff + p0);
+                const uint32_t ov[4] = {o.x, o.y, o.z, o.w};
+                const uint4 c0 = *reinterpret_cast<const uint4*>(rope + j * 64 + (d0 & 63));
+                const uint4 c1 = *reinterpret_cast<const uint4*>(rope + j * 64 + (d0 & 63) + 4);
+                const uint32_t cs[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+#pragma unroll
+                for (int k = 0; k < 8; k++)
+                    val[k] = rope_rotate(bf2f((wv[k >> 1] >> (16 * (k & 1))) & 0xffffu),
+                                         bf2f((ov[k >> 1] >> (16 * (k & 1))) & 0xffffu), d0 + k, cs[k]);
             }
-            kr[j * KS + e] = val;
+            float4* dst = reinterpret_cast<float4*>(kr + j * KS + e0);
+            dst[0] = make_float4(val[0], val[1], val[2], val[3]);
+            dst[1] = make_float4(val[4], val[5], val[6], val[7]);
         }
         __syncthreads();
         const int j = t & (AT - 1);
