@@ -242,7 +242,7 @@ constexpr int PREFILL_CALL_ROWS = 512;
 constexpr size_t ATT_PART_BYTES = size_t(64) << 20;
 // Split-K partials of the tcgen05 GEMM (8 MiB): splits of the small projections at up to a few
 // dozen rows; larger calls have tiles enough for every SM and do not split.
-constexpr size_t TC_PART_FLOATS = size_t(2) << 20;
+constexpr size_t TC_PART_FLOATS = size_t(8) << 20;
 
 template <typename Owner>
 static int alloc_work(Owner& o, plamo_runtime& rt, Work& w, int rows) {

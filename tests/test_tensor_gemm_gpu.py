@@ -58,6 +58,8 @@ CASES = [
     (512, 1536, 12288, 1, 0),
     (300, 1536, 24576, 0, 0),
     (256, 1536, 40000, 2, 0),
+    # long K over few tiles: 256-row activation tiles with K split over the idle SMs
+    (512, 6144, 1536, 0, 0),
 ]
 
 
