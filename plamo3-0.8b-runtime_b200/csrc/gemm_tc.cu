@@ -547,6 +547,10 @@ cudaError_t tc_launch(const GemvArgs& a, int splits, int tiles, TcDevice& dev, c
     cudaError_t e = pdl_launch(k_gemm_tc<BN, MODE>, dim3(tiles * splits), dim3(TC_THREADS), TcTile<BN>::SMEM, s, a, tmx,
                                tmw, splits, dev.error);
     if (e != cudaSuccess || splits == 1) return e;
+    if (MODE == GEMV_PLAIN && a.split_out && !a.out_map) {  // the next kernel adds the partials
+        *a.split_out = splits;
+        return cudaSuccess;
+    }
     const int Mout = MODE == GEMV_SWIGLU ? a.lin.M / 2 : a.lin.M;
     return pdl_launch(k_gemm_tc_finish<MODE>, dim3((Mout + 255) / 256, a.rows), dim3(256), 0, s, a, splits);
 }

@@ -202,41 +202,73 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 
 // The factors bf16(w + offset) of a norm row, read before the row's reduction so their load
 // latency overlaps it.
-__device__ __forceinline__ void norm_factors(const uint16_t* w, int n, float offset, float (&f)[NPT]) {
+template <int NJ>
+__device__ __forceinline__ void norm_factors(const uint16_t* w, int n, float offset, float (&f)[NJ]) {
 #pragma unroll
-    for (int j = 0; j < NPT; j++) {
+    for (int j = 0; j < NJ; j++) {
         const int i = threadIdx.x + j * 256;
         f[j] = i < n ? rbf(bf2f(w[i]) + offset) : 0.f;
     }
 }
 
-__device__ __forceinline__ void norm_row(const float (&v)[NPT], int n, const float (&f)[NPT], float* red,
-                                         float (&z)[NPT]) {
+// Elements past n are zero in v and add nothing to the thread's chain, so the sum does not depend
+// on NJ (elements per thread) once 256 NJ >= n.
+template <int NJ>
+__device__ __forceinline__ void norm_row(const float (&v)[NJ], int n, const float (&f)[NJ], float* red,
+                                         float (&z)[NJ]) {
     float ss = 0.f;
 #pragma unroll
-    for (int j = 0; j < NPT; j++) ss = fmaf(v[j], v[j], ss);
+    for (int j = 0; j < NJ; j++) ss = fmaf(v[j], v[j], ss);
     const float total = block_sum(ss, red);
     const float scale = 1.0f / sqrtf(total / float(n) + PLAMO_EPS);
 #pragma unroll
-    for (int j = 0; j < NPT; j++) {
+    for (int j = 0; j < NJ; j++) {
         const int i = threadIdx.x + j * 256;
         z[j] = i < n ? rbf(rbf(v[j] * scale) * f[j]) : 0.f;
     }
 }
 
+// Source elements of a row given as split-K partials [split][rows][n]: the bf16 rounding of the
+// sum in split order, the value k_gemm_tc_finish would have stored. Every partial of a group of
+// eight splits is loaded before the group's adds.
+template <int NJ>
+__device__ __forceinline__ void split_source(const NormArgs& a, size_t row, float (&v)[NJ]) {
+    const size_t ss = size_t(a.rows) * a.n;
+    float acc[NJ];
+    for (int s0 = 0; s0 < a.src_splits; s0 += 8) {
+        float pv[8][NJ];
+#pragma unroll
+        for (int k = 0; k < 8; k++)
+#pragma unroll
+            for (int j = 0; j < NJ; j++) {
+                const int i = threadIdx.x + j * 256;
+                pv[k][j] = s0 + k < a.src_splits && i < a.n ? a.src_part[size_t(s0 + k) * ss + row + i] : 0.f;
+            }
+#pragma unroll
+        for (int k = 0; k < 8; k++)
+#pragma unroll
+            for (int j = 0; j < NJ; j++)
+                if (s0 + k < a.src_splits) acc[j] = s0 + k == 0 ? pv[k][j] : acc[j] + pv[k][j];
+    }
+#pragma unroll
+    for (int j = 0; j < NJ; j++) v[j] = threadIdx.x + j * 256 < a.n ? rbf(acc[j]) : 0.f;
+}
+
 // Every global read of the row (source, norm weights, residual row, next norm weights) is issued
 // before the first reduction, so a row pays one memory latency instead of one per stage; the
 // arithmetic and its order are unchanged.
+template <int NJ>
 __global__ void __launch_bounds__(256) k_norm(NormArgs a) {
     pdl_enter();
     __shared__ float red[9];
     const int r = blockIdx.x;
     const size_t row = size_t(r) * a.n;
-    float v[NPT], z[NPT], f[NPT], xr[NPT], g[NPT];
+    float v[NJ], z[NJ], f[NJ], xr[NJ], g[NJ];
+    if (a.src_splits > 0) split_source<NJ>(a, row, v);
 #pragma unroll
-    for (int j = 0; j < NPT; j++) {
+    for (int j = 0; j < NJ; j++) {
         const int i = threadIdx.x + j * 256;
-        v[j] = i < a.n ? bf2f(a.src[row + i]) : 0.f;
+        if (a.src_splits <= 0) v[j] = i < a.n ? bf2f(a.src[row + i]) : 0.f;
         xr[j] = a.residual && i < a.n ? bf2f(a.x[row + i]) : 0.f;
     }
     norm_factors(a.w, a.n, a.offset, f);
@@ -245,7 +277,7 @@ __global__ void __launch_bounds__(256) k_norm(NormArgs a) {
     if (!a.residual) {
         const int orow = a.out_map ? a.out_map[r] : r;
 #pragma unroll
-        for (int j = 0; j < NPT; j++) {
+        for (int j = 0; j < NJ; j++) {
             const int i = threadIdx.x + j * 256;
             if (i < a.n) {
                 const uint16_t b = uint16_t(f2bf(z[j]));
@@ -256,7 +288,7 @@ __global__ void __launch_bounds__(256) k_norm(NormArgs a) {
         return;
     }
 #pragma unroll
-    for (int j = 0; j < NPT; j++) {
+    for (int j = 0; j < NJ; j++) {
         const int i = threadIdx.x + j * 256;
         if (i < a.n) {
             const float val = rbf(xr[j] + z[j]);
@@ -269,7 +301,7 @@ __global__ void __launch_bounds__(256) k_norm(NormArgs a) {
     if (!a.next_w) return;
     norm_row(v, a.n, g, red, z);
 #pragma unroll
-    for (int j = 0; j < NPT; j++) {
+    for (int j = 0; j < NJ; j++) {
         const int i = threadIdx.x + j * 256;
         if (i < a.n) a.next[row + i] = uint16_t(f2bf(z[j]));
     }
@@ -330,9 +362,43 @@ __global__ void __launch_bounds__(128) k_qkv(QkvArgs a) {
     if (h == 0 && lane == 0) a.geo[r] = RowGeo{first, count, begin, end};
     const int width = (a.H + 2 * a.KV) * 128;
     const uint16_t* src = a.qkv + size_t(r) * width + h * 128;
+    // the head's elements (and for a key head its value head's) as bf16 bits; from split-K
+    // partials, the bf16 rounding of their sum in split order (k_gemm_tc_finish's value)
+    uint32_t hb[4], vb[4];
+    if (a.src_splits > 0) {
+        const int nv = h < a.H ? 4 : 8;
+        const size_t ss_ = size_t(a.rows) * width, base = size_t(r) * width + h * 128;
+        float acc[8];
+        for (int s0 = 0; s0 < a.src_splits; s0 += 4) {
+            float pv[4][8];
+#pragma unroll
+            for (int k = 0; k < 4; k++)
+#pragma unroll
+                for (int j = 0; j < 8; j++)
+                    pv[k][j] = s0 + k < a.src_splits && j < nv
+                                   ? a.src_part[size_t(s0 + k) * ss_ + base + (j >> 2) * a.KV * 128 + lane + 32 * (j & 3)]
+                                   : 0.f;
+#pragma unroll
+            for (int k = 0; k < 4; k++)
+#pragma unroll
+                for (int j = 0; j < 8; j++)
+                    if (s0 + k < a.src_splits) acc[j] = s0 + k == 0 ? pv[k][j] : acc[j] + pv[k][j];
+        }
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            hb[j] = f2bf(acc[j]);
+            vb[j] = f2bf(acc[4 + j]);
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            hb[j] = src[lane + 32 * j];
+            vb[j] = h < a.H ? 0u : src[a.KV * 128 + lane + 32 * j];  // v head kvh sits KV heads after k head kvh
+        }
+    }
     float v[4], ss = 0.f;
 #pragma unroll
-    for (int j = 0; j < 4; j++) { v[j] = bf2f(src[lane + 32 * j]); ss = fmaf(v[j], v[j], ss); }
+    for (int j = 0; j < 4; j++) { v[j] = bf2f(hb[j]); ss = fmaf(v[j], v[j], ss); }
     ss = warp_sum(ss);
     const float scale = 1.0f / sqrtf(ss / 128.0f + PLAMO_EPS);
     const uint16_t* nw = h < a.H ? a.q_norm : a.k_norm;
@@ -355,7 +421,7 @@ __global__ void __launch_bounds__(128) k_qkv(QkvArgs a) {
             const int d = lane + 32 * j;
             const float k = a.full ? rope_rotate(z[j], z[(j + 2) & 3], d, table[d & 63]) : z[j];
             a.keys[slot + d] = uint16_t(f2bf(k));
-            a.values[slot + d] = src[a.KV * 128 + d];  // v head kvh sits KV heads after k head kvh
+            a.values[slot + d] = uint16_t(vb[j]);
         }
     }
 }
@@ -739,6 +805,7 @@ static cudaError_t gemv_rows(const GemvArgs& a, int mode, cudaStream_t s) {
 
 cudaError_t launch_gemv(const GemvArgs& a, int mode, cudaStream_t s) {
     if (a.lin.K % 128 || a.lin.K > 8192 || a.rows < 1) return cudaErrorInvalidValue;
+    if (a.split_out) *a.split_out = 0;
     // dense contraction on the tensor cores, when the caller chose that path
     if (a.tensor && a.rows >= TC_MIN_ROWS && gemm_tc_supported(a)) return launch_gemm_tc(a, GemvMode(mode), s);
     // many rows of raw weights: the tiled GEMM (same sums, weights read once per 32 rows)
@@ -808,12 +875,28 @@ cudaError_t launch_embed_norm(const int* ids, int rows, int vocab, const uint16_
                       nkeys);
 }
 
+// One CTA of 256 threads per row, at the fewest elements per thread that cover the row.
+static cudaError_t launch_norm_rows(const NormArgs& a, int nc, cudaStream_t s) {
+    switch (nc) {
+        case 1: return pdl_launch(k_norm<1>, dim3(a.rows), dim3(256), 0, s, a);
+        case 2: return pdl_launch(k_norm<2>, dim3(a.rows), dim3(256), 0, s, a);
+        case 3:
+        case 4: return pdl_launch(k_norm<4>, dim3(a.rows), dim3(256), 0, s, a);
+        case 5:
+        case 6: return pdl_launch(k_norm<6>, dim3(a.rows), dim3(256), 0, s, a);
+        case 7:
+        case 8: return pdl_launch(k_norm<8>, dim3(a.rows), dim3(256), 0, s, a);
+        default: return pdl_launch(k_norm<NPT>, dim3(a.rows), dim3(256), 0, s, a);
+    }
+}
+
 cudaError_t launch_norm(const NormArgs& a, cudaStream_t s) {
-    if (a.n > 256 * NPT) return cudaErrorInvalidValue;
-    return pdl_launch(k_norm, dim3(a.rows), dim3(256), 0, s, a);
+    if (a.n > 256 * NPT || a.src_splits < 0 || (a.src_splits > 0 && !a.src_part)) return cudaErrorInvalidValue;
+    return launch_norm_rows(a, (a.n + 255) / 256, s);
 }
 
 cudaError_t launch_qkv(const QkvArgs& a, cudaStream_t s) {
+    if (a.src_splits < 0 || (a.src_splits > 0 && !a.src_part)) return cudaErrorInvalidValue;
     const int warps = a.rows * (a.H + a.KV);
     return pdl_launch(k_qkv, dim3((warps + 3) / 4), dim3(128), 0, s, a);
 }

@@ -37,6 +37,9 @@ struct GemvArgs {
     int tensor = 0;                // dense rows (>= 16) of raw weights go to the tcgen05 GEMM
     float* part = nullptr;         // tcgen05 split-K partials (optional workspace)
     size_t part_cap = 0;           // floats in `part`
+    int* split_out = nullptr;      // plain mode, no out_map: a K split leaves its partials in `part`
+                                   // for the next kernel (no finish launch) and stores the split
+                                   // count here; 0 when y was written
 };
 
 struct AttnArgs {
@@ -67,6 +70,8 @@ struct QkvArgs {
     const uint32_t* rope_global = nullptr;
     long long lane_stride = 0;
     int rows = 1, H = 16, KV = 1, cap = 0, W = 2048, full = 0;
+    const float* src_part = nullptr;  // src_splits > 0: qkv is the bf16 rounding of the split sum of
+    int src_splits = 0;               // src_part [split][rows][(H+2KV)*128], in split order
 };
 
 struct NormArgs {
@@ -80,6 +85,8 @@ struct NormArgs {
     int rows = 1, n = 0;
     float offset = 0.f;
     int residual = 0;
+    const float* src_part = nullptr;  // src_splits > 0: the source rows are the bf16 rounding of
+    int src_splits = 0;               // the split sum of src_part [split][rows][n], in split order
 };
 
 // Launchers (return cudaError_t of the launch).

@@ -352,6 +352,16 @@ static int prof_end(cudaStream_t s, int cls) {
 // argmax back as the next step's input id and advance the row descriptors (device-chained decode).
 // chunked: the rows are prompt chunks (consecutive rows share a chunk and a lane), the shape the
 // tensor-core attention takes; batched decode steps (one row per lane) are not.
+// PLAMO_SPLIT_FINISH=1 in the environment keeps the separate split-K finish launch before the
+// norms (for comparison; both give the same bits).
+static bool fuse_split_sums() {
+    static const bool on = [] {
+        const char* v = std::getenv("PLAMO_SPLIT_FINISH");
+        return !(v && v[0] == '1');
+    }();
+    return on;
+}
+
 static int enqueue_forward(plamo_runtime& rt, Work& w, int rows, const CacheView& cv, int nout, Outputs& o,
                            bool chain, bool chunked = false) {
     const Config& c = rt.c;
@@ -369,10 +379,16 @@ static int enqueue_forward(plamo_runtime& rt, Work& w, int rows, const CacheView
     tc.part_cap = w.part_tc_cap;
     for (int l = 0; l < c.layers; l++) {
         const Layer& L = rt.layers[l];
+        // q/k/v, o_proj and down_proj: a tcgen05 K split leaves its partials to the kernel that
+        // follows (k_qkv, the norms), which adds them in split order (the finish kernel's sums)
+        // instead of a finish launch
+        int qsplits = 0;
         GemvArgs g = tc;
         g.lin = L.qkv; g.x = w.h; g.rows = rows; g.y = w.qkv; g.ystride = c.qkv_rows();
+        g.split_out = fuse_split_sums() ? &qsplits : nullptr;
         LAUNCH(K_GEMV, launch_gemv(g, GEMV_PLAIN, s));
         QkvArgs q;
+        q.src_part = qsplits ? w.part_tc : nullptr; q.src_splits = qsplits;
         q.qkv = w.qkv; q.q_norm = L.q_norm; q.k_norm = L.k_norm; q.q = w.q; q.keys = cv.keys[l]; q.values = cv.values[l];
         q.desc = w.desc; q.geo = w.geo; q.rope_local = rt.rope_local; q.rope_global = rt.rope_global;
         q.lane_stride = cv.stride[l]; q.rows = rows; q.H = c.heads; q.KV = c.kv_heads; q.cap = L.cap; q.W = c.window;
@@ -399,21 +415,26 @@ static int enqueue_forward(plamo_runtime& rt, Work& w, int rows, const CacheView
             if (attn_tc) LAUNCH(K_ATTN, launch_attention_tc(b, s));
             else LAUNCH(K_ATTN, launch_attention(b, s));
         }
+        int osplits = 0;
         g = tc;
         g.lin = L.o; g.x = w.att; g.rows = rows; g.y = w.proj; g.ystride = c.d;
+        g.split_out = fuse_split_sums() ? &osplits : nullptr;
         LAUNCH(K_GEMV, launch_gemv(g, GEMV_PLAIN, s));
         NormArgs n;
         n.w = L.post_mixer; n.src = w.proj; n.x = w.x; n.next_w = L.pre_mlp; n.next = w.h; n.rows = rows; n.n = c.d;
         n.offset = 0.2f; n.residual = 1;
+        n.src_part = osplits ? w.part_tc : nullptr; n.src_splits = osplits;
         LAUNCH(K_NORM, launch_norm(n, s));
         g = tc;
         g.lin = L.gate_up; g.x = w.h; g.rows = rows; g.y = w.act; g.ystride = c.ffn;
         LAUNCH(K_GEMV, launch_gemv(g, GEMV_SWIGLU, s));
         g = tc;
         g.lin = L.down; g.x = w.act; g.rows = rows; g.y = w.proj; g.ystride = c.d;
+        g.split_out = fuse_split_sums() ? &osplits : nullptr;
         LAUNCH(K_GEMV, launch_gemv(g, GEMV_PLAIN, s));
         n = NormArgs();
         n.w = L.post_mlp; n.src = w.proj; n.x = w.x; n.rows = rows; n.n = c.d; n.offset = post_mlp_offset; n.residual = 1;
+        n.src_part = osplits ? w.part_tc : nullptr; n.src_splits = osplits;
         if (l + 1 < c.layers) { n.next_w = rt.layers[l + 1].pre_mixer; n.next = w.h; }
         LAUNCH(K_NORM, launch_norm(n, s));
     }
