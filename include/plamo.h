@@ -143,8 +143,9 @@ PLAMO_API int plamo_debug_wait_timeout(plamo_runtime*, unsigned long long limit_
 /* Dense contractions on the tensor cores ("tensor mode"), a bit mask. Bit 0: every projection over
  * 16 or more rows of raw bf16 weights (prefill calls, batched steps and batched prefill of this
  * runtime and its batches) runs as a tcgen05 GEMM with fp32 accumulation. Bit 1: the attention of
- * every call over 16 or more rows (prefill chunks) runs its scores and P.V as tcgen05 MMAs (16
- * query heads over one KV head; other shapes keep the CUDA-core kernel). 3 selects both. The
+ * every call over 16 or more rows runs its scores and P.V on the tensor cores: prefill chunks as
+ * tcgen05 MMAs, the decode rows of a batched step as warp-level bf16 MMAs (16 query heads over one
+ * KV head; other shapes keep the CUDA-core kernel). 3 selects both. The
  * results then match the default path within the rounding of the accumulation order (next-token
  * logits within the drift the reference's own reordered sums show), not bit for bit; batch-1
  * decode and .p12 weights are unaffected. Off (0) by default. Returns 0, or 1 for a null handle. */

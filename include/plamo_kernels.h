@@ -79,9 +79,11 @@ PLAMO_API int plamo_k_attention(const uint16_t* q, const uint16_t* keys, const u
  * Kernels.metal:301-562): q is [rows][heads*128] bf16 (already rotated); geo is a DEVICE array of
  * [rows][4] int32 {first, count, begin, end} per row as in plamo_k_attention (keys r in [0,count)
  * at slot (first + r) % cap, the row sees r in [begin, end)). tensor == 0: the CUDA-core kernels
- * with `splits` key partitions (bit-identical to the runtime's default path); tensor != 0: the
- * tcgen05 kernel of tensor mode (16 query heads over one KV head, splits chosen by the library),
- * within rounding of the former. Rows of one 16-token chunk should be consecutive; rows with
+ * with `splits` key partitions (bit-identical to the runtime's default path); tensor == 1: the
+ * tcgen05 kernel of tensor mode's prefill (16 query heads over one KV head, splits chosen by the
+ * library); tensor == 2: tensor mode's decode-row kernel (16 query heads over one KV head, warp-level
+ * MMAs, the same `splits` as tensor == 0). 1 and 2 are within rounding of 0. Rows of one 16-token
+ * chunk should be consecutive for tensor == 1; rows with
  * different windows are handled, at a lower rate. `workspace` (device, 256-byte aligned) holds the
  * row descriptors and split partials; a call that finds it too small fails with the bytes needed. */
 PLAMO_API int plamo_k_attention_rows(const uint16_t* q, const uint16_t* keys, const uint16_t* values, int heads,

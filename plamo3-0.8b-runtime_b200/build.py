@@ -24,7 +24,7 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 # explicit fmaf, so the CPU restatement can reproduce the arithmetic bit for bit.
 NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-fmad=false", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
               "--expt-relaxed-constexpr", "-I", str(INCLUDE), "-I", str(CSRC)]
-SOURCES = ["kernels.cu", "gemm.cu", "gemm_tc.cu", "attn_tc.cu", "sampler.cu", "decode_mega.cu", "runtime.cu", "kernel_api.cu", "loader.cpp", "packer.cpp"]
+SOURCES = ["kernels.cu", "gemm.cu", "gemm_tc.cu", "attn_tc.cu", "attn_mma.cu", "sampler.cu", "decode_mega.cu", "runtime.cu", "kernel_api.cu", "loader.cpp", "packer.cpp"]
 
 
 def nvcc() -> str:

@@ -154,7 +154,8 @@ int plamo_k_attention_rows(const uint16_t* q, const uint16_t* keys, const uint16
                            int cap, const int32_t* geo, int rows, int full, const uint32_t* rope_local, int splits,
                            int tensor, uint16_t* out, void* workspace, size_t workspace_bytes, void* stream) {
     if (!q || !keys || !values || !geo || !out || !workspace || rows < 1 || heads < 1 || heads > 32 || kv_heads < 1 ||
-        heads % kv_heads || cap < 1 || (!full && !rope_local) || (!tensor && (splits < 1 || splits > 4096))) {
+        heads % kv_heads || cap < 1 || (!full && !rope_local) || tensor < 0 || tensor > 2 ||
+        (tensor != 1 && (splits < 1 || splits > 4096))) {
         g_error = "Invalid attention arguments";
         return 1;
     }
@@ -162,9 +163,9 @@ int plamo_k_attention_rows(const uint16_t* q, const uint16_t* keys, const uint16
     AttnArgs a;
     a.q = q; a.keys = keys; a.values = values; a.geo = reinterpret_cast<const RowGeo*>(geo); a.rope_local = rope_local;
     a.out = out; a.lane_stride = 0; a.rows = rows; a.H = heads; a.KV = kv_heads; a.cap = cap; a.full = full;
-    a.splits = tensor ? attention_tc_splits(cap) : splits;
+    a.splits = tensor == 1 ? attention_tc_splits(cap) : splits;
     a.per_max = attention_per_max(cap, a.splits);
-    if (tensor && !attention_tc_supported(a)) {
+    if (tensor == 1 && !attention_tc_supported(a)) {
         g_error = "The tensor-core attention takes 16 query heads over one KV head";
         return 1;
     }
@@ -183,7 +184,11 @@ int plamo_k_attention_rows(const uint16_t* q, const uint16_t* keys, const uint16
     a.desc = reinterpret_cast<const RowDesc*>(ws);
     a.part_o = reinterpret_cast<float*>(ws + desc_b);
     a.part_ml = reinterpret_cast<float2*>(ws + desc_b + po_b);
-    e = tensor ? launch_attention_tc(a, s) : launch_attention(a, s);
+    if (tensor == 2 && !attention_mma_supported(a)) {
+        g_error = "The tensor-core decode-row attention takes 16 query heads over one KV head";
+        return 1;
+    }
+    e = tensor == 1 ? launch_attention_tc(a, s) : tensor == 2 ? launch_attention_mma(a, s) : launch_attention(a, s);
     return e == cudaSuccess ? 0 : kfail(e);
 }
 

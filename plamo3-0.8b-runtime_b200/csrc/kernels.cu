@@ -864,6 +864,7 @@ cudaError_t configure_kernels() {
     if (e == cudaSuccess) e = configure_gemm();
     if (e == cudaSuccess) e = configure_gemm_tc();
     if (e == cudaSuccess) e = configure_attention_tc();
+    if (e == cudaSuccess) e = configure_attention_mma();
     return e;
 }
 

@@ -123,6 +123,12 @@ bool attention_tc_supported(const AttnArgs& a);
 int attention_tc_splits(int keys);  // keys: the cache capacity or a smaller bound on the rows' key counts
 cudaError_t launch_attention_tc(const AttnArgs& a, cudaStream_t s);
 cudaError_t configure_attention_tc();
+// Decode rows' attention on the tensor cores (attn_mma.cu, tensor mode): 16 query heads over one KV
+// head, warp-level bf16 MMAs, k_attn_partial's splits, partials and merge; results within rounding
+// of launch_attention.
+bool attention_mma_supported(const AttnArgs& a);
+cudaError_t launch_attention_mma(const AttnArgs& a, cudaStream_t s);
+cudaError_t configure_attention_mma();
 cudaError_t launch_finalize(unsigned long long* keys, const int* key_map, int rows, int* result,
                             int* chain_ids, RowDesc* advance, int* hist, int* hist_count, int hist_cap,
                             cudaStream_t s);

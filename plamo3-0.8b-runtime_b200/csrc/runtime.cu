@@ -362,6 +362,16 @@ static bool fuse_split_sums() {
     return on;
 }
 
+// PLAMO_ATTN_MMA=0 in the environment keeps tensor mode's batched decode rows on the CUDA-core
+// attention kernel (for comparison).
+static bool attention_mma_enabled() {
+    static const bool on = [] {
+        const char* v = std::getenv("PLAMO_ATTN_MMA");
+        return !(v && v[0] == '0');
+    }();
+    return on;
+}
+
 static int enqueue_forward(plamo_runtime& rt, Work& w, int rows, const CacheView& cv, int nout, Outputs& o,
                            bool chain, bool chunked = false) {
     const Config& c = rt.c;
@@ -400,6 +410,9 @@ static int enqueue_forward(plamo_runtime& rt, Work& w, int rows, const CacheView
         a.H = c.heads; a.KV = c.kv_heads; a.cap = L.cap; a.full = L.full; a.splits = L.splits; a.per_max = L.per_max;
         // tensor mode: rows of a prefill-like call attend on the tensor cores (attn_tc.cu)
         const bool attn_tc = rt.tensor_attn && chunked && rows >= TC_MIN_ROWS && attention_tc_supported(a);
+        // tensor mode: decode rows of a batched step attend with warp-level MMAs (attn_mma.cu)
+        const bool attn_mma =
+            rt.tensor_attn && !chunked && rows >= TC_MIN_ROWS && attention_mma_enabled() && attention_mma_supported(a);
         // the tensor-core kernel splits each row's keys into fewer, wider splits: a launch takes as
         // many rows as the partial buffers hold at that split count
         if (attn_tc) {
@@ -413,6 +426,7 @@ static int enqueue_forward(plamo_runtime& rt, Work& w, int rows, const CacheView
             b.q = w.q + size_t(r0) * c.q_dim(); b.out = w.att + size_t(r0) * c.q_dim();
             b.desc = w.desc + r0; b.geo = w.geo + r0;
             if (attn_tc) LAUNCH(K_ATTN, launch_attention_tc(b, s));
+            else if (attn_mma) LAUNCH(K_ATTN, launch_attention_mma(b, s));
             else LAUNCH(K_ATTN, launch_attention(b, s));
         }
         int osplits = 0;
