@@ -75,8 +75,9 @@ __device__ __forceinline__ void stage_tile(uint16_t* dst, const uint16_t* base, 
 __global__ void __launch_bounds__(MMA_THREADS) k_attn_rows_mma(AttnArgs a) {
     pdl_enter();
     extern __shared__ __align__(16) uint8_t smem_raw[];
-    uint16_t* tile = reinterpret_cast<uint16_t*>(smem_raw);              // [MT][KP] keys, then values
-    float* sc = reinterpret_cast<float*>(smem_raw + MT * KP * 2);        // [16][per_max] scores, then P
+    uint16_t* tile = reinterpret_cast<uint16_t*>(smem_raw);              // [MT][KP] keys, later value tiles
+    uint16_t* vfirst = tile + MT * KP;                                   // [MT][KP] the first value tile
+    float* sc = reinterpret_cast<float*>(smem_raw + 2 * MT * KP * 2);    // [16][per_max] scores, then P
     const int r = blockIdx.y, s = blockIdx.x, t = threadIdx.x, warp = t >> 5, lane = t & 31;
     const int gq = lane >> 2, tq = lane & 3;  // MMA fragment coordinates (group, thread in group)
     const RowGeo g = a.geo[r];
@@ -93,6 +94,23 @@ __global__ void __launch_bounds__(MMA_THREADS) k_attn_rows_mma(AttnArgs a) {
     const int n = hi - lo;
     const uint16_t* kbase = a.keys + size_t(lane_id) * a.lane_stride;
     const uint16_t* vbase = a.values + size_t(lane_id) * a.lane_stride;
+    // the first value tile does not depend on the scores: it streams in (cp.async) while they run
+    {
+        const int tk0 = min(MT, n);
+        for (int i = t; i < MT * 16; i += MMA_THREADS) {
+            const int j = i >> 4, d0 = (i & 15) * 8;
+            uint16_t* dst = vfirst + j * KP + d0;
+            if (j < tk0) {
+                const uint16_t* src = vbase + size_t((g.first + lo + j) % a.cap) * 128 + d0;
+                asm volatile("cp.async.cg.shared.global [%0], [%1], 16;"
+                             ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(dst))), "l"(src)
+                             : "memory");
+            } else {
+                *reinterpret_cast<uint4*>(dst) = make_uint4(0u, 0u, 0u, 0u);
+            }
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    }
     // Q fragments of all eight 16-dim k-steps (rows = heads gq and gq + 8)
     const uint32_t* q32 = reinterpret_cast<const uint32_t*>(a.q + size_t(r) * MMA_HEADS * 128);
     uint32_t qa[8][4];
@@ -147,8 +165,10 @@ __global__ void __launch_bounds__(MMA_THREADS) k_attn_rows_mma(AttnArgs a) {
     for (int t0 = 0; t0 < n; t0 += MT) {
         const int tk = min(MT, n - t0);
         __syncthreads();  // the score pass / previous tile is done with `tile`; P is complete
-        stage_tile(tile, vbase, g, lo + t0, tk, a.cap, nullptr, false);
+        if (t0 == 0) asm volatile("cp.async.wait_all;" ::: "memory");
+        else stage_tile(tile, vbase, g, lo + t0, tk, a.cap, nullptr, false);
         __syncthreads();
+        const uint16_t* vt = t0 == 0 ? vfirst : tile;
 #pragma unroll
         for (int kb = 0; kb < MT; kb += 16) {
             if (kb >= tk) break;
@@ -167,7 +187,7 @@ __global__ void __launch_bounds__(MMA_THREADS) k_attn_rows_mma(AttnArgs a) {
 #pragma unroll
             for (int j = 0; j < 4; j++) {
                 uint32_t b0, b1;
-                ldsm_x2_trans(b0, b1, tile + (kb + (lane & 15)) * KP + warp * 32 + j * 8);
+                ldsm_x2_trans(b0, b1, vt + (kb + (lane & 15)) * KP + warp * 32 + j * 8);
                 mma_bf16_16816(o[j], ph, b0, b1);
                 mma_bf16_16816(o[j], pl, b0, b1);
             }
@@ -182,7 +202,7 @@ __global__ void __launch_bounds__(MMA_THREADS) k_attn_rows_mma(AttnArgs a) {
     }
 }
 
-size_t attention_mma_smem(int per_max) { return size_t(MT) * KP * 2 + size_t(MMA_HEADS) * per_max * sizeof(float); }
+size_t attention_mma_smem(int per_max) { return size_t(2) * MT * KP * 2 + size_t(MMA_HEADS) * per_max * sizeof(float); }
 
 }  // namespace
 
