@@ -711,8 +711,9 @@ def main():
                     decode_tok_s=aggregate_rate(args.segment_lanes * args.segment_steps, world, float(st[0])),
                     step_ms=1e3 * float(st[0]) / args.segment_steps,
                     prefill_tok_s=aggregate_rate(args.segment_lanes * PROMPT, world, float(st[1])),
-                    path=("tcgen05 tensor-core projections (fp32 accumulate, within the restatement's reordering "
-                          "drift)" if tensor else "order-exact CUDA-core projections (bit-identical to the restatement)")
+                    path=("tcgen05 tensor-core projections, tcgen05 prefill attention, decode-row attention on "
+                          "warp-level bf16 MMAs (fp32 accumulate, within the restatement's reordering drift)"
+                          if tensor else "order-exact CUDA-core projections (bit-identical to the restatement)")
                     + "; one weight pass for all lanes per step")
 
     seg = seg_tc = None
