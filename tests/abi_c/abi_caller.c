@@ -102,6 +102,14 @@ int main(int argc, char** argv) {
     EXPECT(strstr(plamo_last_error(), "Invalid linear arguments") != NULL);
     EXPECT(plamo_k_attention_static(NULL, NULL, NULL, 16, 1, 64, 0, 64, 0, 64, 1, NULL, 4, NULL, NULL) != 0);
     EXPECT(strstr(plamo_last_error(), "Invalid attention arguments") != NULL);
+    {
+        /* the multi-row attention takes tensor 0 (CUDA cores), 1 (prefill, tcgen05) or 2 (decode rows,
+         * warp-level MMAs); anything else is refused before a device is touched */
+        uint16_t buf[64];
+        const int32_t geo[4] = {0, 64, 0, 64};
+        EXPECT(plamo_k_attention_rows(buf, buf, buf, 16, 1, 64, geo, 1, 1, NULL, 4, 3, buf, buf, sizeof buf, NULL) != 0);
+        EXPECT(strstr(plamo_last_error(), "Invalid attention arguments") != NULL);
+    }
 
     if (failures) fprintf(stderr, "%d check(s) failed\n", failures);
     else printf("abi_caller: ok\n");
